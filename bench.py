@@ -1,0 +1,713 @@
+#!/usr/bin/env python
+"""Benchmark of the hot path on B200: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload NAME]
+
+Workloads (synthetic, seeded inputs with the documented shapes/distributions):
+
+  tv_iso_l1   (default) tv_loss_iso_3d (eps 1e-8) and tv_loss_l1_3d forward +
+              gradient on fp32 [4, 256, 256, 256], uniform[0, 1) with 1% of
+              voxels set to their +W neighbour, seed 1. A step runs both
+              single-sweep ops on the volume. At N GPUs the volume is
+              [4, 256*N, 256, 256], split along D (one 256-plane slab per rank,
+              halo exchange and rank-ordered loss sum each step): weak scaling.
+  tv_sq_128   tv_loss_sq_3d forward + gradient on [128, 128, 128], seed 0.
+  kplanes     kplanes_tilted_fuse forward + backward (autograd ops), N = 2^20
+              points uniform in [-1, 1]^3, 4 rotations from normalised N(0, 1)
+              quaternions, C = 32, 256x256 planes uniform[0.1, 0.5], upstream
+              N(0, 1), seed 2. At N GPUs each rank holds its own 2^20 points
+              and the plane/rotation gradients are all-reduced: weak scaling.
+  tv_1024     tv_loss_sq_3d + tv_loss_iso_3d forward + gradient on [1024]^3,
+              sum of 64 Gaussian blobs (sigma 8..64) + N(0, 0.01) noise, seed 4.
+
+`value` is whole-job throughput with inputs resident in HBM; `e2e` is the same
+metric through the public API from pinned host buffers (host->device copy of
+the step's input and device->host read of its losses inside the timed
+region). `roofline` reports the dominant kernel's algorithmic bytes per launch
+over its CUDA-event duration against the measured HBM copy bandwidth.
+`--impl reference` times the reference computation on the host cores (the
+CPU oracle, a restatement of the reference's kernels: the reference itself
+has no CPU implementation), on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "quantem-cuda_b200"))
+sys.path.insert(0, str(REPO))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ── environment ─────────────────────────────────────────────────────────────
+
+
+def measured_hbm_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(workload: str) -> dict | None:
+    """Per-launch DRAM traffic of the dominant kernel from a committed ncu
+    summary (profiles/*.md lines 'traffic <workload> <bytes_per_unit> <unit>')."""
+    for f in sorted((REPO / "profiles").glob("*.md")):
+        for line in f.read_text().splitlines():
+            parts = line.strip().strip("`").split()
+            if len(parts) >= 4 and parts[0] == "traffic" and parts[1] == workload:
+                try:
+                    return {"bytes_per_unit": float(parts[2]), "unit": parts[3], "source": f.name}
+                except ValueError:
+                    pass
+    return None
+
+
+class ClockSampler:
+    """Polls SM clock, power and throttle reasons through NVML while the timed
+    region runs (reads only; changes no setting)."""
+
+    REASONS = {
+        0x1: "gpu_idle",
+        0x2: "applications_clocks_setting",
+        0x4: "sw_power_cap",
+        0x8: "hw_slowdown",
+        0x20: "sync_boost",
+        0x40: "sw_thermal_slowdown",
+        0x80: "hw_thermal_slowdown",
+        0x100: "hw_power_brake_slowdown",
+        0x200: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.period = period_s
+        self.samples: list[tuple[int, int, float]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.handle = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            uuid = None
+            try:
+                uuid = torch.cuda.get_device_properties(device_index).uuid
+            except Exception:
+                pass
+            self.handle = None
+            if uuid is not None:
+                try:
+                    self.handle = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(uuid))
+                except Exception:
+                    self.handle = None
+            if self.handle is None:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[device_index]) if vis and vis.split(",")[0].isdigit() else device_index
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.handle = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                power = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((mhz, reasons, power))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [s[0] for s in self.samples]
+        bits = 0
+        for s in self.samples:
+            bits |= s[1]
+        reasons = [name for bit, name in self.REASONS.items() if bits & bit and name != "gpu_idle"]
+        return {
+            "sm_mhz": statistics.median(mhz),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": reasons,
+            "samples": len(self.samples),
+            "power_w_max": max(s[2] for s in self.samples),
+        }
+
+
+# ── workload inputs ─────────────────────────────────────────────────────────
+
+
+def tv_iso_l1_volume(seed: int, d: int = 256) -> torch.Tensor:
+    gen = torch.Generator().manual_seed(seed)
+    vol = torch.rand((4, d, 256, 256), generator=gen)
+    flat = vol.view(-1, 256)
+    rows = torch.randint(0, flat.shape[0], (vol.numel() // 100,), generator=gen)
+    cols = torch.randint(0, 255, rows.shape, generator=gen)
+    flat[rows, cols] = flat[rows, cols + 1]  # dw == 0 exactly: sign(0) = 0
+    return vol
+
+
+def blob_volume(n: int, seed: int, device) -> torch.Tensor:
+    """Sum of 64 Gaussian blobs (centres U[0, n)^3, sigma U[8, 64], amplitude 1)
+    + N(0, 0.01) noise, built on the device plane by plane."""
+    gen = torch.Generator().manual_seed(seed)
+    centres = torch.rand((64, 3), generator=gen) * n
+    sigmas = 8 + torch.rand(64, generator=gen) * 56
+    vol = torch.empty((n, n, n), device=device)
+    ax = torch.arange(n, device=device, dtype=torch.float32)
+    gd = torch.Generator(device=device).manual_seed(seed)
+    for z in range(n):
+        plane = torch.zeros((n, n), device=device)
+        for (cz, cy, cx), s in zip(centres.tolist(), sigmas.tolist()):
+            wz = math.exp(-((z - cz) ** 2) / (2 * s * s))
+            if wz < 1e-6:
+                continue
+            gy = torch.exp(-((ax - cy) ** 2) / (2 * s * s))
+            gx = torch.exp(-((ax - cx) ** 2) / (2 * s * s))
+            plane += wz * gy[:, None] * gx[None, :]
+        vol[z] = plane + 0.01 * torch.randn((n, n), device=device, generator=gd)
+    return vol
+
+
+def quaternion_rotations(T: int, gen: torch.Generator) -> torch.Tensor:
+    q = torch.randn((T, 4), generator=gen)
+    q = q / q.norm(dim=1, keepdim=True)
+    w, x, y, z = q.unbind(1)
+    return torch.stack(
+        [
+            1 - 2 * (y * y + z * z), 2 * (x * y - z * w), 2 * (x * z + y * w),
+            2 * (x * y + z * w), 1 - 2 * (x * x + z * z), 2 * (y * z - x * w),
+            2 * (x * z - y * w), 2 * (y * z + x * w), 1 - 2 * (x * x + y * y),
+        ],
+        dim=1,
+    ).reshape(T, 3, 3)
+
+
+def kplanes_inputs(seed: int, N: int = 1 << 20, T: int = 4, C: int = 32, res: int = 256):
+    gen = torch.Generator().manual_seed(seed)
+    pts = torch.empty((N, 3)).uniform_(-1.0, 1.0, generator=gen)
+    rot = quaternion_rotations(T, gen)
+    plane = torch.empty((3 * T, C, res, res)).uniform_(0.1, 0.5, generator=gen)
+    up = torch.randn((N, T * C), generator=gen)
+    return pts, rot, plane, up
+
+
+# ── timing helpers ──────────────────────────────────────────────────────────
+
+
+class Ctx:
+    def __init__(self, args):
+        self.args = args
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.device = None
+
+    def barrier(self):
+        if self.world > 1:
+            dist.barrier(device_ids=[self.local_rank]) if self.device is not None else dist.barrier()
+
+    def max_over_ranks(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+
+def time_steps(ctx: Ctx, step, steps: int, warmup: int, sampler: ClockSampler | None = None):
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler is not None:
+        sampler.__enter__()
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    if sampler is not None:
+        sampler.__exit__(None, None, None)
+    ctx.barrier()
+    ms = start.elapsed_time(end)
+    return ctx.max_over_ranks(ms)
+
+
+class KernelTimer:
+    """CUDA-event durations of one launch site inside the timed loop."""
+
+    def __init__(self):
+        self.pairs = []
+
+    def wrap(self, fn):
+        def run(*a, **k):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            r = fn(*a, **k)
+            e.record()
+            self.pairs.append((s, e))
+            return r
+
+        return run
+
+    def mean_ms(self, last: int) -> float:
+        sel = self.pairs[-last:]
+        return sum(s.elapsed_time(e) for s, e in sel) / max(1, len(sel))
+
+
+# ── CPU (oracle) baselines ──────────────────────────────────────────────────
+
+
+def cpu_oracle():
+    from oracle import oracle
+
+    oracle.build()
+    n = oracle.available_cores()
+    oracle.set_threads(n)
+    return oracle, oracle.threads()
+
+
+def cpu_tv_iso_l1(sample_d: int = 32, min_seconds: float = 10.0, reps: int | None = None):
+    oracle, threads = cpu_oracle()
+    x = tv_iso_l1_volume(1, d=sample_d).numpy()
+    voxels = x.size
+    b, d, h, w = x.shape
+    n = b * (d - 1) * (h - 1) * (w - 1)
+
+    def step():
+        oracle.tv_iso_sum(x, 1e-8)
+        oracle.tv_iso_grad(x, 1.0 / n, 1e-8)
+        oracle.tv_l1_loss(x)
+        oracle.tv_l1_grad(x, [1.0, 1.0, 1.0])
+
+    step()
+    t0 = time.perf_counter()
+    k = 0
+    while True:
+        step()
+        k += 1
+        el = time.perf_counter() - t0
+        if (reps is not None and k >= reps) or (reps is None and el >= min_seconds):
+            break
+    per_step = el / k
+    return {
+        "value": voxels / per_step,
+        "unit": "voxels/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"[4, {sample_d}, 256, 256] slab of the workload volume (1/{256 // sample_d} of it): "
+        f"iso loss + iso grad + L1 sums + L1 grad with the C oracle (OpenMP), {k} reps, {el:.1f} s",
+    }, per_step
+
+
+def cpu_kplanes(sample_n: int = 1 << 14, min_seconds: float = 10.0, reps: int | None = None):
+    oracle, threads = cpu_oracle()
+    pts, rot, plane, up = kplanes_inputs(2)
+    p, r, g, u = pts[:sample_n].numpy(), rot.numpy(), plane.numpy(), up[:sample_n].numpy()
+
+    def step():
+        oracle.kplanes_fwd(p, r, g)
+        oracle.kplanes_bwd(p, r, g, u)
+
+    step()
+    t0 = time.perf_counter()
+    k = 0
+    while True:
+        step()
+        k += 1
+        el = time.perf_counter() - t0
+        if (reps is not None and k >= reps) or (reps is None and el >= min_seconds):
+            break
+    per_step = el / k
+    return {
+        "value": sample_n / per_step,
+        "unit": "points/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"first {sample_n} of the 2^20 points, forward + backward with the C oracle "
+        f"(OpenMP), {k} reps, {el:.1f} s",
+    }, per_step
+
+
+# ── workloads (ours) ────────────────────────────────────────────────────────
+
+
+def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
+    from quantem.cuda import sharded
+    from quantem.cuda.core import tv_loss_iso_3d_fwd_grad, tv_loss_l1_3d_fwd_grad
+
+    dev = ctx.device
+    D_LOCAL = 256
+    vol_cpu = tv_iso_l1_volume(1 + 1000 * ctx.rank, d=D_LOCAL)
+    voxels_local = vol_cpu.numel()
+    g1 = torch.ones(1, device=dev)
+    g3 = torch.ones(3, device=dev)
+    t_iso, t_l1 = KernelTimer(), KernelTimer()
+    launches_per_step = 4  # two sweeps + two fixed-order finalize kernels
+
+    if ctx.world == 1:
+        vol = vol_cpu.to(dev)
+        iso = t_iso.wrap(lambda v: tv_loss_iso_3d_fwd_grad(v, g1, eps=1e-8))
+        l1 = t_l1.wrap(lambda v: tv_loss_l1_3d_fwd_grad(v, g3))
+
+        def step():
+            iso(vol)
+            l1(vol)
+
+    else:
+        global_d = D_LOCAL * ctx.world
+        slab = torch.zeros((4, D_LOCAL + 2, 256, 256), device=dev)
+        slab[:, 1 : D_LOCAL + 1] = vol_cpu.to(dev)
+        iso = t_iso.wrap(lambda: sharded.tv_loss_slab_fwd_grad(sharded.ISO, slab, g1, global_d, 1e-8, exchange=False))
+        l1 = t_l1.wrap(lambda: sharded.tv_loss_slab_fwd_grad(sharded.L1, slab, g3, global_d, exchange=False))
+
+        def step():
+            sharded.exchange_halos(slab)
+            iso()
+            l1()
+
+        vol = slab
+
+    sampler = ClockSampler(ctx.local_rank)
+    ms = time_steps(ctx, step, steps, warmup, sampler)
+    ms_step = ms / steps
+    iso_ms = t_iso.mean_ms(steps)
+    l1_ms = t_l1.mean_ms(steps)
+    dom_ms = max(iso_ms, l1_ms)
+    dom = "tv iso single sweep" if iso_ms >= l1_ms else "tv L1 single sweep"
+
+    # end to end: the public API from pinned host memory
+    e2e = None
+    if ctx.world == 1:
+        host = vol_cpu.pin_memory()
+        res_host = torch.empty(4, pin_memory=True)
+
+        def e2e_step():
+            v = host.to(dev, non_blocking=True)
+            li, _ = tv_loss_iso_3d_fwd_grad(v, g1, eps=1e-8)
+            ls, _ = tv_loss_l1_3d_fwd_grad(v, g3)
+            res_host[:1].copy_(li.reshape(1), non_blocking=True)
+            res_host[1:].copy_(ls, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
+        e2e = {
+            "value": voxels_local / (e2e_ms / steps / 1e3),
+            "unit": "voxels/s",
+            "h2d_bytes_per_step": host.numel() * 4,
+            "d2h_bytes_per_step": 16,
+        }
+
+    peak, peak_kind = measured_hbm_peak()
+    algo_bytes = 8.0 * voxels_local  # single sweep: read 4 B + write 4 B per voxel
+    achieved = algo_bytes / (dom_ms / 1e3) / 1e9
+    tr = ncu_traffic("tv_iso_l1")
+    return {
+        "metric": "TV fwd+grad voxels/sec",
+        "value": voxels_local * ctx.world / (ms_step / 1e3),
+        "unit": "voxels/s",
+        "ms_per_step": ms_step,
+        "gpu_launches": launches_per_step * steps,
+        "config": {
+            "workload": "tv_iso_l1: tv_loss_iso_3d (eps 1e-8) + tv_loss_l1_3d single-sweep fwd+grad",
+            "shape_per_gpu": [4, D_LOCAL, 256, 256],
+            "global_shape": [4, D_LOCAL * ctx.world, 256, 256],
+            "parallelism": f"d-slab{ctx.world}" if ctx.world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (268 MB volume per GPU, 2 x 268 MB of gradients written per step)",
+            "per_loss_ms": {"iso": iso_ms, "l1": l1_ms},
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": dom,
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": f"{peak_kind} HBM copy bandwidth",
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": None if tr is None else tr["bytes_per_unit"] * voxels_local,
+            "algorithmic_bytes": algo_bytes,
+        },
+        "clocks": sampler.summary(),
+        "e2e": e2e,
+        "dtype": "f32",
+    }
+
+
+def run_tv_sq_128(ctx: Ctx, steps: int, warmup: int) -> dict:
+    from quantem.cuda.core import tv_loss_sq_3d_fwd_grad
+
+    gen = torch.Generator().manual_seed(0)
+    vol_cpu = torch.rand((128, 128, 128), generator=gen)
+    vol = vol_cpu.to(ctx.device)
+    g1 = torch.ones(1, device=ctx.device)
+    flush = torch.empty(192 << 20, dtype=torch.uint8, device=ctx.device)  # > L2
+    t = KernelTimer()
+    sq = t.wrap(lambda: tv_loss_sq_3d_fwd_grad(vol, g1))
+
+    def step():
+        flush.zero_()
+        sq()
+
+    sampler = ClockSampler(ctx.local_rank)
+    ms = time_steps(ctx, step, steps, warmup, sampler)
+    k_ms = t.mean_ms(steps)
+    peak, peak_kind = measured_hbm_peak()
+    algo = 8.0 * vol.numel()
+    return {
+        "metric": "TV fwd+grad voxels/sec",
+        "value": vol.numel() * ctx.world / (k_ms / 1e3),
+        "unit": "voxels/s",
+        "ms_per_step": k_ms,
+        "gpu_launches": 2 * steps,
+        "config": {"workload": "tv_sq_128: tv_loss_sq_3d single-sweep fwd+grad on [128,128,128]",
+                   "l2": "L2 flushed (192 MB write) between steps; value uses the op's event time",
+                   "step_ms_with_flush": ms / steps},
+        "roofline": {"bound": "hbm", "kernel": "tv sq single sweep", "achieved": algo / (k_ms / 1e3) / 1e9,
+                     "peak": peak, "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
+                     "frac": algo / (k_ms / 1e3) / 1e9 / peak, "traffic": None, "algorithmic_bytes": algo},
+        "clocks": sampler.summary(),
+        "e2e": None,
+        "dtype": "f32",
+    }
+
+
+def run_tv_1024(ctx: Ctx, steps: int, warmup: int) -> dict:
+    from quantem.cuda.core import tv_loss_iso_3d_fwd_grad, tv_loss_sq_3d_fwd_grad
+
+    vol = blob_volume(1024, 4, ctx.device)
+    g1 = torch.ones(1, device=ctx.device)
+    t_sq, t_iso = KernelTimer(), KernelTimer()
+    sq = t_sq.wrap(lambda: tv_loss_sq_3d_fwd_grad(vol, g1))
+    iso = t_iso.wrap(lambda: tv_loss_iso_3d_fwd_grad(vol, g1, eps=1e-8))
+
+    def step():
+        sq()
+        iso()
+
+    sampler = ClockSampler(ctx.local_rank)
+    ms = time_steps(ctx, step, steps, warmup, sampler)
+    ms_step = ms / steps
+    peak, peak_kind = measured_hbm_peak()
+    dom_ms = max(t_sq.mean_ms(steps), t_iso.mean_ms(steps))
+    algo = 8.0 * vol.numel()
+    return {
+        "metric": "TV fwd+grad voxels/sec",
+        "value": vol.numel() * ctx.world / (ms_step / 1e3),
+        "unit": "voxels/s",
+        "ms_per_step": ms_step,
+        "gpu_launches": 4 * steps,
+        "config": {"workload": "tv_1024: tv_loss_sq_3d + tv_loss_iso_3d single-sweep fwd+grad on [1024]^3 blobs",
+                   "l2": "inputs larger than L2 (4 GiB)",
+                   "per_loss_ms": {"sq": t_sq.mean_ms(steps), "iso": t_iso.mean_ms(steps)}},
+        "roofline": {"bound": "hbm", "kernel": "tv single sweep", "achieved": algo / (dom_ms / 1e3) / 1e9,
+                     "peak": peak, "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
+                     "frac": algo / (dom_ms / 1e3) / 1e9 / peak, "traffic": None, "algorithmic_bytes": algo},
+        "clocks": sampler.summary(),
+        "e2e": None,
+        "dtype": "f32",
+    }
+
+
+def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
+    from quantem.cuda import sharded
+    from quantem.cuda.core.ml import kplanes_tilted_fuse
+
+    pts, rot, plane, up = kplanes_inputs(2 + 1000 * ctx.rank)
+    dev = ctx.device
+    N, T, C = pts.shape[0], rot.shape[0], plane.shape[1]
+    p, r, g, u = pts.to(dev), rot.to(dev), plane.to(dev), up.to(dev)
+    t_f, t_b = KernelTimer(), KernelTimer()
+    fwd = t_f.wrap(lambda: torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, g))
+    bwd = t_b.wrap(lambda: torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, g, u))
+
+    if ctx.world == 1:
+        def step():
+            fwd()
+            bwd()
+    else:
+        def step():
+            fwd()
+            g_pts, g_r, g_p = bwd()
+            dist.all_reduce(g_p)
+            dist.all_reduce(g_r)
+
+    sampler = ClockSampler(ctx.local_rank)
+    ms = time_steps(ctx, step, steps, warmup, sampler)
+    ms_step = ms / steps
+    f_ms, b_ms = t_f.mean_ms(steps), t_b.mean_ms(steps)
+    P = 3 * T * C * plane.shape[2] * plane.shape[3] * 4
+    fwd_bytes = 12 * N + P + 4 * N * T * C
+    bwd_bytes = 12 * N + 4 * N * T * C + P + P + 12 * N
+    peak, peak_kind = measured_hbm_peak()
+
+    e2e = None
+    if ctx.world == 1:
+        hp, hr, hg, hu = (t.pin_memory() for t in (pts, rot, plane, up))
+        res_host = torch.empty(1, pin_memory=True)
+
+        def e2e_step():
+            pp = hp.to(dev, non_blocking=True).requires_grad_(True)
+            rr = hr.to(dev, non_blocking=True).requires_grad_(True)
+            gg = hg.to(dev, non_blocking=True).requires_grad_(True)
+            uu = hu.to(dev, non_blocking=True)
+            out = kplanes_tilted_fuse(pp, rr, gg)
+            loss = (out * uu).sum()
+            loss.backward()
+            res_host.copy_(loss.detach().reshape(1), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
+        e2e = {"value": N / (e2e_ms / steps / 1e3), "unit": "points/s",
+               "h2d_bytes_per_step": sum(t.numel() * 4 for t in (hp, hr, hg, hu)), "d2h_bytes_per_step": 4}
+
+    return {
+        "metric": "K-Planes fwd+bwd points/sec",
+        "value": N * ctx.world / (ms_step / 1e3),
+        "unit": "points/s",
+        "ms_per_step": ms_step,
+        "gpu_launches": 7 * steps,
+        "config": {"workload": "kplanes: kplanes_tilted_fuse fwd + bwd ops, N=2^20, T=4, C=32, 256^2",
+                   "points_per_gpu": N, "parallelism": f"points{ctx.world}" if ctx.world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (512 MiB output + 512 MiB upstream gradient per step)",
+                   "fwd_op_ms": f_ms, "bwd_op_ms": b_ms},
+        "roofline": {"bound": "hbm", "kernel": "kplanes backward op",
+                     "achieved": bwd_bytes / (b_ms / 1e3) / 1e9, "peak": peak,
+                     "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
+                     "frac": bwd_bytes / (b_ms / 1e3) / 1e9 / peak, "traffic": None,
+                     "algorithmic_bytes": bwd_bytes, "step_algorithmic_bytes": fwd_bytes + bwd_bytes,
+                     "step_frac": (fwd_bytes + bwd_bytes) / (ms_step / 1e3) / 1e9 / peak},
+        "clocks": sampler.summary(),
+        "e2e": e2e,
+        "dtype": "f32",
+    }
+
+
+WORKLOADS = {
+    "tv_iso_l1": run_tv_iso_l1,
+    "tv_sq_128": run_tv_sq_128,
+    "tv_1024": run_tv_1024,
+    "kplanes": run_kplanes,
+}
+
+
+# ── reference arm: the reference computation on the host cores ──────────────
+
+
+def run_reference(ctx: Ctx, args) -> dict | None:
+    if ctx.rank != 0:
+        return None
+    if args.workload in ("kplanes",):
+        cb, per_step = cpu_kplanes(reps=args.steps)
+        metric = "K-Planes fwd+bwd points/sec"
+    else:
+        cb, per_step = cpu_tv_iso_l1(reps=args.steps)
+        metric = "TV fwd+grad voxels/sec"
+    return {
+        "metric": metric,
+        "value": cb["value"],
+        "unit": cb["unit"],
+        "impl": "reference",
+        "ms_per_step": per_step * 1e3,
+        "config": {"workload": args.workload, "sample": cb["sample"]},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "dtype": "f32",
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tv_iso_l1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    ctx = Ctx(args)
+    warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        res = run_reference(ctx, args)
+        if res is not None:
+            res.update({"n_gpus": args.gpus, "steps": args.steps, "warmup": warmup,
+                        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                        "data": "synthetic"})
+            print(json.dumps(res), flush=True)
+        return
+
+    if ctx.world > 1:
+        torch.cuda.set_device(ctx.local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", ctx.local_rank))
+    ctx.device = torch.device("cuda", ctx.local_rank)
+    torch.cuda.set_device(ctx.device)
+
+    res = WORKLOADS[args.workload](ctx, args.steps, warmup)
+
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
+        if args.workload == "kplanes":
+            res["cpu_baseline"], _ = cpu_kplanes()
+        else:
+            res["cpu_baseline"], _ = cpu_tv_iso_l1()
+
+    if ctx.world > 1:
+        dist.barrier(device_ids=[ctx.local_rank])
+        dist.destroy_process_group()
+    if ctx.rank == 0:
+        out = {
+            "metric": res.pop("metric"),
+            "value": res.pop("value"),
+            "unit": res.pop("unit"),
+            "n_gpus": ctx.world,
+            "steps": args.steps,
+            "warmup": warmup,
+            "ms_per_step": res.pop("ms_per_step"),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": res.pop("dtype"),
+            "data": "synthetic",
+        }
+        out.update(res)
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,172 @@
+/* quantem_cuda_b200.h — C ABI of the B200 (sm_100a) kernels for quantem-cuda's
+ * data-parallel hot path: the 3-D total-variation losses and the fused tilted
+ * K-Planes interpolation.
+ *
+ * Every entry point is `extern "C"`, takes raw device pointers, plain integer
+ * shapes and a CUDA stream, and never allocates device memory: buffers belong
+ * to the caller. All launches are asynchronous on `stream`. An entry point
+ * returns 0 on success; otherwise a CUDA runtime error code (1..9999) or one of
+ * the QC_ERR_* codes below, and `quantem_cuda_last_error()` returns a message
+ * for the calling thread. Launch-time errors are reported at the call; errors
+ * raised while a kernel runs surface at the caller's next synchronisation,
+ * exactly as in the reference's launchers (csrc/common.cuh:26-33).
+ *
+ * Layouts (all fp32, C-contiguous):
+ *   TV volume           [B, D, H, W]      (B flattens any leading dims)
+ *   K-Planes points     [N, 3]            (the reference calls N "B")
+ *   K-Planes rotations  [T, 3, 3]         row-major
+ *   K-Planes grid       [3T, H, W, C]     channels-last, plane index t*3 + {XY, ZX, YZ}
+ *   K-Planes output     [N, T*C]          out[b, t*C + c]
+ *
+ * Differences from the reference launchers (csrc/ops/core.h, csrc/ops/core/ml.h):
+ *   - each returns an int status instead of throwing std::runtime_error;
+ *   - the TV loss entries take a caller-owned scratch buffer (`workspace`,
+ *     `workspace_bytes`, at least tv_loss_3d_workspace_bytes()) that holds the
+ *     per-CTA partial sums of the deterministic two-pass reduction. Its
+ *     contents need no initialisation; calls that share one workspace must be
+ *     ordered on the GPU (one stream, or events).
+ */
+#ifndef QUANTEM_CUDA_B200_H
+#define QUANTEM_CUDA_B200_H
+
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ── status ─────────────────────────────────────────────────────────────── */
+
+#define QC_OK 0
+#define QC_ERR_INVALID_ARGUMENT 10001    /* bad shape, null pointer, size overflow */
+#define QC_ERR_WORKSPACE_TOO_SMALL 10002 /* workspace_bytes below the required size */
+#define QC_ERR_NO_DEVICE 10003           /* no CUDA device / driver entry point missing */
+#define QC_ERR_TENSOR_MAP 10004          /* cuTensorMapEncodeTiled rejected the layout */
+
+/* Message describing the last non-zero status returned on this thread. */
+const char *quantem_cuda_last_error(void);
+
+/* Human-readable name of a status code. */
+const char *quantem_cuda_status_string(int status);
+
+/* CUDART_VERSION the library was compiled against (e.g. 12090).
+ * Replaces the reference's `_core.__cudart_version__` (csrc/bindings.cpp:24). */
+int quantem_cuda_cudart_version(void);
+
+/* Reads (and, if `clear` != 0, resets) the device-side fault word of `device`.
+ * Kernels that wait on a TMA barrier give up after a bounded time and set a bit
+ * here instead of hanging; 0 means no kernel has given up. Synchronises the
+ * device. */
+int quantem_cuda_device_fault_word(int device, unsigned int *word, int clear);
+
+/* ── 3-D total variation ────────────────────────────────────────────────── */
+
+/* Bytes of scratch the TV loss entry points need for a [B, D, H, W] volume. */
+size_t tv_loss_3d_workspace_bytes(int B, int D, int H, int W);
+
+/* Isotropic TV: acc[0] += Σ_b Σ_corners sqrt(dd² + dh² + dw² + eps), corners
+ * [0,D-2]×[0,H-2]×[0,W-2]. Deterministic. Replaces tv_loss_iso_3d_cuda
+ * (reference csrc/ops/core.h:16-22, csrc/cuda/core/tv_loss.cu:98-121). */
+int tv_loss_iso_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W, float eps,
+                        void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Gradient of the isotropic sum times *d_g_scaled (upstream / N); grad_vol is
+ * fully written (zero when a dim is < 2). Replaces tv_loss_iso_3d_grad_cuda
+ * (reference csrc/ops/core.h:27-34, tv_loss.cu:194-218). */
+int tv_loss_iso_3d_grad_cuda(const float *d_vol, const float *d_g_scaled, float *d_grad_vol,
+                             int B, int D, int H, int W, float eps, cudaStream_t stream);
+
+/* Squared-anisotropic TV: acc[0] += Σ_b Σ_axes Σ (forward difference)², each axis
+ * over its full complementary range. Replaces tv_loss_sq_3d_cuda
+ * (reference csrc/ops/core.h:40-45, tv_loss.cu:276-294). */
+int tv_loss_sq_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                       void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* 2·g·∇ of the squared sum; grad_vol fully written. Replaces
+ * tv_loss_sq_3d_grad_cuda (reference csrc/ops/core.h:50-56, tv_loss.cu:334-352). */
+int tv_loss_sq_3d_grad_cuda(const float *d_vol, const float *d_g, float *d_grad_vol, int B, int D,
+                            int H, int W, cudaStream_t stream);
+
+/* L1-anisotropic TV: acc[axis] += Σ_b Σ |forward difference along axis|, axis
+ * order (D, H, W). Replaces tv_loss_l1_3d_cuda (reference csrc/ops/core.h:62-67,
+ * tv_loss.cu:411-429). */
+int tv_loss_l1_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                       void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Σ_axis g[axis]·∇ of the per-axis L1 sums, sign(0) = 0; grad_vol fully
+ * written. Replaces tv_loss_l1_3d_grad_cuda (reference csrc/ops/core.h:72-78,
+ * tv_loss.cu:477-495). */
+int tv_loss_l1_3d_grad_cuda(const float *d_vol, const float *d_g, float *d_grad_vol, int B, int D,
+                            int H, int W, cudaStream_t stream);
+
+/* Single-sweep forward + gradient: one HBM pass reads the volume once and
+ * writes both the loss (acc, as the *_cuda entries: acc += Σ) and the gradient
+ * (as the *_grad_cuda entries, scaled by the device scalar(s) at d_g). No
+ * reference counterpart: the reference runs the loss and gradient kernels as
+ * two passes (tv_loss.cu:47-96 then :140-192, and likewise for sq and L1). */
+int tv_loss_iso_3d_fwd_grad_cuda(const float *d_vol, const float *d_g_scaled, float *d_acc,
+                                 float *d_grad_vol, int B, int D, int H, int W, float eps,
+                                 void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+int tv_loss_sq_3d_fwd_grad_cuda(const float *d_vol, const float *d_g, float *d_acc,
+                                float *d_grad_vol, int B, int D, int H, int W, void *d_workspace,
+                                size_t workspace_bytes, cudaStream_t stream);
+int tv_loss_l1_3d_fwd_grad_cuda(const float *d_vol, const float *d_g, float *d_acc,
+                                float *d_grad_vol, int B, int D, int H, int W, void *d_workspace,
+                                size_t workspace_bytes, cudaStream_t stream);
+
+/* General D-slab form behind all TV entries, used directly by the sharded
+ * (multi-GPU) path. The volume holds Dp physical planes per batch slice; planes
+ * [d_lo, d_hi) are owned. has_prev / has_next say whether plane d_lo-1 / d_hi is
+ * a real neighbour (a halo received from another rank) rather than the edge of
+ * the global volume. Loss terms anchored at owned planes are summed, and the
+ * gradient of owned planes is written (planes outside [d_lo, d_hi) are left
+ * untouched).
+ *   variant: QC_TV_SQ, QC_TV_ISO, QC_TV_L1
+ *   flags:   QC_TV_LOSS and/or QC_TV_GRAD, optionally QC_TV_ACC_OVERWRITE
+ *            (acc = scale·Σ instead of acc += scale·Σ)
+ *   d_g:     device scalar (sq, iso) or 3-vector (L1) multiplying the gradient
+ *   acc_scale multiplies both the stored sum and the gradient (the isotropic
+ *            op passes 1/N, folding the mean into the kernel). */
+#define QC_TV_SQ 0
+#define QC_TV_ISO 1
+#define QC_TV_L1 2
+#define QC_TV_LOSS 1
+#define QC_TV_GRAD 2
+#define QC_TV_ACC_OVERWRITE 4
+int tv_loss_3d_slab_cuda(int variant, int flags, const float *d_vol, const float *d_g, float *d_acc,
+                         float *d_grad_vol, int B, int Dp, int H, int W, int d_lo, int d_hi,
+                         int has_prev, int has_next, float eps, float acc_scale, void *d_workspace,
+                         size_t workspace_bytes, cudaStream_t stream);
+
+/* ── tilted K-Planes ────────────────────────────────────────────────────── */
+
+/* out[b, t*C + c] = Π_{p∈XY,ZX,YZ} bilinear(grid[t*3+p], (R_t·pts_b) pair p), with
+ * grid_sample(align_corners=True, padding_mode="border") semantics; out fully
+ * written. Replaces kplanes_tilted_fuse_cuda (reference csrc/ops/core/ml.h:17-24,
+ * csrc/cuda/core/ml/kplanes_tilted.cu:289-302). Requires C*H*W < 2^31. */
+int kplanes_tilted_fuse_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                             float *d_out, long B, int T, int C, int H, int W,
+                             cudaStream_t stream);
+
+/* Backward: ggrid [3T,H,W,C], gR [T,3,3] and gpts [N,3] are accumulated into
+ * (caller pre-zeroes for a plain gradient). Coordinate gradients are zero where
+ * the border clip engaged. Replaces kplanes_tilted_fuse_grad_cuda (reference
+ * csrc/ops/core/ml.h:26-40, kplanes_tilted.cu:304-327). */
+int kplanes_tilted_fuse_grad_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                                  const float *d_gout, float *d_ggrid, float *d_gR, float *d_gpts,
+                                  long B, int T, int C, int H, int W, cudaStream_t stream);
+
+/* Plane layout conversion [P, C, H, W] -> [P, H, W, C] and back. Replaces the
+ * torch permute+contiguous of the reference's op layer
+ * (src/quantem/cuda/core/ml/_ops.py:21-25, :82). src and dst must not overlap. */
+int kplanes_planes_to_channels_last_cuda(const float *d_src, float *d_dst, int P, int C, int H,
+                                         int W, cudaStream_t stream);
+int kplanes_planes_from_channels_last_cuda(const float *d_src, float *d_dst, int P, int C, int H,
+                                           int W, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QUANTEM_CUDA_B200_H */

@@ -1,0 +1,577 @@
+// kplanes_tilted.cu — fused tilted K-Planes interpolation, forward and
+// backward, for sm_100a.
+//
+// Reference semantics: csrc/cuda/core/ml/kplanes_tilted.cu:62-327 (kernels and
+// launchers), src/quantem/cuda/core/ml/_ops.py:28-101 (op layer), and the
+// pure-torch definition in tests/core/ml/test_kplanes_tilted.py:26-40:
+//
+//   r = R_t · p;  (gx, gy) per plane p: XY (rx, ry), ZX (rz, rx), YZ (ry, rz)
+//   s_p = grid_sample(plane[t*3+p], (gx, gy), align_corners=True, border)
+//   out[b, t*C + c] = s_0 · s_1 · s_2
+//
+// Mapping. A "group" of L = C/4 lanes handles one (point, rotation); each lane
+// owns 4 consecutive channels and moves them with 16-byte loads, stores and
+// vector reductions, so a C=32 corner row (128 B, one L2 line) is one
+// instruction for 8 lanes. A warp holds 32/L groups, i.e. a tile of 32/L
+// consecutive points, and loops over the T rotations for its tile. Looping
+// rotations inside the warp keeps a point's gradient in registers (no
+// atomics on grad_pts) and writes a point's T·C outputs as full lines.
+//
+// The tap arithmetic (unnormalise, clamp, floor, bilinear weights, border
+// gradient mask) is written with the same operation order as the reference's
+// make_tap (kplanes_tilted.cu:69-94) and the rotation as explicit FMAs in the
+// reference's left-to-right order, so forward values agree bit for bit with
+// the reference kernel wherever the compiler contracts the reference's
+// expressions the same way.
+//
+// Backward. Plane gradients go out as red.global.add.v4.f32 (one L2 atomic op
+// per 16 B instead of four); corners with zero bilinear weight are skipped.
+// Coordinate gradients are reduced over the group's lanes with xor shuffles,
+// mapped to dL/dr with the border masks, and accumulated into grad_pts in
+// registers across rotations; grad_R goes through per-CTA shared-memory
+// accumulators flushed once per CTA.
+#include "qc_common.cuh"
+
+namespace qc {
+namespace kp {
+
+struct Tap {
+    int cell[4];     // y*W + x of the (nw, ne, sw, se) corners, +1 sides clamped
+    float w[4];      // bilinear weights; 0 exactly where a +1 side was clamped
+    float tx, ty;    // fractional offsets
+    float gxm, gym;  // d(ix)/d(gx), d(iy)/d(gy) with torch's border-clip mask
+};
+
+__device__ __forceinline__ Tap make_tap(float gx, float gy, int H, int W) {
+    Tap t;
+    const float wm1 = (float)(W - 1), hm1 = (float)(H - 1);
+    float ix = (gx + 1.f) * 0.5f * wm1;
+    float iy = (gy + 1.f) * 0.5f * hm1;
+    // torch's clip_coordinates_set_grad: zero gradient at and beyond the border.
+    t.gxm = (ix > 0.f && ix < wm1) ? 0.5f * wm1 : 0.f;
+    t.gym = (iy > 0.f && iy < hm1) ? 0.5f * hm1 : 0.f;
+    ix = fminf(fmaxf(ix, 0.f), wm1);
+    iy = fminf(fmaxf(iy, 0.f), hm1);
+    const int x0 = (int)ix, y0 = (int)iy;
+    t.tx = ix - (float)x0;
+    t.ty = iy - (float)y0;
+    t.w[0] = (1.f - t.tx) * (1.f - t.ty);
+    t.w[1] = t.tx * (1.f - t.ty);
+    t.w[2] = (1.f - t.tx) * t.ty;
+    t.w[3] = t.tx * t.ty;
+    const int x1 = min(x0 + 1, W - 1), y1 = min(y0 + 1, H - 1);
+    t.cell[0] = y0 * W + x0;
+    t.cell[1] = y0 * W + x1;
+    t.cell[2] = y1 * W + x0;
+    t.cell[3] = y1 * W + x1;
+    return t;
+}
+
+__device__ __forceinline__ void rotate(const float *Rt, float px, float py, float pz, float &rx,
+                                       float &ry, float &rz) {
+    rx = __fmaf_rn(Rt[2], pz, __fmaf_rn(Rt[1], py, __fmul_rn(Rt[0], px)));
+    ry = __fmaf_rn(Rt[5], pz, __fmaf_rn(Rt[4], py, __fmul_rn(Rt[3], px)));
+    rz = __fmaf_rn(Rt[8], pz, __fmaf_rn(Rt[7], py, __fmul_rn(Rt[6], px)));
+}
+
+// w0*v0 + w1*v1 + w2*v2 + w3*v3, accumulated left to right.
+__device__ __forceinline__ float bilerp(const float w[4], float v0, float v1, float v2, float v3) {
+    return __fmaf_rn(w[3], v3, __fmaf_rn(w[2], v2, __fmaf_rn(w[1], v1, __fmul_rn(w[0], v0))));
+}
+
+__device__ __forceinline__ void plane_coords(float rx, float ry, float rz, int p, float &gx,
+                                             float &gy) {
+    // p: 0 = XY (rx, ry), 1 = ZX (rz, rx), 2 = YZ (ry, rz).
+    gx = p == 0 ? rx : (p == 1 ? rz : ry);
+    gy = p == 0 ? ry : (p == 1 ? rx : rz);
+}
+
+// ── vectorised path: C == 4*L, L in {1, 2, 4, 8, 16, 32} ────────────────────
+
+constexpr int kThreads = 256;
+
+template <int L>
+__global__ void __launch_bounds__(kThreads) kpt_fwd_v4_kernel(const float *__restrict__ pts,
+                                                              const float *__restrict__ R,
+                                                              const float *__restrict__ grid,
+                                                              float *__restrict__ out, long long B,
+                                                              int T, int H, int W) {
+    constexpr int C = 4 * L;
+    constexpr int G = 32 / L;  // points per warp tile
+    extern __shared__ float sR[];
+    for (int i = threadIdx.x; i < T * 9; i += blockDim.x) sR[i] = R[i];
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int grp = lane / L, c4 = 4 * (lane % L);
+    const long long planeHWC = (long long)H * W * C;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+
+    for (long long b0 = warp0 * G; b0 < B; b0 += nwarps * G) {
+        const long long b = b0 + grp;
+        if (b >= B) continue;
+        const float px = __ldg(pts + 3 * b), py = __ldg(pts + 3 * b + 1),
+                    pz = __ldg(pts + 3 * b + 2);
+        float *orow = out + b * (long long)(T * C) + c4;
+#pragma unroll 2
+        for (int t = 0; t < T; ++t) {
+            float rx, ry, rz;
+            rotate(sR + 9 * t, px, py, pz, rx, ry, rz);
+            float4 s[3];
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                float gx, gy;
+                plane_coords(rx, ry, rz, p, gx, gy);
+                const Tap tp = make_tap(gx, gy, H, W);
+                const float *pc = grid + (long long)(3 * t + p) * planeHWC + c4;
+                const float4 v0 = ldg4(pc + tp.cell[0] * C), v1 = ldg4(pc + tp.cell[1] * C);
+                const float4 v2 = ldg4(pc + tp.cell[2] * C), v3 = ldg4(pc + tp.cell[3] * C);
+                s[p].x = bilerp(tp.w, v0.x, v1.x, v2.x, v3.x);
+                s[p].y = bilerp(tp.w, v0.y, v1.y, v2.y, v3.y);
+                s[p].z = bilerp(tp.w, v0.z, v1.z, v2.z, v3.z);
+                s[p].w = bilerp(tp.w, v0.w, v1.w, v2.w, v3.w);
+            }
+            float4 o;
+            o.x = __fmul_rn(__fmul_rn(s[0].x, s[1].x), s[2].x);
+            o.y = __fmul_rn(__fmul_rn(s[0].y, s[1].y), s[2].y);
+            o.z = __fmul_rn(__fmul_rn(s[0].z, s[1].z), s[2].z);
+            o.w = __fmul_rn(__fmul_rn(s[0].w, s[1].w), s[2].w);
+            __stcs(reinterpret_cast<float4 *>(orow + t * C), o);
+        }
+    }
+}
+
+template <int L>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int off = L / 2; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+template <int L>
+__global__ void __launch_bounds__(kThreads) kpt_bwd_v4_kernel(
+    const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
+    const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
+    float *__restrict__ gpts, long long B, int T, int H, int W) {
+    constexpr int C = 4 * L;
+    constexpr int G = 32 / L;
+    extern __shared__ float smem[];
+    float *sR = smem;
+    float *sgR = smem + 9 * T;
+    for (int i = threadIdx.x; i < T * 9; i += blockDim.x) {
+        sR[i] = R[i];
+        sgR[i] = 0.f;
+    }
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int grp = lane / L, lis = lane % L, c4 = 4 * lis;
+    const long long planeHWC = (long long)H * W * C;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+
+    for (long long b0 = warp0 * G; b0 < B; b0 += nwarps * G) {
+        const long long b_raw = b0 + grp;
+        const bool active = b_raw < B;
+        const long long b = active ? b_raw : B - 1;  // keep addresses valid; contributions zeroed
+        const float px = __ldg(pts + 3 * b), py = __ldg(pts + 3 * b + 1),
+                    pz = __ldg(pts + 3 * b + 2);
+        const float *grow = gout + b * (long long)(T * C) + c4;
+        float gpx = 0.f, gpy = 0.f, gpz = 0.f;
+
+        for (int t = 0; t < T; ++t) {
+            const float *Rt = sR + 9 * t;
+            float rx, ry, rz;
+            rotate(Rt, px, py, pz, rx, ry, rz);
+            float4 go = __ldcs(reinterpret_cast<const float4 *>(grow + t * C));
+            if (!active) go = make_float4(0.f, 0.f, 0.f, 0.f);
+
+            Tap tap[3];
+            float4 s[3], dx[3], dy[3];
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                float gx, gy;
+                plane_coords(rx, ry, rz, p, gx, gy);
+                tap[p] = make_tap(gx, gy, H, W);
+                const float *pc = grid + (long long)(3 * t + p) * planeHWC + c4;
+                const float4 v0 = ldg4(pc + tap[p].cell[0] * C), v1 = ldg4(pc + tap[p].cell[1] * C);
+                const float4 v2 = ldg4(pc + tap[p].cell[2] * C), v3 = ldg4(pc + tap[p].cell[3] * C);
+                const float *w = tap[p].w;
+                const float tx = tap[p].tx, ty = tap[p].ty;
+                s[p] = make_float4(bilerp(w, v0.x, v1.x, v2.x, v3.x), bilerp(w, v0.y, v1.y, v2.y, v3.y),
+                                   bilerp(w, v0.z, v1.z, v2.z, v3.z), bilerp(w, v0.w, v1.w, v2.w, v3.w));
+                // ds/dix = (1-ty)(v1-v0) + ty(v3-v2);  ds/diy = (1-tx)(v2-v0) + tx(v3-v1)
+                // (clamped +1 corners only differ where the border mask zeroes the result)
+                dx[p].x = (1.f - ty) * (v1.x - v0.x) + ty * (v3.x - v2.x);
+                dx[p].y = (1.f - ty) * (v1.y - v0.y) + ty * (v3.y - v2.y);
+                dx[p].z = (1.f - ty) * (v1.z - v0.z) + ty * (v3.z - v2.z);
+                dx[p].w = (1.f - ty) * (v1.w - v0.w) + ty * (v3.w - v2.w);
+                dy[p].x = (1.f - tx) * (v2.x - v0.x) + tx * (v3.x - v1.x);
+                dy[p].y = (1.f - tx) * (v2.y - v0.y) + tx * (v3.y - v1.y);
+                dy[p].z = (1.f - tx) * (v2.z - v0.z) + tx * (v3.z - v1.z);
+                dy[p].w = (1.f - tx) * (v2.w - v0.w) + tx * (v3.w - v1.w);
+            }
+
+            float dgx[3], dgy[3];
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                const float4 sa = s[(p + 1) % 3], sb = s[(p + 2) % 3];
+                float4 other;
+                other.x = sa.x * sb.x * go.x;
+                other.y = sa.y * sb.y * go.y;
+                other.z = sa.z * sb.z * go.z;
+                other.w = sa.w * sb.w * go.w;
+                float *gpc = ggrid + (long long)(3 * t + p) * planeHWC + c4;
+                if (active) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float wk = tap[p].w[k];
+                        if (wk != 0.f)
+                            red_add_v4(gpc + tap[p].cell[k] * C,
+                                       make_float4(other.x * wk, other.y * wk, other.z * wk,
+                                                   other.w * wk));
+                    }
+                }
+                dgx[p] = other.x * dx[p].x + other.y * dx[p].y + other.z * dx[p].z +
+                         other.w * dx[p].w;
+                dgy[p] = other.x * dy[p].x + other.y * dy[p].y + other.z * dy[p].z +
+                         other.w * dy[p].w;
+            }
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                dgx[p] = group_sum<L>(dgx[p]);
+                dgy[p] = group_sum<L>(dgy[p]);
+            }
+            // Back to the rotated point: XY=(rx,ry), ZX=(rz,rx), YZ=(ry,rz).
+            const float drx = dgx[0] * tap[0].gxm + dgy[1] * tap[1].gym;
+            const float dry = dgy[0] * tap[0].gym + dgx[2] * tap[2].gxm;
+            const float drz = dgx[1] * tap[1].gxm + dgy[2] * tap[2].gym;
+            // dL/dp += R_t^T dr
+            gpx += Rt[0] * drx + Rt[3] * dry + Rt[6] * drz;
+            gpy += Rt[1] * drx + Rt[4] * dry + Rt[7] * drz;
+            gpz += Rt[2] * drx + Rt[5] * dry + Rt[8] * drz;
+            // dL/dR_t[i, j] += dr_i * p_j
+            if (active && lis == 0) {
+                float *sg = sgR + 9 * t;
+                atomicAdd(sg + 0, drx * px);
+                atomicAdd(sg + 1, drx * py);
+                atomicAdd(sg + 2, drx * pz);
+                atomicAdd(sg + 3, dry * px);
+                atomicAdd(sg + 4, dry * py);
+                atomicAdd(sg + 5, dry * pz);
+                atomicAdd(sg + 6, drz * px);
+                atomicAdd(sg + 7, drz * py);
+                atomicAdd(sg + 8, drz * pz);
+            }
+        }
+        if (active && lis == 0) {
+            // This group alone owns point b: plain read-modify-write accumulates.
+            float *gp = gpts + 3 * b;
+            gp[0] += gpx;
+            gp[1] += gpy;
+            gp[2] += gpz;
+        }
+    }
+
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * 9; i += blockDim.x)
+        if (sgR[i] != 0.f) atomicAdd(gR + i, sgR[i]);
+}
+
+// ── generic path: any C (scalar channels, one warp per point) ─────────────
+
+__global__ void __launch_bounds__(kThreads) kpt_fwd_generic_kernel(
+    const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
+    float *__restrict__ out, long long B, int T, int C, int H, int W) {
+    extern __shared__ float sR[];
+    for (int i = threadIdx.x; i < T * 9; i += blockDim.x) sR[i] = R[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const long long planeHWC = (long long)H * W * C;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp0; b < B; b += nwarps) {
+        const float px = pts[3 * b], py = pts[3 * b + 1], pz = pts[3 * b + 2];
+        for (int t = 0; t < T; ++t) {
+            float rx, ry, rz;
+            rotate(sR + 9 * t, px, py, pz, rx, ry, rz);
+            Tap tp[3];
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                float gx, gy;
+                plane_coords(rx, ry, rz, p, gx, gy);
+                tp[p] = make_tap(gx, gy, H, W);
+            }
+            for (int c = lane; c < C; c += 32) {
+                float s[3];
+#pragma unroll
+                for (int p = 0; p < 3; ++p) {
+                    const float *pc = grid + (long long)(3 * t + p) * planeHWC + c;
+                    s[p] = bilerp(tp[p].w, __ldg(pc + (long long)tp[p].cell[0] * C),
+                                  __ldg(pc + (long long)tp[p].cell[1] * C),
+                                  __ldg(pc + (long long)tp[p].cell[2] * C),
+                                  __ldg(pc + (long long)tp[p].cell[3] * C));
+                }
+                out[b * (long long)(T * C) + (long long)t * C + c] =
+                    __fmul_rn(__fmul_rn(s[0], s[1]), s[2]);
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) kpt_bwd_generic_kernel(
+    const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
+    const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
+    float *__restrict__ gpts, long long B, int T, int C, int H, int W) {
+    extern __shared__ float smem[];
+    float *sR = smem;
+    float *sgR = smem + 9 * T;
+    for (int i = threadIdx.x; i < T * 9; i += blockDim.x) {
+        sR[i] = R[i];
+        sgR[i] = 0.f;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const long long planeHWC = (long long)H * W * C;
+    const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long b = warp0; b < B; b += nwarps) {
+        const float px = pts[3 * b], py = pts[3 * b + 1], pz = pts[3 * b + 2];
+        float gpx = 0.f, gpy = 0.f, gpz = 0.f;
+        for (int t = 0; t < T; ++t) {
+            const float *Rt = sR + 9 * t;
+            float rx, ry, rz;
+            rotate(Rt, px, py, pz, rx, ry, rz);
+            Tap tp[3];
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                float gx, gy;
+                plane_coords(rx, ry, rz, p, gx, gy);
+                tp[p] = make_tap(gx, gy, H, W);
+            }
+            float dgx[3] = {0.f, 0.f, 0.f}, dgy[3] = {0.f, 0.f, 0.f};
+            for (int c = lane; c < C; c += 32) {
+                const float go = gout[b * (long long)(T * C) + (long long)t * C + c];
+                float v[3][4], s[3];
+#pragma unroll
+                for (int p = 0; p < 3; ++p) {
+                    const float *pc = grid + (long long)(3 * t + p) * planeHWC + c;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) v[p][k] = __ldg(pc + (long long)tp[p].cell[k] * C);
+                    s[p] = bilerp(tp[p].w, v[p][0], v[p][1], v[p][2], v[p][3]);
+                }
+#pragma unroll
+                for (int p = 0; p < 3; ++p) {
+                    const float other = s[(p + 1) % 3] * s[(p + 2) % 3] * go;
+                    float *gpc = ggrid + (long long)(3 * t + p) * planeHWC + c;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float val = other * tp[p].w[k];
+                        if (val != 0.f) atomicAdd(gpc + (long long)tp[p].cell[k] * C, val);
+                    }
+                    const float tx = tp[p].tx, ty = tp[p].ty;
+                    dgx[p] += other * ((1.f - ty) * (v[p][1] - v[p][0]) + ty * (v[p][3] - v[p][2]));
+                    dgy[p] += other * ((1.f - tx) * (v[p][2] - v[p][0]) + tx * (v[p][3] - v[p][1]));
+                }
+            }
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    dgx[p] += __shfl_xor_sync(0xffffffffu, dgx[p], off);
+                    dgy[p] += __shfl_xor_sync(0xffffffffu, dgy[p], off);
+                }
+            }
+            const float drx = dgx[0] * tp[0].gxm + dgy[1] * tp[1].gym;
+            const float dry = dgy[0] * tp[0].gym + dgx[2] * tp[2].gxm;
+            const float drz = dgx[1] * tp[1].gxm + dgy[2] * tp[2].gym;
+            gpx += Rt[0] * drx + Rt[3] * dry + Rt[6] * drz;
+            gpy += Rt[1] * drx + Rt[4] * dry + Rt[7] * drz;
+            gpz += Rt[2] * drx + Rt[5] * dry + Rt[8] * drz;
+            if (lane == 0) {
+                float *sg = sgR + 9 * t;
+                atomicAdd(sg + 0, drx * px);
+                atomicAdd(sg + 1, drx * py);
+                atomicAdd(sg + 2, drx * pz);
+                atomicAdd(sg + 3, dry * px);
+                atomicAdd(sg + 4, dry * py);
+                atomicAdd(sg + 5, dry * pz);
+                atomicAdd(sg + 6, drz * px);
+                atomicAdd(sg + 7, drz * py);
+                atomicAdd(sg + 8, drz * pz);
+            }
+        }
+        if (lane == 0) {
+            gpts[3 * b] += gpx;
+            gpts[3 * b + 1] += gpy;
+            gpts[3 * b + 2] += gpz;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * 9; i += blockDim.x)
+        if (sgR[i] != 0.f) atomicAdd(gR + i, sgR[i]);
+}
+
+// ── plane layout conversion [P, C, HW] <-> [P, HW, C] ─────────────────────
+
+constexpr int kTT = 32;  // transpose tile
+
+// dst[p][j][i] = src[p][i][j] for a [P, R, S] -> [P, S, R] transpose.
+__global__ void __launch_bounds__(kTT * 8) transpose_kernel(const float *__restrict__ src,
+                                                          float *__restrict__ dst, int Rn, int Sn) {
+    __shared__ float tile[kTT][kTT + 1];
+    const long long base = (long long)blockIdx.z * Rn * Sn;
+    const int i0 = blockIdx.y * kTT, j0 = blockIdx.x * kTT;
+    for (int k = threadIdx.y; k < kTT; k += 8) {
+        const int i = i0 + k, j = j0 + threadIdx.x;
+        if (i < Rn && j < Sn) tile[k][threadIdx.x] = __ldcs(src + base + (long long)i * Sn + j);
+    }
+    __syncthreads();
+    for (int k = threadIdx.y; k < kTT; k += 8) {
+        const int j = j0 + k, i = i0 + threadIdx.x;
+        if (i < Rn && j < Sn) dst[base + (long long)j * Rn + i] = tile[threadIdx.x][k];
+    }
+}
+
+int launch_transpose(const float *src, float *dst, int P, int Rn, int Sn, cudaStream_t stream) {
+    QC_RETURN_IF(P < 0 || Rn < 0 || Sn < 0, QC_ERR_INVALID_ARGUMENT, "transpose: negative shape");
+    if ((long long)P * Rn * Sn == 0) return 0;
+    QC_RETURN_IF(src == nullptr || dst == nullptr, QC_ERR_INVALID_ARGUMENT, "transpose: null pointer");
+    QC_RETURN_IF(P > 65535, QC_ERR_INVALID_ARGUMENT, "transpose: more than 65535 planes");
+    const dim3 grid((Sn + kTT - 1) / kTT, (Rn + kTT - 1) / kTT, P);
+    QC_RETURN_IF(grid.y > 65535, QC_ERR_INVALID_ARGUMENT, "transpose: row extent too large");
+    transpose_kernel<<<grid, dim3(kTT, 8), 0, stream>>>(src, dst, Rn, Sn);
+    QC_CHECK_LAUNCH("transpose_kernel launch");
+    return 0;
+}
+
+// ── launch plumbing ───────────────────────────────────────────────────────
+
+int check_shapes(const char *who, long B, int T, int C, int H, int W) {
+    QC_RETURN_IF(B < 0 || T < 0 || C < 0 || H < 0 || W < 0, QC_ERR_INVALID_ARGUMENT,
+                 "%s: negative shape (B=%ld T=%d C=%d H=%d W=%d)", who, B, T, C, H, W);
+    QC_RETURN_IF((long long)C * H * W >= (1LL << 31), QC_ERR_INVALID_ARGUMENT,
+                 "%s: C*H*W must be < 2^31 (32-bit per-plane offsets)", who);
+    QC_RETURN_IF(T > 4096, QC_ERR_INVALID_ARGUMENT, "%s: T=%d exceeds 4096", who, T);
+    return 0;
+}
+
+int grid_size(long long work_warps, int *grid) {
+    int sms = 0;
+    if (int st = device_sm_count(&sms)) return st;
+    const long long warps_per_block = kThreads / 32;
+    long long blocks = (work_warps + warps_per_block - 1) / warps_per_block;
+    const long long cap = (long long)sms * 64;  // persistent: enough waves to balance
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    *grid = (int)blocks;
+    return 0;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <int L>
+int fwd_v4(const float *pts, const float *R, const float *grid, float *out, long long B, int T,
+           int H, int W, cudaStream_t stream) {
+    constexpr int G = 32 / L;
+    int blocks = 0;
+    if (int st = grid_size((B + G - 1) / G, &blocks)) return st;
+    kpt_fwd_v4_kernel<L><<<blocks, kThreads, 9 * T * sizeof(float), stream>>>(pts, R, grid, out,
+                                                                              B, T, H, W);
+    QC_CHECK_LAUNCH("kpt_fwd_v4_kernel launch");
+    return 0;
+}
+
+template <int L>
+int bwd_v4(const float *pts, const float *R, const float *grid, const float *gout, float *ggrid,
+           float *gR, float *gpts, long long B, int T, int H, int W, cudaStream_t stream) {
+    constexpr int G = 32 / L;
+    int blocks = 0;
+    if (int st = grid_size((B + G - 1) / G, &blocks)) return st;
+    kpt_bwd_v4_kernel<L><<<blocks, kThreads, 18 * T * sizeof(float), stream>>>(
+        pts, R, grid, gout, ggrid, gR, gpts, B, T, H, W);
+    QC_CHECK_LAUNCH("kpt_bwd_v4_kernel launch");
+    return 0;
+}
+
+}  // namespace kp
+}  // namespace qc
+
+extern "C" {
+
+int kplanes_tilted_fuse_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                             float *d_out, long B, int T, int C, int H, int W,
+                             cudaStream_t stream) {
+    using namespace qc::kp;
+    if (int st = check_shapes("kplanes_tilted_fuse_cuda", B, T, C, H, W)) return st;
+    if (B == 0 || T == 0 || C == 0) return 0;
+    QC_RETURN_IF(H == 0 || W == 0, QC_ERR_INVALID_ARGUMENT, "kplanes_tilted_fuse_cuda: empty plane");
+    QC_RETURN_IF(!d_pts || !d_R || !d_grid || !d_out, QC_ERR_INVALID_ARGUMENT,
+                 "kplanes_tilted_fuse_cuda: null pointer");
+    const bool vec = (C % 4 == 0) && C <= 128 && aligned16(d_grid) && aligned16(d_out);
+    if (vec) {
+        switch (C / 4) {
+            case 1: return fwd_v4<1>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
+            case 2: return fwd_v4<2>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
+            case 4: return fwd_v4<4>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
+            case 8: return fwd_v4<8>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
+            case 16: return fwd_v4<16>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
+            case 32: return fwd_v4<32>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
+            default: break;
+        }
+    }
+    int blocks = 0;
+    if (int st = grid_size(B, &blocks)) return st;
+    kpt_fwd_generic_kernel<<<blocks, kThreads, 9 * T * sizeof(float), stream>>>(d_pts, d_R, d_grid,
+                                                                              d_out, B, T, C, H, W);
+    QC_CHECK_LAUNCH("kpt_fwd_generic_kernel launch");
+    return 0;
+}
+
+int kplanes_tilted_fuse_grad_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                                  const float *d_gout, float *d_ggrid, float *d_gR, float *d_gpts,
+                                  long B, int T, int C, int H, int W, cudaStream_t stream) {
+    using namespace qc::kp;
+    if (int st = check_shapes("kplanes_tilted_fuse_grad_cuda", B, T, C, H, W)) return st;
+    if (B == 0 || T == 0 || C == 0) return 0;
+    QC_RETURN_IF(H == 0 || W == 0, QC_ERR_INVALID_ARGUMENT,
+                 "kplanes_tilted_fuse_grad_cuda: empty plane");
+    QC_RETURN_IF(!d_pts || !d_R || !d_grid || !d_gout || !d_ggrid || !d_gR || !d_gpts,
+                 QC_ERR_INVALID_ARGUMENT, "kplanes_tilted_fuse_grad_cuda: null pointer");
+    const bool vec = (C % 4 == 0) && C <= 128 && aligned16(d_grid) && aligned16(d_gout) &&
+                     aligned16(d_ggrid);
+    if (vec) {
+        switch (C / 4) {
+            case 1: return bwd_v4<1>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
+            case 2: return bwd_v4<2>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
+            case 4: return bwd_v4<4>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
+            case 8: return bwd_v4<8>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
+            case 16: return bwd_v4<16>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
+            case 32: return bwd_v4<32>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
+            default: break;
+        }
+    }
+    int blocks = 0;
+    if (int st = grid_size(B, &blocks)) return st;
+    kpt_bwd_generic_kernel<<<blocks, kThreads, 18 * T * sizeof(float), stream>>>(
+        d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, C, H, W);
+    QC_CHECK_LAUNCH("kpt_bwd_generic_kernel launch");
+    return 0;
+}
+
+int kplanes_planes_to_channels_last_cuda(const float *d_src, float *d_dst, int P, int C, int H,
+                                         int W, cudaStream_t stream) {
+    QC_RETURN_IF((long long)H * W >= (1LL << 31), QC_ERR_INVALID_ARGUMENT,
+                 "kplanes_planes_to_channels_last_cuda: H*W too large");
+    return qc::kp::launch_transpose(d_src, d_dst, P, C, H * W, stream);
+}
+
+int kplanes_planes_from_channels_last_cuda(const float *d_src, float *d_dst, int P, int C, int H,
+                                           int W, cudaStream_t stream) {
+    QC_RETURN_IF((long long)H * W >= (1LL << 31), QC_ERR_INVALID_ARGUMENT,
+                 "kplanes_planes_from_channels_last_cuda: H*W too large");
+    return qc::kp::launch_transpose(d_src, d_dst, P, H * W, C, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,181 @@
+// pybind_core.cpp — the `quantem.cuda._core` extension: a torch-free binding
+// of the C ABI (include/quantem_cuda_b200.h). Tensors cross as integer device
+// pointers (tensor.data_ptr()), shapes as ints and the stream as the integer
+// torch.cuda.current_stream().cuda_stream, exactly like the reference's
+// `_core` (csrc/bindings.cpp:22-28, csrc/bindings/core.cpp:101-148,
+// csrc/bindings/core/ml.cpp:89-128). A non-zero status raises RuntimeError,
+// which is what the reference's std::runtime_error becomes in Python.
+#include <pybind11/pybind11.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "quantem_cuda_b200.h"
+
+namespace py = pybind11;
+
+namespace {
+
+void check(int status) {
+    if (status != 0)
+        throw std::runtime_error(std::string(quantem_cuda_status_string(status)) + ": " +
+                                 quantem_cuda_last_error());
+}
+
+template <typename T>
+T *ptr(uintptr_t v) {
+    return reinterpret_cast<T *>(v);
+}
+
+cudaStream_t stream_of(uintptr_t v) { return reinterpret_cast<cudaStream_t>(v); }
+
+}  // namespace
+
+PYBIND11_MODULE(_core, m) {
+    m.doc() = "quantem-cuda B200 kernels (raw-pointer API; use quantem.cuda.* instead)";
+    m.attr("__cudart_version__") = quantem_cuda_cudart_version();
+
+    // ── TV ──
+    m.def("tv_loss_3d_workspace_bytes", &tv_loss_3d_workspace_bytes, py::arg("B"), py::arg("D"),
+          py::arg("H"), py::arg("W"));
+
+    m.def(
+        "tv_loss_iso_3d_cuda",
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, float eps, uintptr_t ws,
+           size_t ws_bytes, uintptr_t stream) {
+            check(tv_loss_iso_3d_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W, eps,
+                                      ptr<void>(ws), ws_bytes, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
+        py::arg("W"), py::arg("eps"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_iso_3d_grad_cuda",
+        [](uintptr_t vol, uintptr_t g, uintptr_t grad, int B, int D, int H, int W, float eps,
+           uintptr_t stream) {
+            check(tv_loss_iso_3d_grad_cuda(ptr<const float>(vol), ptr<const float>(g),
+                                           ptr<float>(grad), B, D, H, W, eps, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("g_scaled_ptr"), py::arg("grad_vol_ptr"), py::arg("B"),
+        py::arg("D"), py::arg("H"), py::arg("W"), py::arg("eps"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_sq_3d_cuda",
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, uintptr_t ws, size_t ws_bytes,
+           uintptr_t stream) {
+            check(tv_loss_sq_3d_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W,
+                                     ptr<void>(ws), ws_bytes, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
+        py::arg("W"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_sq_3d_grad_cuda",
+        [](uintptr_t vol, uintptr_t g, uintptr_t grad, int B, int D, int H, int W,
+           uintptr_t stream) {
+            check(tv_loss_sq_3d_grad_cuda(ptr<const float>(vol), ptr<const float>(g),
+                                          ptr<float>(grad), B, D, H, W, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("g_ptr"), py::arg("grad_vol_ptr"), py::arg("B"), py::arg("D"),
+        py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_l1_3d_cuda",
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, uintptr_t ws, size_t ws_bytes,
+           uintptr_t stream) {
+            check(tv_loss_l1_3d_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W,
+                                     ptr<void>(ws), ws_bytes, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
+        py::arg("W"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_l1_3d_grad_cuda",
+        [](uintptr_t vol, uintptr_t g, uintptr_t grad, int B, int D, int H, int W,
+           uintptr_t stream) {
+            check(tv_loss_l1_3d_grad_cuda(ptr<const float>(vol), ptr<const float>(g),
+                                          ptr<float>(grad), B, D, H, W, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("g_ptr"), py::arg("grad_vol_ptr"), py::arg("B"), py::arg("D"),
+        py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_3d_slab_cuda",
+        [](int variant, int flags, uintptr_t vol, uintptr_t g, uintptr_t acc, uintptr_t grad,
+           int B, int Dp, int H, int W, int d_lo, int d_hi, int has_prev, int has_next, float eps,
+           float acc_scale, uintptr_t ws, size_t ws_bytes, uintptr_t stream) {
+            check(tv_loss_3d_slab_cuda(variant, flags, ptr<const float>(vol), ptr<const float>(g),
+                                       ptr<float>(acc), ptr<float>(grad), B, Dp, H, W, d_lo, d_hi,
+                                       has_prev, has_next, eps, acc_scale, ptr<void>(ws), ws_bytes,
+                                       stream_of(stream)));
+        },
+        py::arg("variant"), py::arg("flags"), py::arg("vol_ptr"), py::arg("g_ptr"),
+        py::arg("acc_ptr"), py::arg("grad_vol_ptr"), py::arg("B"), py::arg("Dp"), py::arg("H"),
+        py::arg("W"), py::arg("d_lo"), py::arg("d_hi"), py::arg("has_prev"), py::arg("has_next"),
+        py::arg("eps"), py::arg("acc_scale"), py::arg("ws_ptr"), py::arg("ws_bytes"),
+        py::arg("stream_ptr"));
+
+    m.attr("TV_SQ") = QC_TV_SQ;
+    m.attr("TV_ISO") = QC_TV_ISO;
+    m.attr("TV_L1") = QC_TV_L1;
+    m.attr("TV_LOSS") = QC_TV_LOSS;
+    m.attr("TV_GRAD") = QC_TV_GRAD;
+    m.attr("TV_ACC_OVERWRITE") = QC_TV_ACC_OVERWRITE;
+
+    // ── K-Planes ──
+    m.def(
+        "kplanes_tilted_fuse_cuda",
+        [](uintptr_t pts, uintptr_t r, uintptr_t grid, uintptr_t out, long B, int T, int C, int H,
+           int W, uintptr_t stream) {
+            check(kplanes_tilted_fuse_cuda(ptr<const float>(pts), ptr<const float>(r),
+                                           ptr<const float>(grid), ptr<float>(out), B, T, C, H, W,
+                                           stream_of(stream)));
+        },
+        "Fused TILTED K-Planes interpolation (one level). grid_ptr: fp32 [3T,H,W,C] "
+        "channels-last; out_ptr: fp32 [B,T*C], fully written.",
+        py::arg("pts_ptr"), py::arg("r_ptr"), py::arg("grid_ptr"), py::arg("out_ptr"), py::arg("B"),
+        py::arg("T"), py::arg("C"), py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
+
+    m.def(
+        "kplanes_tilted_fuse_grad_cuda",
+        [](uintptr_t pts, uintptr_t r, uintptr_t grid, uintptr_t gout, uintptr_t ggrid,
+           uintptr_t gr, uintptr_t gpts, long B, int T, int C, int H, int W, uintptr_t stream) {
+            check(kplanes_tilted_fuse_grad_cuda(ptr<const float>(pts), ptr<const float>(r),
+                                                ptr<const float>(grid), ptr<const float>(gout),
+                                                ptr<float>(ggrid), ptr<float>(gr), ptr<float>(gpts),
+                                                B, T, C, H, W, stream_of(stream)));
+        },
+        "Backward of kplanes_tilted_fuse. ggrid [3T,H,W,C], gr [T,3,3] and gpts [B,3] are "
+        "accumulated into (pre-zero them).",
+        py::arg("pts_ptr"), py::arg("r_ptr"), py::arg("grid_ptr"), py::arg("gout_ptr"),
+        py::arg("ggrid_ptr"), py::arg("gr_ptr"), py::arg("gpts_ptr"), py::arg("B"), py::arg("T"),
+        py::arg("C"), py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
+
+    m.def(
+        "kplanes_planes_to_channels_last_cuda",
+        [](uintptr_t src, uintptr_t dst, int P, int C, int H, int W, uintptr_t stream) {
+            check(kplanes_planes_to_channels_last_cuda(ptr<const float>(src), ptr<float>(dst), P, C,
+                                                       H, W, stream_of(stream)));
+        },
+        py::arg("src_ptr"), py::arg("dst_ptr"), py::arg("P"), py::arg("C"), py::arg("H"),
+        py::arg("W"), py::arg("stream_ptr"));
+
+    m.def(
+        "kplanes_planes_from_channels_last_cuda",
+        [](uintptr_t src, uintptr_t dst, int P, int C, int H, int W, uintptr_t stream) {
+            check(kplanes_planes_from_channels_last_cuda(ptr<const float>(src), ptr<float>(dst), P,
+                                                         C, H, W, stream_of(stream)));
+        },
+        py::arg("src_ptr"), py::arg("dst_ptr"), py::arg("P"), py::arg("C"), py::arg("H"),
+        py::arg("W"), py::arg("stream_ptr"));
+
+    m.def(
+        "device_fault_word",
+        [](int device, bool clear) {
+            unsigned int w = 0;
+            check(quantem_cuda_device_fault_word(device, &w, clear ? 1 : 0));
+            return w;
+        },
+        py::arg("device"), py::arg("clear") = false);
+}

@@ -1,0 +1,97 @@
+"""CPU-only checks of the product boundary: the C-ABI library loads and
+exports every entry point declared in include/*.h, the torch-free `_core`
+binding carries the reference's function names, and the host-side argument
+checks return status codes (no device work is issued)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+HEADERS = sorted((REPO / "include").glob("*.h"))
+LIB = REPO / "quantem-cuda_b200" / "quantem" / "cuda" / "libquantem_cuda_b200.so"
+
+
+def declared_functions() -> list[str]:
+    names = []
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"#.*", "", text)
+        names += re.findall(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", text)
+    skip = {"extern", "if", "sizeof"}
+    return sorted({n for n in names if n not in skip})
+
+
+def test_header_declares_the_hot_path():
+    names = declared_functions()
+    for required in (
+        "tv_loss_iso_3d_cuda",
+        "tv_loss_iso_3d_grad_cuda",
+        "tv_loss_sq_3d_cuda",
+        "tv_loss_sq_3d_grad_cuda",
+        "tv_loss_l1_3d_cuda",
+        "tv_loss_l1_3d_grad_cuda",
+        "kplanes_tilted_fuse_cuda",
+        "kplanes_tilted_fuse_grad_cuda",
+    ):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(LIB))
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_status_strings_and_version():
+    lib = ctypes.CDLL(str(LIB))
+    lib.quantem_cuda_status_string.restype = ctypes.c_char_p
+    assert lib.quantem_cuda_status_string(0) == b"QC_OK"
+    assert lib.quantem_cuda_status_string(10001) == b"QC_ERR_INVALID_ARGUMENT"
+    assert lib.quantem_cuda_cudart_version() >= 12000
+
+
+def test_argument_errors_need_no_device():
+    lib = ctypes.CDLL(str(LIB))
+    lib.quantem_cuda_last_error.restype = ctypes.c_char_p
+    f = lib.tv_loss_3d_slab_cuda
+    f.restype = ctypes.c_int
+    vp = ctypes.c_void_p
+    i = ctypes.c_int
+    fl = ctypes.c_float
+    f.argtypes = [i, i, vp, vp, vp, vp, i, i, i, i, i, i, i, i, fl, fl, vp, ctypes.c_size_t, vp]
+    # unknown variant
+    assert f(7, 1, None, None, None, None, 1, 4, 4, 4, 0, 4, 0, 0, 0.0, 1.0, None, 0, None) == 10001
+    assert b"variant" in lib.quantem_cuda_last_error()
+    # loss without a workspace
+    st = f(0, 1, vp(16), None, vp(16), None, 1, 4, 4, 4, 0, 4, 0, 0, 0.0, 1.0, None, 0, None)
+    assert st == 10002
+    # owned range outside the volume
+    assert f(0, 2, vp(16), vp(16), None, vp(16), 1, 4, 4, 4, 0, 5, 0, 0, 0.0, 1.0, None, 0, None) == 10001
+    k = lib.kplanes_tilted_fuse_cuda
+    k.restype = ctypes.c_int
+    k.argtypes = [vp, vp, vp, vp, ctypes.c_long, i, i, i, i, vp]
+    assert k(vp(16), vp(16), vp(16), vp(16), 8, 2, 1 << 16, 1 << 8, 1 << 8, None) == 10001  # C*H*W >= 2^31
+
+
+def test_core_binding_has_reference_names():
+    from quantem.cuda import _core
+
+    for name in (
+        "tv_loss_iso_3d_cuda",
+        "tv_loss_iso_3d_grad_cuda",
+        "tv_loss_sq_3d_cuda",
+        "tv_loss_sq_3d_grad_cuda",
+        "tv_loss_l1_3d_cuda",
+        "tv_loss_l1_3d_grad_cuda",
+        "kplanes_tilted_fuse_cuda",
+        "kplanes_tilted_fuse_grad_cuda",
+    ):
+        assert callable(getattr(_core, name))
+    assert int(_core.__cudart_version__) >= 12000
+    with pytest.raises(RuntimeError, match="QC_ERR_INVALID_ARGUMENT"):
+        _core.tv_loss_3d_slab_cuda(9, 1, 0, 0, 0, 0, 1, 2, 2, 2, 0, 2, 0, 0, 0.0, 1.0, 0, 0, 0)

@@ -1,0 +1,255 @@
+"""GPU parity of the fused tilted K-Planes kernels against the CPU oracle,
+the golden fixtures (the reference's grid_sample definition), the reference's
+own CUDA `_core` (when built into oracle/_ref) and the reference's behavioural
+tests (tests/core/ml/test_kplanes_tilted.py)."""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from quantem.cuda import _core
+    from quantem.cuda.core.ml import kplanes_tilted_fuse
+
+# (N, T, C, H, W): the reference's configs (test_kplanes_tilted.py:18-23) and
+# every vector width of the fast path (C = 4, 8, 16, 32, 64, 128), plus C not
+# a multiple of 4 and C above 128 (scalar path).
+CONFIGS = [
+    (37, 1, 1, 5, 5),
+    (257, 3, 5, 7, 9),
+    (4096, 4, 8, 200, 200),
+    (2000, 8, 32, 50, 33),
+    (777, 4, 4, 11, 13),
+    (1000, 2, 16, 20, 30),
+    (600, 2, 64, 17, 9),
+    (300, 3, 128, 16, 16),
+    (200, 2, 132, 8, 8),
+]
+
+FWD_RTOL = 1e-5
+
+
+def make_inputs(N, T, C, H, W, seed, pts_scale=1.1):
+    gen = torch.Generator().manual_seed(seed)
+    pts = torch.empty((N, 3)).uniform_(-pts_scale, pts_scale, generator=gen)
+    rot = torch.empty((T, 3, 3)).uniform_(-1.0, 1.0, generator=gen)
+    plane = torch.empty((3 * T, C, H, W)).uniform_(0.1, 0.5, generator=gen)
+    up = torch.randn((N, T * C), generator=gen)
+    return pts, rot, plane, up
+
+
+def grads(pts, rot, plane, up):
+    inp = [t.cuda().requires_grad_(True) for t in (pts, rot, plane)]
+    out = kplanes_tilted_fuse(*inp)
+    (out * up.cuda()).sum().backward()
+    return out.detach(), [t.grad for t in inp]
+
+
+def assert_rel_max(actual: torch.Tensor, expected: np.ndarray, rel: float, what: str):
+    exp = torch.from_numpy(np.ascontiguousarray(expected)).double()
+    err = (actual.detach().cpu().double() - exp).abs().max().item()
+    scale = exp.abs().max().item()
+    assert err <= rel * max(scale, 1e-30), f"{what}: max err {err:.3e} vs scale {scale:.3e}"
+
+
+@pytest.mark.parametrize("cfg", CONFIGS)
+def test_forward_matches_oracle(cfg):
+    pts, rot, plane, _ = make_inputs(*cfg, seed=1)
+    out = kplanes_tilted_fuse(pts.cuda(), rot.cuda(), plane.cuda()).cpu()
+    ref = torch.from_numpy(oracle.kplanes_fwd(pts.numpy(), rot.numpy(), plane.numpy()))
+    torch.testing.assert_close(out, ref, rtol=FWD_RTOL, atol=1e-7)
+
+
+@pytest.mark.parametrize("cfg", CONFIGS)
+def test_gradients_match_oracle(cfg):
+    pts, rot, plane, up = make_inputs(*cfg, seed=2)
+    _, (gp, gr, gg) = grads(pts, rot, plane, up)
+    o_gp, o_gr, o_gg = oracle.kplanes_bwd(pts.numpy(), rot.numpy(), plane.numpy(), up.numpy())
+    # gradient tolerance rel 1e-4 (atomics reorder sums), measured against each
+    # gradient's largest magnitude
+    assert_rel_max(gg, o_gg, 1e-4, "grad_plane")
+    assert_rel_max(gp, o_gp, 1e-4, "grad_pts")
+    assert_rel_max(gr, o_gr, 1e-4, "grad_rotations")
+
+
+def test_golden_fixtures_fp64_anchored(kp_golden):
+    """test_kplanes_tilted.py:71-95 on the committed fixtures: the kernel's
+    error against fp64 torch is no worse than 2x torch's own fp32 error."""
+    names = sorted({k.split("/")[0] for k in kp_golden if not k.startswith("border")})
+    for name in names:
+        t = {k: torch.from_numpy(kp_golden[f"{name}/{k}"]) for k in ("pts", "rotations", "plane", "upstream")}
+        out, got = grads(t["pts"], t["rotations"], t["plane"], t["upstream"])
+        torch.testing.assert_close(out.cpu(), torch.from_numpy(kp_golden[f"{name}/out_f32"]), rtol=1e-4, atol=5e-6)
+        for label, mine in zip(("pts", "rotations", "plane"), got):
+            ref64 = kp_golden[f"{name}/grad_{label}_f64"]
+            err_torch = np.abs(kp_golden[f"{name}/grad_{label}_f32"].astype(np.float64) - ref64).max()
+            err_kernel = np.abs(mine.cpu().double().numpy() - ref64).max()
+            assert err_kernel <= max(2.0 * err_torch, 1e-6), (name, label, err_kernel, err_torch)
+
+
+def test_points_exactly_on_border(kp_golden):
+    pts, rot, plane = (torch.from_numpy(kp_golden[f"border/{k}"]).cuda() for k in ("pts", "rotations", "plane"))
+    p = pts.clone().requires_grad_(True)
+    out = kplanes_tilted_fuse(p, rot, plane)
+    torch.testing.assert_close(out.cpu(), torch.from_numpy(kp_golden["border/out_f32"]), rtol=1e-5, atol=1e-6)
+    (g,) = torch.autograd.grad(out.sum(), p)
+    torch.testing.assert_close(g.cpu(), torch.from_numpy(kp_golden["border/grad_pts_f32"]), rtol=1e-4, atol=1e-6)
+    # with rotations requiring grad too (test_kplanes_tilted.py:118-128)
+    r = rot.clone().requires_grad_(True)
+    p2 = pts.clone().requires_grad_(True)
+    out2 = kplanes_tilted_fuse(p2, r, plane)
+    (g2,) = torch.autograd.grad(out2.sum(), p2)
+    torch.testing.assert_close(g2.cpu(), torch.from_numpy(kp_golden["border/grad_pts_f32"]), rtol=1e-4, atol=1e-6)
+
+
+def test_upstream_grad_scaling():
+    pts, rot, plane, _ = make_inputs(64, 2, 4, 9, 9, seed=3)
+    pl = plane.cuda().requires_grad_(True)
+    p, r = pts.cuda(), rot.cuda()
+    kplanes_tilted_fuse(p, r, pl).sum().backward()
+    g1 = pl.grad.clone()
+    pl.grad = None
+    (kplanes_tilted_fuse(p, r, pl) * 3.0).sum().backward()
+    torch.testing.assert_close(pl.grad, g1 * 3.0, rtol=1e-5, atol=1e-6)
+
+
+def test_non_contiguous_and_channels_last_inputs():
+    pts, rot, plane, up = make_inputs(128, 2, 8, 9, 11, seed=4)
+    p, r, pl = pts.cuda(), rot.cuda(), plane.cuda()
+    ref = kplanes_tilted_fuse(p, r, pl)
+    pts_nc = p.t().contiguous().t()
+    plane_nc = pl.permute(0, 1, 3, 2).contiguous().permute(0, 1, 3, 2)
+    assert not pts_nc.is_contiguous() and not plane_nc.is_contiguous()
+    torch.testing.assert_close(kplanes_tilted_fuse(pts_nc, r, plane_nc), ref, rtol=0, atol=0)
+    # a channels-last parameter takes the no-copy path, and its gradient keeps
+    # the parameter's layout
+    plane_cl = pl.contiguous(memory_format=torch.channels_last).requires_grad_(True)
+    out = kplanes_tilted_fuse(p, r, plane_cl)
+    torch.testing.assert_close(out, ref, rtol=0, atol=0)
+    (out * up.cuda()).sum().backward()
+    plane_c = pl.clone().requires_grad_(True)
+    (kplanes_tilted_fuse(p, r, plane_c) * up.cuda()).sum().backward()
+    assert plane_cl.grad.stride() == plane_cl.stride()
+    torch.testing.assert_close(plane_cl.grad, plane_c.grad, rtol=1e-5, atol=1e-7)
+
+
+def test_compile_fullgraph():
+    pts, rot, plane, _ = make_inputs(512, 2, 4, 17, 17, seed=5)
+    p, r, g = (t.cuda().requires_grad_(True) for t in (pts, rot, plane))
+
+    @torch.compile(fullgraph=True)
+    def f(a, b, c):
+        return kplanes_tilted_fuse(a, b, c).square().mean()
+
+    f(p, r, g).backward()
+    assert p.grad is not None and r.grad is not None and g.grad is not None
+
+
+def test_input_validation_on_device():
+    pts, rot, plane, _ = make_inputs(16, 2, 4, 9, 9, seed=6)
+    pts, rot, plane = pts.cuda(), rot.cuda(), plane.cuda()
+    with pytest.raises(ValueError, match=r"pts \[B, 3\]"):
+        kplanes_tilted_fuse(pts[:, :2], rot, plane)
+    with pytest.raises(ValueError, match=r"rotations \[T, 3, 3\]"):
+        kplanes_tilted_fuse(pts, rot[:, :2, :], plane)
+    with pytest.raises(ValueError, match=r"3\*T"):
+        kplanes_tilted_fuse(pts, rot, plane[:3])
+    with pytest.raises(TypeError, match="fp32-only"):
+        kplanes_tilted_fuse(pts.double(), rot, plane)
+
+
+def test_empty_point_set():
+    pts, rot, plane, _ = make_inputs(0, 2, 8, 9, 9, seed=7)
+    p = pts.cuda().requires_grad_(True)
+    pl = plane.cuda().requires_grad_(True)
+    out = kplanes_tilted_fuse(p, rot.cuda(), pl)
+    assert out.shape == (0, 16)
+    out.sum().backward()
+    assert torch.all(pl.grad == 0)
+
+
+def test_c_abi_accumulates_like_the_reference():
+    """kplanes_tilted_fuse_grad_cuda accumulates into ggrid, gR and gpts:
+    two calls on the same buffers give twice the gradient."""
+    lib = ctypes.CDLL(str(Path(_core.__file__).parent / "libquantem_cuda_b200.so"))
+    vp, i, L = ctypes.c_void_p, ctypes.c_int, ctypes.c_long
+    lib.kplanes_tilted_fuse_grad_cuda.argtypes = [vp] * 7 + [L, i, i, i, i, vp]
+    N, T, C, H, W = 500, 3, 32, 19, 23
+    pts, rot, plane, up = make_inputs(N, T, C, H, W, seed=8)
+    p, r, go = pts.cuda(), rot.cuda(), up.cuda()
+    grid_cl = plane.cuda().permute(0, 2, 3, 1).contiguous()
+    gg = torch.zeros_like(grid_cl)
+    gr = torch.zeros_like(r)
+    gp = torch.zeros_like(p)
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        assert lib.kplanes_tilted_fuse_grad_cuda(p.data_ptr(), r.data_ptr(), grid_cl.data_ptr(), go.data_ptr(),
+                                                 gg.data_ptr(), gr.data_ptr(), gp.data_ptr(), N, T, C, H, W, st) == 0
+    o_gp, o_gr, o_gg = oracle.kplanes_bwd(pts.numpy(), rot.numpy(), plane.numpy(), up.numpy())
+    assert_rel_max(gg.permute(0, 3, 1, 2), 2 * o_gg, 1e-4, "2x grad_plane")
+    assert_rel_max(gr, 2 * o_gr, 1e-4, "2x grad_rotations")
+    assert_rel_max(gp, 2 * o_gp, 1e-4, "2x grad_pts")
+
+
+@pytest.mark.skipif(oracle.ref_core() is None, reason="reference _core not built into oracle/_ref")
+@pytest.mark.parametrize("cfg", [(4096, 4, 8, 200, 200), (2000, 8, 32, 50, 33), (257, 3, 5, 7, 9)])
+def test_matches_reference_cuda_kernels(cfg):
+    ref = oracle.ref_core()
+    N, T, C, H, W = cfg
+    pts, rot, plane, up = make_inputs(*cfg, seed=9)
+    p, r, go = pts.cuda(), rot.cuda(), up.cuda()
+    grid_cl = plane.cuda().permute(0, 2, 3, 1).contiguous()
+    st = torch.cuda.current_stream().cuda_stream
+    ref_out = torch.empty((N, T * C), device="cuda")
+    ref.kplanes_tilted_fuse_cuda(p.data_ptr(), r.data_ptr(), grid_cl.data_ptr(), ref_out.data_ptr(), N, T, C, H, W, st)
+    out = kplanes_tilted_fuse(p, r, plane.cuda())
+    torch.testing.assert_close(out, ref_out, rtol=FWD_RTOL, atol=1e-7)
+    gg = torch.zeros_like(grid_cl)
+    gr = torch.zeros_like(r)
+    gp = torch.zeros_like(p)
+    ref.kplanes_tilted_fuse_grad_cuda(p.data_ptr(), r.data_ptr(), grid_cl.data_ptr(), go.data_ptr(), gg.data_ptr(),
+                                      gr.data_ptr(), gp.data_ptr(), N, T, C, H, W, st)
+    _, (m_gp, m_gr, m_gg) = grads(pts, rot, plane, up)
+    for mine, theirs, what in ((m_gg, gg.permute(0, 3, 1, 2), "plane"), (m_gr, gr, "rotations"), (m_gp, gp, "pts")):
+        err = (mine - theirs).abs().max().item()
+        assert err <= 1e-4 * theirs.abs().max().item(), (what, err)
+
+
+def test_benchmark_scale_properties():
+    """N = 2^20 points, T = 4, C = 32, 256x256 planes (the single-level
+    benchmark): forward against the oracle on a sample of points, gradient
+    linearity in the upstream gradient, and grad_pts against the oracle on the
+    sample (a point's gradient depends on that point only)."""
+    N, T, C, H, W = 1 << 20, 4, 32, 256, 256
+    gen = torch.Generator().manual_seed(2)
+    pts = torch.empty((N, 3)).uniform_(-1.0, 1.0, generator=gen)
+    q = torch.randn((T, 4), generator=gen)
+    q = q / q.norm(dim=1, keepdim=True)
+    w, x, y, z = q.unbind(1)
+    rot = torch.stack([
+        1 - 2 * (y * y + z * z), 2 * (x * y - z * w), 2 * (x * z + y * w),
+        2 * (x * y + z * w), 1 - 2 * (x * x + z * z), 2 * (y * z - x * w),
+        2 * (x * z - y * w), 2 * (y * z + x * w), 1 - 2 * (x * x + y * y),
+    ], dim=1).reshape(T, 3, 3)
+    plane = torch.empty((3 * T, C, H, W)).uniform_(0.1, 0.5, generator=gen)
+    up = torch.randn((N, T * C), generator=gen)
+    p, r, pl, go = pts.cuda(), rot.cuda(), plane.cuda(), up.cuda()
+    out = kplanes_tilted_fuse(p, r, pl)
+    sample = torch.randperm(N, generator=gen)[:4096]
+    ref = oracle.kplanes_fwd(pts[sample].numpy(), rot.numpy(), plane.numpy())
+    torch.testing.assert_close(out[sample.cuda()].cpu(), torch.from_numpy(ref), rtol=FWD_RTOL, atol=1e-7)
+    g1 = torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, pl, go)
+    g2 = torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, pl, 2 * go)
+    for a, b in zip(g1, g2):
+        assert_rel_max(b, (2 * a).cpu().numpy(), 1e-5, "linearity")
+    o_gp, _, _ = oracle.kplanes_bwd(pts[sample].numpy(), rot.numpy(), plane.numpy(), up[sample].numpy())
+    assert_rel_max(g1[0][sample.cuda()], o_gp, 1e-4, "grad_pts sample")

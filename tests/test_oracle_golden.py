@@ -1,0 +1,100 @@
+"""Pins the CPU oracle (oracle/) against golden vectors produced by the
+reference's own pure-torch definitions (tests/golden/make_golden.py)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+
+from conftest import golden_cases
+
+
+def _tv_names(tv_golden):
+    return [c for c in golden_cases(tv_golden) if not c.startswith("ptycho")]
+
+
+def test_tv_losses_match_reference_definitions(tv_golden):
+    for name in _tv_names(tv_golden):
+        vol = tv_golden[f"{name}/vol"]
+        iso_ref = tv_golden[f"{name}/iso_loss"]
+        if np.isnan(iso_ref):
+            # torch's mean over an empty corner set is NaN; the op's contract
+            # is loss 0 (reference test_tv_loss.py:99-107).
+            assert oracle.tv_iso_loss(vol, 1e-8) == 0.0
+        else:
+            np.testing.assert_allclose(oracle.tv_iso_loss(vol, 1e-8), iso_ref, rtol=1e-6, atol=1e-9)
+        np.testing.assert_allclose(oracle.tv_sq_loss(vol), tv_golden[f"{name}/sq_loss"], rtol=1e-6, atol=1e-9)
+        np.testing.assert_allclose(oracle.tv_l1_loss(vol), tv_golden[f"{name}/l1_sums"], rtol=1e-6, atol=1e-9)
+
+
+def test_tv_gradients_match_reference_definitions(tv_golden):
+    for name in _tv_names(tv_golden):
+        vol = tv_golden[f"{name}/vol"]
+        v4 = vol.reshape(-1, *vol.shape[-3:])
+        b, d, h, w = v4.shape
+        n = max(1, b * (d - 1) * (h - 1) * (w - 1))
+        np.testing.assert_allclose(
+            oracle.tv_iso_grad(vol, 1.0 / n, 1e-6), tv_golden[f"{name}/iso_grad_eps1e-6"], rtol=1e-4, atol=1e-7
+        )
+        np.testing.assert_allclose(oracle.tv_sq_grad(vol, 1.0), tv_golden[f"{name}/sq_grad"], rtol=1e-4, atol=1e-6)
+        np.testing.assert_allclose(
+            oracle.tv_l1_grad(vol, [0.7, 1.3, 0.2]), tv_golden[f"{name}/l1_grad_w0.7_1.3_0.2"], rtol=1e-4, atol=1e-6
+        )
+
+
+def test_degenerate_and_plateau_known_answers(tv_golden):
+    vol = tv_golden["degenerate_1x32x32/vol"]
+    assert oracle.tv_iso_sum(vol, 1e-8) == 0.0
+    assert np.all(oracle.tv_iso_grad(vol, 1.0, 1e-8) == 0.0)
+    assert oracle.tv_l1_loss(vol)[0] == 0.0
+    ones = np.ones((8, 8, 8), np.float32)
+    assert np.all(oracle.tv_l1_grad(ones, [1.0, 1.0, 1.0]) == 0.0)  # sign(0) = 0
+
+
+@pytest.mark.parametrize("key", ["ptycho_16_5.0_0.1", "ptycho_16_5.0_0.0", "ptycho_1_0.0_0.3"])
+def test_ptycho_recipe_from_l1_sums(tv_golden, key):
+    arr = tv_golden[f"{key}/array"]
+    wz, wxy = (float(x) for x in key.split("_")[2:4])
+    s, h, w = arr.shape
+    sums = oracle.tv_l1_loss(arr)
+    counts = np.maximum(np.array([(s - 1) * h * w, s * (h - 1) * w, s * h * (w - 1)], np.float64), 1)
+    wt = np.array([wz, wxy, wxy])
+    active = max(1, int(wz > 0) + 2 * int(wxy > 0))
+    loss = (wt * sums / counts).sum() / active
+    np.testing.assert_allclose(loss, tv_golden[f"{key}/loss"], rtol=1e-5, atol=1e-7)
+
+
+def _kp_names(kp_golden):
+    return [c for c in golden_cases(kp_golden) if c != "border"]
+
+
+def test_kplanes_forward_matches_grid_sample_reference(kp_golden):
+    for name in _kp_names(kp_golden):
+        g = {k: kp_golden[f"{name}/{k}"] for k in ("pts", "rotations", "plane")}
+        out = oracle.kplanes_fwd(g["pts"], g["rotations"], g["plane"])
+        # the reference's own forward tolerance against grid_sample (test_kplanes_tilted.py:68)
+        np.testing.assert_allclose(out, kp_golden[f"{name}/out_f32"], rtol=1e-4, atol=5e-6)
+        np.testing.assert_allclose(out, kp_golden[f"{name}/out_f64"], rtol=1e-4, atol=5e-6)
+
+
+def test_kplanes_gradients_fp64_anchored(kp_golden):
+    # test_kplanes_tilted.py:71-95: the oracle's error against the fp64 torch
+    # gradients must be no worse than 2x torch's own fp32 error.
+    for name in _kp_names(kp_golden):
+        g = {k: kp_golden[f"{name}/{k}"] for k in ("pts", "rotations", "plane", "upstream")}
+        got = oracle.kplanes_bwd(g["pts"], g["rotations"], g["plane"], g["upstream"])
+        for label, mine in zip(("pts", "rotations", "plane"), got):
+            ref64 = kp_golden[f"{name}/grad_{label}_f64"]
+            err_torch = np.abs(kp_golden[f"{name}/grad_{label}_f32"].astype(np.float64) - ref64).max()
+            err_oracle = np.abs(mine.astype(np.float64) - ref64).max()
+            assert err_oracle <= max(2.0 * err_torch, 1e-6), (name, label, err_oracle, err_torch)
+
+
+def test_kplanes_border_points(kp_golden):
+    pts, rot, plane = (kp_golden[f"border/{k}"] for k in ("pts", "rotations", "plane"))
+    out = oracle.kplanes_fwd(pts, rot, plane)
+    np.testing.assert_allclose(out, kp_golden["border/out_f32"], rtol=1e-5, atol=1e-6)
+    gp, _, _ = oracle.kplanes_bwd(pts, rot, plane, np.ones_like(out))
+    np.testing.assert_allclose(gp, kp_golden["border/grad_pts_f32"], rtol=1e-4, atol=1e-6)

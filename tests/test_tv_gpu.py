@@ -1,0 +1,307 @@
+"""GPU parity of the 3-D TV kernels against the CPU oracle, the golden
+fixtures, the reference's own CUDA `_core` (when built into oracle/_ref) and
+the reference's behavioural tests (tests/core/test_tv_loss.py)."""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from quantem.cuda import _core
+    from quantem.cuda.core import (
+        ptycho_tv_loss,
+        tv_loss_iso_3d,
+        tv_loss_iso_3d_fwd_grad,
+        tv_loss_l1_3d,
+        tv_loss_l1_3d_fwd_grad,
+        tv_loss_sq_3d,
+        tv_loss_sq_3d_fwd_grad,
+    )
+
+# Shapes: the reference's (test_tv_loss.py:10) plus TMA-path shapes with
+# partial tiles in H and W, several tiles, odd W (generic path) and a size-1 dim.
+SHAPES = [
+    (33, 57, 18),
+    (3, 32, 32, 32),
+    (2, 3, 16, 16, 16),
+    (1, 32, 32),
+    (2, 40, 70, 260),
+    (3, 17, 33, 132),
+    (2, 9, 31, 37),
+    (1, 64, 64, 64),
+    (5, 2, 3, 8),
+]
+
+FWD_RTOL = 1e-5  # forward tolerance (relative)
+GRAD_RTOL = 1e-4  # gradient tolerance (relative, element-wise)
+
+
+def rand_vol(shape, seed):
+    gen = torch.Generator().manual_seed(seed)
+    return torch.rand(shape, generator=gen, dtype=torch.float32)
+
+
+def n_corners(shape):
+    b = int(np.prod(shape[:-3])) if len(shape) > 3 else 1
+    d, h, w = shape[-3:]
+    return max(1, b * (d - 1) * (h - 1) * (w - 1))
+
+
+def assert_grad_close(actual: torch.Tensor, expected: np.ndarray):
+    exp = torch.from_numpy(np.ascontiguousarray(expected)).reshape(actual.shape)
+    scale = float(exp.abs().max()) if exp.numel() else 1.0
+    torch.testing.assert_close(actual.cpu(), exp, rtol=GRAD_RTOL, atol=1e-6 * max(scale, 1e-30))
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_losses_match_oracle(shape):
+    vol = rand_vol(shape, 11)
+    v = vol.cuda()
+    iso = tv_loss_iso_3d(v, eps=1e-8).item()
+    sq = tv_loss_sq_3d(v).item()
+    l1 = tv_loss_l1_3d(v).cpu().numpy()
+    np.testing.assert_allclose(iso, oracle.tv_iso_loss(vol.numpy(), 1e-8), rtol=FWD_RTOL, atol=1e-12)
+    np.testing.assert_allclose(sq, oracle.tv_sq_loss(vol.numpy()), rtol=FWD_RTOL, atol=1e-12)
+    np.testing.assert_allclose(l1, oracle.tv_l1_loss(vol.numpy()), rtol=FWD_RTOL, atol=1e-12)
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_autograd_gradients_match_oracle(shape):
+    vol = rand_vol(shape, 12)
+    x = vol.numpy()
+    v = vol.cuda().requires_grad_(True)
+    tv_loss_iso_3d(v, eps=1e-6).backward()
+    assert_grad_close(v.grad, oracle.tv_iso_grad(x, 1.0 / n_corners(shape), 1e-6))
+    v.grad = None
+    (2.5 * tv_loss_sq_3d(v)).backward()
+    assert_grad_close(v.grad, oracle.tv_sq_grad(x, 2.5))
+    v.grad = None
+    w = torch.tensor([0.7, 1.3, 0.2], device="cuda")
+    (tv_loss_l1_3d(v) * w).sum().backward()
+    assert_grad_close(v.grad, oracle.tv_l1_grad(x, [0.7, 1.3, 0.2]))
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_single_sweep_matches_pair(shape):
+    v = rand_vol(shape, 13).cuda()
+    loss, grad = tv_loss_iso_3d_fwd_grad(v, 0.5, eps=1e-8)
+    vv = v.clone().requires_grad_(True)
+    ref = tv_loss_iso_3d(vv, eps=1e-8)
+    (0.5 * ref).backward()
+    torch.testing.assert_close(loss, ref.detach(), rtol=1e-6, atol=0)
+    torch.testing.assert_close(grad, vv.grad, rtol=1e-6, atol=1e-12)
+
+    loss, grad = tv_loss_sq_3d_fwd_grad(v, 3.0)
+    vv.grad = None
+    (3.0 * tv_loss_sq_3d(vv)).backward()
+    torch.testing.assert_close(loss, tv_loss_sq_3d(v), rtol=1e-6, atol=0)
+    torch.testing.assert_close(grad, vv.grad, rtol=1e-6, atol=1e-12)
+
+    g3 = (0.7, 1.3, 0.2)
+    sums, grad = tv_loss_l1_3d_fwd_grad(v, g3)
+    vv.grad = None
+    (tv_loss_l1_3d(vv) * torch.tensor(g3, device="cuda")).sum().backward()
+    torch.testing.assert_close(sums, tv_loss_l1_3d(v), rtol=1e-6, atol=0)
+    torch.testing.assert_close(grad, vv.grad, rtol=1e-6, atol=1e-12)
+
+
+def test_golden_fixtures(tv_golden):
+    names = sorted({k.split("/")[0] for k in tv_golden if not k.startswith("ptycho")})
+    for name in names:
+        vol = torch.from_numpy(tv_golden[f"{name}/vol"]).cuda()
+        iso_ref = float(tv_golden[f"{name}/iso_loss"])
+        iso = tv_loss_iso_3d(vol, eps=1e-8).item()
+        if np.isnan(iso_ref):
+            assert iso == 0.0
+        else:
+            np.testing.assert_allclose(iso, iso_ref, rtol=FWD_RTOL)
+        np.testing.assert_allclose(tv_loss_sq_3d(vol).item(), float(tv_golden[f"{name}/sq_loss"]), rtol=FWD_RTOL)
+        np.testing.assert_allclose(tv_loss_l1_3d(vol).cpu().numpy(), tv_golden[f"{name}/l1_sums"], rtol=FWD_RTOL, atol=1e-9)
+        v = vol.clone().requires_grad_(True)
+        tv_loss_iso_3d(v, eps=1e-6).backward()
+        assert_grad_close(v.grad, tv_golden[f"{name}/iso_grad_eps1e-6"])
+        v.grad = None
+        tv_loss_sq_3d(v).backward()
+        assert_grad_close(v.grad, tv_golden[f"{name}/sq_grad"])
+        v.grad = None
+        (tv_loss_l1_3d(v) * torch.tensor([0.7, 1.3, 0.2], device="cuda")).sum().backward()
+        assert_grad_close(v.grad, tv_golden[f"{name}/l1_grad_w0.7_1.3_0.2"])
+
+
+@pytest.mark.parametrize("key", ["ptycho_16_5.0_0.1", "ptycho_16_5.0_0.0", "ptycho_1_0.0_0.3"])
+def test_ptycho_recipe(tv_golden, key):
+    wz, wxy = (float(x) for x in key.split("_")[2:4])
+    a = torch.from_numpy(tv_golden[f"{key}/array"]).cuda().requires_grad_(True)
+    loss = ptycho_tv_loss(a, (wz, wxy))
+    torch.testing.assert_close(loss.cpu(), torch.tensor(float(tv_golden[f"{key}/loss"])), rtol=1e-5, atol=1e-7)
+    loss.backward()
+    torch.testing.assert_close(a.grad.cpu(), torch.from_numpy(tv_golden[f"{key}/grad"]), rtol=1e-4, atol=1e-7)
+
+
+def test_deterministic_losses():
+    v = rand_vol((2, 40, 70, 260), 14).cuda()
+    for fn in (lambda x: tv_loss_iso_3d(x), tv_loss_sq_3d, tv_loss_l1_3d):
+        a, b = fn(v), fn(v)
+        assert torch.equal(a, b)
+
+
+def test_reference_behaviours():
+    # upstream scaling (test_tv_loss.py:77-86)
+    vol = rand_vol((16, 16, 16), 4).cuda()
+    v1 = vol.clone().requires_grad_(True)
+    v2 = vol.clone().requires_grad_(True)
+    tv_loss_sq_3d(v1).backward()
+    (3.0 * tv_loss_sq_3d(v2)).backward()
+    torch.testing.assert_close(v2.grad, 3.0 * v1.grad, rtol=1e-6, atol=1e-8)
+    # non-contiguous input (:89-96, :247-251)
+    nc = rand_vol((24, 18, 30), 5).cuda().permute(2, 0, 1)
+    assert not nc.is_contiguous()
+    x = nc.contiguous().cpu().numpy()
+    np.testing.assert_allclose(tv_loss_sq_3d(nc).item(), oracle.tv_sq_loss(x), rtol=FWD_RTOL)
+    np.testing.assert_allclose(tv_loss_iso_3d(nc).item(), oracle.tv_iso_loss(x, 1e-8), rtol=FWD_RTOL)
+    np.testing.assert_allclose(tv_loss_l1_3d(nc).cpu().numpy(), oracle.tv_l1_loss(x), rtol=FWD_RTOL)
+    # degenerate dims: iso loss 0 and grad 0 (:99-110), L1 empty axis (:238-244)
+    d = rand_vol((1, 32, 32), 6).cuda().requires_grad_(True)
+    loss = tv_loss_iso_3d(d)
+    assert loss.item() == 0.0
+    loss.backward()
+    assert torch.all(d.grad == 0)
+    assert tv_loss_l1_3d(d.detach())[0].item() == 0.0
+    # L1 plateau: sign(0) = 0 (:204-210)
+    ones = torch.ones(8, 8, 8, device="cuda", requires_grad=True)
+    tv_loss_l1_3d(ones).sum().backward()
+    assert torch.all(ones.grad == 0)
+
+
+def test_torch_compile_fullgraph():
+    def loss_fn(v):
+        return tv_loss_iso_3d(v, eps=1e-8) + 0.1 * tv_loss_sq_3d(v) + (tv_loss_l1_3d(v) * v.new_tensor([1.0, 0.5, 0.5])).sum()
+
+    compiled = torch.compile(loss_fn, fullgraph=True)
+    vol = rand_vol((32, 32, 32), 7).cuda().requires_grad_(True)
+    torch.testing.assert_close(compiled(vol), loss_fn(vol), rtol=1e-6, atol=1e-8)
+
+
+def test_slab_decomposition_reassembles_whole_volume():
+    """The D-slab form behind the multi-GPU path: slabs with one-plane halos,
+    owned ranges and boundary flags, summed and stitched, equal the whole."""
+    B, D, H, W = 2, 23, 37, 136
+    vol = rand_vol((B, D, H, W), 15).cuda()
+    g = torch.tensor([1.7], device="cuda")
+    g3 = torch.tensor([0.3, 1.1, 0.6], device="cuda")
+    cuts = [0, 5, 6, 14, 23]
+    for variant, gv, n_acc, eps in ((_core.TV_SQ, g, 1, 0.0), (_core.TV_ISO, g, 1, 1e-6), (_core.TV_L1, g3, 3, 0.0)):
+        ws = torch.empty(_core.tv_loss_3d_workspace_bytes(0, 0, 0, 0), dtype=torch.uint8, device="cuda")
+        whole_acc = torch.zeros(n_acc, device="cuda")
+        whole_grad = torch.empty_like(vol)
+        st = torch.cuda.current_stream().cuda_stream
+        _core.tv_loss_3d_slab_cuda(variant, 3, vol.data_ptr(), gv.data_ptr(), whole_acc.data_ptr(), whole_grad.data_ptr(),
+                                   B, D, H, W, 0, D, 0, 0, eps, 1.0, ws.data_ptr(), ws.numel(), st)
+        total = torch.zeros(n_acc, dtype=torch.float64, device="cuda")
+        stitched = torch.empty_like(vol)
+        for lo, hi in zip(cuts[:-1], cuts[1:]):
+            has_prev, has_next = lo > 0, hi < D
+            slab = torch.zeros((B, hi - lo + 2, H, W), device="cuda")
+            slab[:, 1 : hi - lo + 1] = vol[:, lo:hi]
+            if has_prev:
+                slab[:, 0] = vol[:, lo - 1]
+            if has_next:
+                slab[:, -1] = vol[:, hi]
+            acc = torch.zeros(n_acc, device="cuda")
+            grad = torch.full_like(slab, float("nan"))
+            _core.tv_loss_3d_slab_cuda(variant, 3, slab.data_ptr(), gv.data_ptr(), acc.data_ptr(), grad.data_ptr(),
+                                       B, hi - lo + 2, H, W, 1, hi - lo + 1, int(has_prev), int(has_next), eps, 1.0,
+                                       ws.data_ptr(), ws.numel(), st)
+            total += acc.double()
+            stitched[:, lo:hi] = grad[:, 1 : hi - lo + 1]
+            assert torch.isnan(grad[:, 0]).all() and torch.isnan(grad[:, -1]).all()  # halos untouched
+        torch.testing.assert_close(total.float(), whole_acc, rtol=1e-6, atol=0)
+        torch.testing.assert_close(stitched, whole_grad, rtol=1e-6, atol=1e-12)
+
+
+def test_c_abi_reference_signatures():
+    """Calls the reference-named entry points through the C ABI with the
+    reference's conventions (pre-zeroed accumulator, acc += sum)."""
+    lib = ctypes.CDLL(str(Path(_core.__file__).parent / "libquantem_cuda_b200.so"))
+    vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    lib.tv_loss_sq_3d_cuda.argtypes = [vp, vp, i, i, i, i, vp, ctypes.c_size_t, vp]
+    lib.tv_loss_iso_3d_grad_cuda.argtypes = [vp, vp, vp, i, i, i, i, f, vp]
+    vol = rand_vol((3, 20, 24, 68), 16)
+    v = vol.cuda()
+    ws = torch.empty(lib.tv_loss_3d_workspace_bytes(0, 0, 0, 0), dtype=torch.uint8, device="cuda")
+    acc = torch.full((1,), 2.0, device="cuda")  # accumulates on top of 2.0
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.tv_loss_sq_3d_cuda(v.data_ptr(), acc.data_ptr(), 3, 20, 24, 68, ws.data_ptr(), ws.numel(), st) == 0
+    np.testing.assert_allclose(acc.item() - 2.0, oracle.tv_sq_loss(vol.numpy()), rtol=FWD_RTOL)
+    g = torch.tensor([0.25], device="cuda")
+    grad = torch.empty_like(v)
+    assert lib.tv_loss_iso_3d_grad_cuda(v.data_ptr(), g.data_ptr(), grad.data_ptr(), 3, 20, 24, 68, f(1e-6), st) == 0
+    assert_grad_close(grad, oracle.tv_iso_grad(vol.numpy(), 0.25, 1e-6))
+
+
+@pytest.mark.skipif(oracle.ref_core() is None, reason="reference _core not built into oracle/_ref")
+@pytest.mark.parametrize("shape", [(3, 32, 32, 32), (2, 40, 70, 260), (33, 57, 18)])
+def test_matches_reference_cuda_kernels(shape):
+    ref = oracle.ref_core()
+    v = rand_vol(shape, 17).cuda().reshape(-1, *shape[-3:])
+    b, d, h, w = v.shape
+    st = torch.cuda.current_stream().cuda_stream
+    for name, eps in (("iso", 1e-8), ("sq", None), ("l1", None)):
+        acc = torch.zeros(3 if name == "l1" else 1, device="cuda")
+        if eps is None:
+            getattr(ref, f"tv_loss_{name}_3d_cuda")(v.data_ptr(), acc.data_ptr(), b, d, h, w, st)
+        else:
+            ref.tv_loss_iso_3d_cuda(v.data_ptr(), acc.data_ptr(), b, d, h, w, eps, st)
+        mine = {"iso": lambda: tv_loss_iso_3d(v, eps=1e-8) * n_corners(v.shape), "sq": lambda: tv_loss_sq_3d(v),
+                "l1": lambda: tv_loss_l1_3d(v)}[name]()
+        torch.testing.assert_close(mine.reshape(-1), acc, rtol=FWD_RTOL, atol=0)
+    # gradients
+    gs = torch.tensor([0.3], device="cuda")
+    g3 = torch.tensor([0.7, 1.3, 0.2], device="cuda")
+    for name, gv in (("iso", gs), ("sq", gs), ("l1", g3)):
+        ref_grad = torch.zeros_like(v)
+        if name == "iso":
+            ref.tv_loss_iso_3d_grad_cuda(v.data_ptr(), gv.data_ptr(), ref_grad.data_ptr(), b, d, h, w, 1e-6, st)
+            vv = v.clone().requires_grad_(True)
+            (tv_loss_iso_3d(vv, eps=1e-6) * (0.3 * n_corners(v.shape))).backward()
+        else:
+            getattr(ref, f"tv_loss_{name}_3d_grad_cuda")(v.data_ptr(), gv.data_ptr(), ref_grad.data_ptr(), b, d, h, w, st)
+            vv = v.clone().requires_grad_(True)
+            out = tv_loss_sq_3d(vv) * 0.3 if name == "sq" else (tv_loss_l1_3d(vv) * g3).sum()
+            out.backward()
+        scale = float(ref_grad.abs().max())
+        torch.testing.assert_close(vv.grad, ref_grad, rtol=GRAD_RTOL, atol=1e-6 * scale)
+
+
+def test_full_size_iso_l1_workload():
+    """The benchmark workload: [4, 256, 256, 256] with 1% of voxels equal to
+    their +W neighbour (sign(0) = 0 exercised), single-sweep ops vs oracle."""
+    gen = torch.Generator().manual_seed(1)
+    vol = torch.rand((4, 256, 256, 256), generator=gen)
+    flat = vol.view(-1, 256)
+    rows = torch.randint(0, flat.shape[0], (vol.numel() // 100,), generator=gen)
+    cols = torch.randint(0, 255, rows.shape, generator=gen)
+    flat[rows, cols] = flat[rows, cols + 1]
+    x = vol.numpy()
+    v = vol.cuda()
+    loss, grad = tv_loss_iso_3d_fwd_grad(v, 1.0, eps=1e-8)
+    np.testing.assert_allclose(loss.item(), oracle.tv_iso_loss(x, 1e-8), rtol=FWD_RTOL)
+    assert_grad_close(grad, oracle.tv_iso_grad(x, 1.0 / n_corners(x.shape), 1e-8))
+    del grad
+    sums, grad = tv_loss_l1_3d_fwd_grad(v, 1.0)
+    np.testing.assert_allclose(sums.cpu().numpy(), oracle.tv_l1_loss(x), rtol=FWD_RTOL)
+    assert_grad_close(grad, oracle.tv_l1_grad(x, [1.0, 1.0, 1.0]))
+
+
+def test_no_kernel_gave_up_waiting():
+    torch.cuda.synchronize()
+    assert _core.device_fault_word(torch.cuda.current_device()) == 0

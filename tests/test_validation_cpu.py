@@ -1,0 +1,91 @@
+"""Input validation of the public wrappers, on CPU tensors (mirrors the
+reference's CPU-tier tests: test_tv_loss.py:125-138, 264-266;
+test_kplanes_tilted.py:168-186)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from quantem.cuda.core import (
+    ptycho_tv_loss,
+    tv_loss_iso_3d,
+    tv_loss_iso_3d_fwd_grad,
+    tv_loss_l1_3d,
+    tv_loss_l1_3d_fwd_grad,
+    tv_loss_sq_3d,
+    tv_loss_sq_3d_fwd_grad,
+)
+from quantem.cuda.core.ml import kplanes_tilted_fuse
+
+
+def test_rejects_cpu_tensor():
+    vol = torch.rand(8, 8, 8)
+    for fn in (tv_loss_iso_3d, tv_loss_sq_3d, tv_loss_l1_3d):
+        with pytest.raises(ValueError, match="CUDA"):
+            fn(vol)
+    for fn in (tv_loss_iso_3d_fwd_grad, tv_loss_sq_3d_fwd_grad, tv_loss_l1_3d_fwd_grad):
+        with pytest.raises(ValueError, match="CUDA"):
+            fn(vol)
+
+
+def test_rejects_bad_dtype_and_ndim():
+    with pytest.raises(TypeError, match="fp32"):
+        tv_loss_iso_3d(torch.rand(8, 8, 8, dtype=torch.float64))
+    with pytest.raises(ValueError, match="ndim"):
+        tv_loss_sq_3d(torch.rand(8, 8))
+    with pytest.raises(ValueError, match="ndim"):
+        tv_loss_l1_3d(torch.rand(8))
+    with pytest.raises(ValueError, match=r"\[S, H, W\]"):
+        ptycho_tv_loss(torch.rand(2, 3, 4, 5), (1.0, 1.0))
+
+
+def test_kplanes_cpu_rejected():
+    pts = torch.rand(8, 3)
+    rotations = torch.rand(2, 3, 3)
+    plane = torch.rand(6, 4, 9, 9)
+    with pytest.raises(ValueError, match="CUDA"):
+        kplanes_tilted_fuse(pts, rotations, plane)
+
+
+def test_kplanes_shape_validation_messages():
+    pts = torch.rand(16, 3)
+    rotations = torch.rand(2, 3, 3)
+    plane = torch.rand(6, 4, 9, 9)
+    with pytest.raises(ValueError, match=r"pts \[B, 3\]"):
+        kplanes_tilted_fuse(pts[:, :2], rotations, plane)
+    with pytest.raises(ValueError, match=r"rotations \[T, 3, 3\]"):
+        kplanes_tilted_fuse(pts, rotations[:, :2, :], plane)
+    with pytest.raises(ValueError, match=r"3\*T"):
+        kplanes_tilted_fuse(pts, rotations, plane[:3])
+    with pytest.raises(TypeError, match="fp32-only"):
+        kplanes_tilted_fuse(pts.double(), rotations, plane)
+
+
+def test_ops_registered_with_reference_names():
+    for name in (
+        "tv_loss_iso_3d",
+        "tv_loss_iso_3d_bwd",
+        "tv_loss_sq_3d",
+        "tv_loss_sq_3d_bwd",
+        "tv_loss_l1_3d",
+        "tv_loss_l1_3d_bwd",
+        "kplanes_tilted_fuse",
+        "kplanes_tilted_fuse_bwd",
+    ):
+        assert hasattr(torch.ops.quantem_cuda, name)
+
+
+def test_fake_impls_give_output_shapes():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        vol = torch.empty(2, 5, 6, 7)
+        assert torch.ops.quantem_cuda.tv_loss_iso_3d(vol, 1e-8).shape == ()
+        assert torch.ops.quantem_cuda.tv_loss_l1_3d(vol).shape == (3,)
+        loss, grad = torch.ops.quantem_cuda.tv_loss_sq_3d_fwd_grad(vol, torch.empty(1))
+        assert loss.shape == () and grad.shape == vol.shape
+        out = torch.ops.quantem_cuda.kplanes_tilted_fuse(
+            torch.empty(10, 3), torch.empty(2, 3, 3), torch.empty(6, 4, 5, 5)
+        )
+        assert out.shape == (10, 8)
