@@ -17,9 +17,10 @@
  * op layer permutes to channels-last only for the GPU; _ops.py:21-25).
  *
  * The forward is fp32 with every multiply-add written as fmaf() in the order
- * an fp32 GPU evaluates the reference expressions (rotation and bilinear sums
- * left to right), so it reproduces a correctly-rounded fused evaluation on any
- * host. Gradients accumulate in fp64.
+ * nvcc contracts the reference's expressions (measured on the GPU: a0*x0 +
+ * a1*x1 + a2*x2 becomes fma(a2, x2, fma(a0, x0, a1*x1)), and likewise for the
+ * four-term bilinear sum), so it reproduces the reference kernel's forward
+ * values bit for bit on any host. Gradients accumulate in fp64.
  */
 #include <math.h>
 #include <stddef.h>
@@ -57,10 +58,16 @@ static OTap otap(float gx, float gy, int H, int W) {
     return t;
 }
 
+/* a0*x0 + a1*x1 + a2*x2 as an fp32 GPU evaluates the reference's expression
+ * after contraction: fma(a2, x2, fma(a0, x0, a1*x1)). */
+static float odot3(float a0, float x0, float a1, float x1, float a2, float x2) {
+    return fmaf(a2, x2, fmaf(a0, x0, a1 * x1));
+}
+
 static void orotate(const float *Rt, float px, float py, float pz, float r[3]) {
-    r[0] = fmaf(Rt[2], pz, fmaf(Rt[1], py, Rt[0] * px));
-    r[1] = fmaf(Rt[5], pz, fmaf(Rt[4], py, Rt[3] * px));
-    r[2] = fmaf(Rt[8], pz, fmaf(Rt[7], py, Rt[6] * px));
+    r[0] = odot3(Rt[0], px, Rt[1], py, Rt[2], pz);
+    r[1] = odot3(Rt[3], px, Rt[4], py, Rt[5], pz);
+    r[2] = odot3(Rt[6], px, Rt[7], py, Rt[8], pz);
 }
 
 static void ocoords(const float r[3], int p, float *gx, float *gy) {
@@ -70,8 +77,10 @@ static void ocoords(const float r[3], int p, float *gx, float *gy) {
     *gy = r[iy[p]];
 }
 
+/* w0*v0 + w1*v1 + w2*v2 + w3*v3, contracted the same way:
+ * fma(w3, v3, fma(w2, v2, fma(w0, v0, w1*v1))). */
 static float obilerp(const float w[4], float v0, float v1, float v2, float v3) {
-    return fmaf(w[3], v3, fmaf(w[2], v2, fmaf(w[1], v1, w[0] * v0)));
+    return fmaf(w[3], v3, fmaf(w[2], v2, fmaf(w[0], v0, w[1] * v1)));
 }
 
 /* pts [N,3], R [T,3,3], plane [3T,C,H,W] -> out [N, T*C] */

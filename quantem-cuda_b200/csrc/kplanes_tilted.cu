@@ -18,11 +18,12 @@
 // atomics on grad_pts) and writes a point's T·C outputs as full lines.
 //
 // The tap arithmetic (unnormalise, clamp, floor, bilinear weights, border
-// gradient mask) is written with the same operation order as the reference's
-// make_tap (kplanes_tilted.cu:69-94) and the rotation as explicit FMAs in the
-// reference's left-to-right order, so forward values agree bit for bit with
-// the reference kernel wherever the compiler contracts the reference's
-// expressions the same way.
+// gradient mask) follows the operation order of the reference's make_tap
+// (kplanes_tilted.cu:69-94). The rotation and the bilinear sums are written as
+// explicit FMAs in the order nvcc gives the reference's plain expressions
+// (a0*x0 + a1*x1 + ... contracts to fma(.., fma(a0, x0, a1*x1))), so forward
+// values agree bit for bit with the reference kernel and with the CPU oracle,
+// which uses the same explicit order.
 //
 // Backward. Plane gradients go out as red.global.add.v4.f32 (one L2 atomic op
 // per 16 B instead of four); corners with zero bilinear weight are skipped.
@@ -67,16 +68,24 @@ __device__ __forceinline__ Tap make_tap(float gx, float gy, int H, int W) {
     return t;
 }
 
-__device__ __forceinline__ void rotate(const float *Rt, float px, float py, float pz, float &rx,
-                                       float &ry, float &rz) {
-    rx = __fmaf_rn(Rt[2], pz, __fmaf_rn(Rt[1], py, __fmul_rn(Rt[0], px)));
-    ry = __fmaf_rn(Rt[5], pz, __fmaf_rn(Rt[4], py, __fmul_rn(Rt[3], px)));
-    rz = __fmaf_rn(Rt[8], pz, __fmaf_rn(Rt[7], py, __fmul_rn(Rt[6], px)));
+// r = R_t·p as a0*x0 + a1*x1 + a2*x2 evaluated the way nvcc contracts that
+// expression: the first product is fused around the second, then the third
+// is fused on top — fma(a2, x2, fma(a0, x0, a1*x1)).
+__device__ __forceinline__ float dot3(float a0, float x0, float a1, float x1, float a2, float x2) {
+    return __fmaf_rn(a2, x2, __fmaf_rn(a0, x0, __fmul_rn(a1, x1)));
 }
 
-// w0*v0 + w1*v1 + w2*v2 + w3*v3, accumulated left to right.
+__device__ __forceinline__ void rotate(const float *Rt, float px, float py, float pz, float &rx,
+                                       float &ry, float &rz) {
+    rx = dot3(Rt[0], px, Rt[1], py, Rt[2], pz);
+    ry = dot3(Rt[3], px, Rt[4], py, Rt[5], pz);
+    rz = dot3(Rt[6], px, Rt[7], py, Rt[8], pz);
+}
+
+// w0*v0 + w1*v1 + w2*v2 + w3*v3 in the same contracted order:
+// fma(w3, v3, fma(w2, v2, fma(w0, v0, w1*v1))).
 __device__ __forceinline__ float bilerp(const float w[4], float v0, float v1, float v2, float v3) {
-    return __fmaf_rn(w[3], v3, __fmaf_rn(w[2], v2, __fmaf_rn(w[1], v1, __fmul_rn(w[0], v0))));
+    return __fmaf_rn(w[3], v3, __fmaf_rn(w[2], v2, __fmaf_rn(w[0], v0, __fmul_rn(w[1], v1))));
 }
 
 __device__ __forceinline__ void plane_coords(float rx, float ry, float rz, int p, float &gx,

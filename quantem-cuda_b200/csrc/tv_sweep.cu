@@ -19,18 +19,28 @@
 //
 // This reproduces the reference's gradient kernels term by term
 // (tv_loss.cu:320-330 for squared, :462-473 for L1, :165-188 for iso) while
-// letting one sweep produce loss and gradient together.
+// letting one sweep produce loss and gradient together, each difference being
+// evaluated once and used by both voxels it touches.
 //
-// Fast path (W % 4 == 0, 16-byte aligned pointers): a warp-specialised CTA
-// marches along D through a column of 16×128 (H×W) tiles. One producer warp
-// streams each plane tile plus a one-voxel halo (18 rows × 136 columns; the
+// Fast path (W % 4 == 0, 16-byte aligned pointers). A CTA marches along D
+// through a column of (R·NW) × 128 (H × W) tiles. One producer warp streams
+// each plane tile with a one-voxel halo — (R·NW + 2) rows × 136 columns; the
 // left halo is 4 columns wide because a TMA box must start on a 16-byte
-// boundary) into a 4-stage shared-memory ring with cp.async.bulk.tensor; four
-// consumer warps each own 4 rows × 128 columns (4 consecutive columns per
-// lane), keep the previous plane's Fd in registers, and take in-plane
-// neighbours from shared memory and warp shuffles. Each voxel is read from HBM
-// once per sweep (halo rows/columns are shared with neighbouring tiles, which
-// the chunk-major schedule processes at the same time, so they hit L2).
+// boundary — into an S-stage shared-memory ring with cp.async.bulk.tensor
+// (no multicast). NW consumer warps each own R consecutive rows × 128 columns
+// (4 columns per lane, moved as float4). Per plane a consumer thread:
+//   * keeps Fd of the previous plane in registers (R × 4 values),
+//   * carries Fh from row to row down its strip, computing Fh of the row
+//     above the strip once (1 extra row per R),
+//   * takes Fw of the column to its left from the neighbouring lane by
+//     shuffle; the tile's left halo column is computed once per plane with
+//     the warp's lanes standing for rows, then broadcast to lane 0.
+// Square roots use the MUFU approximations (sqrt/rsqrt.approx, relative error
+// ~2^-23), which keeps the kernel free of the IEEE slow path's branches.
+//
+// Each voxel is read from HBM once per sweep: halo rows and columns are shared
+// with neighbouring tiles, which the chunk-major schedule runs at the same
+// time, so they hit L2.
 //
 // Reductions are deterministic: each CTA writes fp64 partial sums to a
 // caller-owned workspace slot, and a one-CTA finalize kernel, launched with
@@ -54,13 +64,25 @@ constexpr int kAccSlots = 3;        // L1 keeps one sum per axis
 
 // ── per-variant arithmetic ───────────────────────────────────────────────
 
-__device__ __forceinline__ float sgnf(float x) {
-    // torch's convention for d|x|/dx: sign(0) = 0 (tv_loss.cu:434-436).
-    return (float)((x > 0.0f) - (x < 0.0f));
+__device__ __forceinline__ float sqrt_approx(float x) {
+    float y;
+    asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float rsqrt_approx(float x) {
+    float y;
+    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// g·sign(x) with sign(0) = 0: torch's convention for d|x|/dx (tv_loss.cu:434-436).
+__device__ __forceinline__ float gsign(float g, float x) {
+    return x > 0.f ? g : (x < 0.f ? -g : 0.f);
 }
 
 struct Gains {
-    float gmul;      // multiplies the divergence
+    float gmul;        // multiplies the divergence
     float gd, gh, gw;  // L1 per-axis gains folded into F
 };
 
@@ -71,39 +93,39 @@ __device__ __forceinline__ void voxel_flux(float v, float nd, float nh, float nw
                                            bool vw, bool own, float eps, const Gains &gn,
                                            float &Fd, float &Fh, float &Fw, float &l0, float &l1,
                                            float &l2) {
-    const float dd = nd - v, dh = nh - v, dw = nw - v;
+    const float dd = vd ? nd - v : 0.f;
+    const float dh = vh ? nh - v : 0.f;
+    const float dw = vw ? nw - v : 0.f;
     if constexpr (V == QC_TV_SQ) {
-        if (LOSS && own) {
-            float s = vd ? dd * dd : 0.f;
-            s += vh ? dh * dh : 0.f;
-            s += vw ? dw * dw : 0.f;
-            l0 += s;
+        if (LOSS) {
+            const float s = __fmaf_rn(dw, dw, __fmaf_rn(dh, dh, dd * dd));
+            l0 += own ? s : 0.f;
         }
         if (GRAD) {
-            Fd = vd ? dd : 0.f;
-            Fh = vh ? dh : 0.f;
-            Fw = vw ? dw : 0.f;
+            Fd = dd;
+            Fh = dh;
+            Fw = dw;
         }
     } else if constexpr (V == QC_TV_L1) {
         if (LOSS && own) {
-            l0 += vd ? fabsf(dd) : 0.f;
-            l1 += vh ? fabsf(dh) : 0.f;
-            l2 += vw ? fabsf(dw) : 0.f;
+            l0 += fabsf(dd);
+            l1 += fabsf(dh);
+            l2 += fabsf(dw);
         }
         if (GRAD) {
-            Fd = vd ? gn.gd * sgnf(dd) : 0.f;
-            Fh = vh ? gn.gh * sgnf(dh) : 0.f;
-            Fw = vw ? gn.gw * sgnf(dw) : 0.f;
+            Fd = gsign(gn.gd, dd);
+            Fh = gsign(gn.gh, dh);
+            Fw = gsign(gn.gw, dw);
         }
     } else {  // QC_TV_ISO
         const bool ok = vd && vh && vw;
         const float x = dd * dd + dh * dh + dw * dw + eps;
-        if (LOSS && own) l0 += ok ? sqrtf(x) : 0.f;
+        if (LOSS) l0 += (ok && own) ? sqrt_approx(x) : 0.f;
         if (GRAD) {
-            const float inv = rsqrtf(x);
-            Fd = ok ? dd * inv : 0.f;
-            Fh = ok ? dh * inv : 0.f;
-            Fw = ok ? dw * inv : 0.f;
+            const float inv = ok ? rsqrt_approx(x) : 0.f;
+            Fd = dd * inv;
+            Fh = dh * inv;
+            Fw = dw * inv;
         }
     }
 }
@@ -114,15 +136,16 @@ template <int V>
 __device__ __forceinline__ float flux_from_up(float v, float up, float up_nd, float up_nw,
                                               bool has_up, bool vd, bool vw_up, float eps,
                                               const Gains &gn) {
+    const float dh = has_up ? v - up : 0.f;
     if constexpr (V == QC_TV_SQ) {
-        return has_up ? v - up : 0.f;
+        return dh;
     } else if constexpr (V == QC_TV_L1) {
-        return has_up ? gn.gh * sgnf(v - up) : 0.f;
+        return gsign(gn.gh, dh);
     } else {
-        const float dd = up_nd - up, dh = v - up, dw = up_nw - up;
         const bool ok = has_up && vd && vw_up;
-        const float inv = rsqrtf(dd * dd + dh * dh + dw * dw + eps);
-        return ok ? dh * inv : 0.f;
+        const float dd = up_nd - up, dw = up_nw - up;
+        const float inv = ok ? rsqrt_approx(dd * dd + dh * dh + dw * dw + eps) : 0.f;
+        return dh * inv;
     }
 }
 
@@ -132,15 +155,16 @@ template <int V>
 __device__ __forceinline__ float flux_from_left(float v, float lf, float lf_nd, float lf_nh,
                                                 bool has_left, bool vd, bool vh, float eps,
                                                 const Gains &gn) {
+    const float dw = has_left ? v - lf : 0.f;
     if constexpr (V == QC_TV_SQ) {
-        return has_left ? v - lf : 0.f;
+        return dw;
     } else if constexpr (V == QC_TV_L1) {
-        return has_left ? gn.gw * sgnf(v - lf) : 0.f;
+        return gsign(gn.gw, dw);
     } else {
-        const float dd = lf_nd - lf, dh = lf_nh - lf, dw = v - lf;
         const bool ok = has_left && vd && vh;
-        const float inv = rsqrtf(dd * dd + dh * dh + dw * dw + eps);
-        return ok ? dw * inv : 0.f;
+        const float dd = lf_nd - lf, dh = lf_nh - lf;
+        const float inv = ok ? rsqrt_approx(dd * dd + dh * dh + dw * dw + eps) : 0.f;
+        return dw * inv;
     }
 }
 
@@ -202,30 +226,34 @@ __device__ __forceinline__ Unit decode_unit(const Plan &pl, long long u, int til
 
 // ── fast path: TMA ring + warp-specialised D-march ───────────────────────
 
-constexpr int kTileW = 128;                        // owned columns per tile
-constexpr int kHaloW = 4;                          // halo columns each side
-constexpr int kBoxW = kTileW + 2 * kHaloW;         // 136
-constexpr int kRowsPerWarp = 4;
-constexpr int kConsumerWarps = 4;
-constexpr int kTileH = kRowsPerWarp * kConsumerWarps;  // 16
-constexpr int kBoxH = kTileH + 2;                  // 18
-constexpr int kStages = 4;
-constexpr uint32_t kBoxBytes = kBoxW * kBoxH * 4;  // 9792
-constexpr int kStageFloats = 2464;                 // 9856 B: keeps each stage 128-B aligned
-constexpr int kSweepThreads = (kConsumerWarps + 1) * 32;
-static_assert(kStageFloats * 4 >= (int)kBoxBytes, "stage too small");
-static_assert((kStageFloats * 4) % 128 == 0, "stage alignment");
+constexpr int kTileW = 128;                 // owned columns per tile
+constexpr int kHaloW = 4;                   // halo columns each side
+constexpr int kBoxW = kTileW + 2 * kHaloW;  // 136
 
+template <int R_, int NW_, int S_, int MINB_>
+struct Geom {
+    static constexpr int R = R_;        // rows per consumer warp
+    static constexpr int NW = NW_;      // consumer warps
+    static constexpr int S = S_;        // ring stages
+    static constexpr int MinB = MINB_;  // CTAs per SM the register budget is sized for
+    static constexpr int TileH = R * NW;
+    static constexpr int BoxH = TileH + 2;
+    static constexpr uint32_t BoxBytes = kBoxW * BoxH * 4;
+    static constexpr int StageFloats = (int)(((BoxBytes + 127) / 128) * 32);  // 128-B aligned
+    static constexpr int Threads = (NW + 1) * 32;
+};
+
+template <class G>
 struct SweepSmem {
-    float stage[kStages][kStageFloats];
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
-    double red[kConsumerWarps][kAccSlots];
+    float stage[G::S][G::StageFloats];
+    uint64_t full[G::S];
+    uint64_t empty[G::S];
+    double red[G::NW][kAccSlots];
     int abort;
 };
-static_assert(sizeof(SweepSmem) + 128 <= 48 * 1024, "sweep smem must fit without opt-in");
 
-__device__ __forceinline__ bool aborted(const SweepSmem &sm) {
+template <class G>
+__device__ __forceinline__ bool aborted(const SweepSmem<G> &sm) {
     return *reinterpret_cast<const volatile int *>(&sm.abort) != 0;
 }
 
@@ -235,22 +263,27 @@ __device__ __forceinline__ float4 lds4(const float *s, int row, int col) {
 __device__ __forceinline__ float lds1(const float *s, int row, int col) {
     return s[row * kBoxW + col];
 }
+__device__ __forceinline__ float comp(const float4 &v, int j) {
+    return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
+}
 
-template <int V, bool LOSS, bool GRAD>
-__global__ void __launch_bounds__(kSweepThreads) tv_sweep_tma_kernel(
+template <int V, bool LOSS, bool GRAD, class G>
+__global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
     const __grid_constant__ CUtensorMap map, const float *__restrict__ g,
     float *__restrict__ grad, double *__restrict__ partials, const Plan pl) {
+    constexpr int R = G::R, NW = G::NW, S = G::S;
     // TMA destinations must be 128-byte aligned: align the ring explicitly
     // (the launch requests sizeof(SweepSmem) + 128 bytes).
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    SweepSmem &sm = *reinterpret_cast<SweepSmem *>(smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
+    SweepSmem<G> &sm = *reinterpret_cast<SweepSmem<G> *>(
+        smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], kConsumerWarps);
+            mbar_init(&sm.empty[s], NW);
         }
         sm.abort = 0;
         fence_mbar_init();
@@ -259,35 +292,40 @@ __global__ void __launch_bounds__(kSweepThreads) tv_sweep_tma_kernel(
 
     double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0;
 
-    if (warp == kConsumerWarps) {
+    if (warp == NW) {
         // ── producer warp: one lane issues every TMA load ──
         if (lane == 0) {
             prefetch_tensor_map(&map);
-            long long seq = 0;
-            long long last_seq[kStages] = {-1, -1, -1, -1};
+            int seq = 0;
+            int last_seq[S];
+#pragma unroll
+            for (int s = 0; s < S; ++s) last_seq[s] = -1;
             for (long long u = blockIdx.x; u < pl.n_units && !aborted(sm); u += gridDim.x) {
-                const Unit U = decode_unit<GRAD>(pl, u, kTileH, kTileW);
+                const Unit U = decode_unit<GRAD>(pl, u, G::TileH, kTileW);
                 const int zbase = U.n * pl.Dp;
                 for (int p = U.first; p <= U.last; ++p, ++seq) {
-                    const int s = (int)(seq % kStages);
-                    if (seq >= kStages) {
-                        const uint32_t par = (uint32_t)(((seq / kStages) - 1) & 1);
+                    const int s = seq % S;
+                    if (seq >= S) {
+                        const uint32_t par = (uint32_t)(((seq / S) - 1) & 1);
                         if (!mbar_wait_bounded(&sm.empty[s], par, kWaitLimitNs)) {
                             atomicOr(&g_tv_fault_word, 1u);
                             sm.abort = 1;
                             break;
                         }
                     }
-                    mbar_arrive_expect_tx(&sm.full[s], kBoxBytes);
+                    mbar_arrive_expect_tx(&sm.full[s], G::BoxBytes);
                     tma_load_3d(sm.stage[s], &map, U.w0 - kHaloW, U.h0 - 1, zbase + p, &sm.full[s]);
-                    last_seq[s] = seq;
+#pragma unroll
+                    for (int q = 0; q < S; ++q)
+                        if (q == s) last_seq[q] = seq;
                 }
             }
             // Never leave a bulk copy in flight into shared memory that is about
             // to be released: wait (bounded) for the last load of every stage.
-            for (int s = 0; s < kStages; ++s) {
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
                 if (last_seq[s] < 0) continue;
-                const uint32_t par = (uint32_t)((last_seq[s] / kStages) & 1);
+                const uint32_t par = (uint32_t)((last_seq[s] / S) & 1);
                 if (!mbar_wait_bounded(&sm.full[s], par, kWaitLimitNs))
                     atomicOr(&g_tv_fault_word, 1u);
             }
@@ -295,133 +333,151 @@ __global__ void __launch_bounds__(kSweepThreads) tv_sweep_tma_kernel(
     } else {
         // ── consumer warps ──
         const Gains gn = load_gains<V>(g, pl.scale);
-        const int r0 = warp * kRowsPerWarp;  // first tile row of this warp's strip
+        const int r0 = warp * R;             // first tile row of this warp's strip
         const int scol = kHaloW + 4 * lane;  // smem column of this lane's first voxel
-        float Fd_prev[kRowsPerWarp][4];
-        long long seq = 0;
+        const size_t plane_elems = (size_t)pl.H * pl.W;
+        float Fd_prev[R][4];
+        int seq = 0;
 
         for (long long u = blockIdx.x; u < pl.n_units; u += gridDim.x) {
-            const Unit U = decode_unit<GRAD>(pl, u, kTileH, kTileW);
+            const Unit U = decode_unit<GRAD>(pl, u, G::TileH, kTileW);
             const int wcol = U.w0 + 4 * lane;  // global column of the lane's first voxel
-            const bool col_in = wcol < pl.W;   // W % 4 == 0: 4 voxels all in or all out
+            const int hbase = U.h0 + r0;       // global row of the strip's first row
+            // Per-unit masks (constant along D).
+            const bool col_in = wcol < pl.W;   // W % 4 == 0: the 4 voxels are all in or all out
+            bool vw[4];
 #pragma unroll
-            for (int i = 0; i < kRowsPerWarp; ++i)
+            for (int j = 0; j < 4; ++j) vw[j] = wcol + j + 1 < pl.W;
+            const bool has_up = hbase >= 1;
+            // Lanes stand for rows when computing the left halo column.
+            const int hrow = r0 + (lane < R ? lane : R - 1);  // tile row
+            const bool hrow_vh = U.h0 + hrow + 1 < pl.H;
+            const bool halo_left = U.w0 >= 1;
+            float *gbase = grad + (((size_t)U.n * pl.Dp) * pl.H + hbase) * (size_t)pl.W + wcol;
+
+#pragma unroll
+            for (int i = 0; i < R; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) Fd_prev[i][j] = 0.f;
 
-            const long long q0 = seq;
-            {
-                const int s0 = (int)(q0 % kStages);
-                if (!mbar_wait_bounded(&sm.full[s0], (uint32_t)((q0 / kStages) & 1),
-                                       kWaitLimitNs)) {
-                    atomicOr(&g_tv_fault_word, 1u);
-                    sm.abort = 1;
-                }
+            const int q0 = seq;
+            if (!mbar_wait_bounded(&sm.full[q0 % S], (uint32_t)((q0 / S) & 1), kWaitLimitNs)) {
+                atomicOr(&g_tv_fault_word, 1u);
+                sm.abort = 1;
             }
             if (aborted(sm)) break;
 
             for (int p = U.first; p < U.d_end; ++p) {
-                const long long qc = q0 + (p - U.first);
+                const int qc = q0 + (p - U.first);
                 const bool has_nxt = (p + 1) <= U.last;
-                const float *Sc = sm.stage[qc % kStages];
+                const float *Sc = sm.stage[qc % S];
                 const float *Sn = Sc;
                 if (has_nxt) {
-                    const long long qn = qc + 1;
-                    const int sn = (int)(qn % kStages);
-                    if (!mbar_wait_bounded(&sm.full[sn], (uint32_t)((qn / kStages) & 1),
+                    const int qn = qc + 1;
+                    if (!mbar_wait_bounded(&sm.full[qn % S], (uint32_t)((qn / S) & 1),
                                            kWaitLimitNs)) {
                         atomicOr(&g_tv_fault_word, 1u);
                         sm.abort = 1;
                     }
-                    Sn = sm.stage[sn];
+                    Sn = sm.stage[qn % S];
                 }
                 if (aborted(sm)) break;
                 const bool owned = p >= U.d_start;
                 float l0 = 0.f, l1 = 0.f, l2 = 0.f;
 
-                // Row above the strip (tile row r0-1 is smem row r0).
-                float4 up = make_float4(0.f, 0.f, 0.f, 0.f), up_nd = up;
-                float up_right = 0.f;
-                if (GRAD) {
-                    up = lds4(Sc, r0, scol);
-                    if (V == QC_TV_ISO) {
-                        up_nd = lds4(Sn, r0, scol);
-                        up_right = __shfl_down_sync(0xffffffffu, up.x, 1);
-                        if (lane == 31) up_right = lds1(Sc, r0, scol + 4);
-                    }
-                }
-                float Fh_up[4];
-                float4 cur = lds4(Sc, r0 + 1, scol);
-                const int hbase = U.h0 + r0;
-
-#pragma unroll
-                for (int i = 0; i < kRowsPerWarp; ++i) {
-                    const int h = hbase + i;
-                    const int srow = r0 + 1 + i;  // smem row of tile row r0+i
-                    const float4 down = lds4(Sc, srow + 1, scol);
-                    const float4 nxt = has_nxt ? lds4(Sn, srow, scol) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    float right = __shfl_down_sync(0xffffffffu, cur.x, 1);
-                    if (lane == 31) right = lds1(Sc, srow, scol + 4);
-
-                    const float cv[4] = {cur.x, cur.y, cur.z, cur.w};
-                    const float nv[4] = {nxt.x, nxt.y, nxt.z, nxt.w};
-                    const float dv[4] = {down.x, down.y, down.z, down.w};
-                    const float rv[4] = {cur.y, cur.z, cur.w, right};
-                    const bool row_in = h < pl.H;
-                    const bool vh = h + 1 < pl.H;
-                    float Fd[4], Fh[4], Fw[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const bool vw = wcol + j + 1 < pl.W;
-                        voxel_flux<V, LOSS, GRAD>(cv[j], nv[j], dv[j], rv[j], has_nxt, vh, vw,
-                                                  owned && row_in && col_in, pl.eps, gn, Fd[j],
-                                                  Fh[j], Fw[j], l0, l1, l2);
-                    }
-
+                if (!owned) {
+                    // Halo plane below the chunk: only Fd is needed, for the
+                    // first owned plane's backward difference.
                     if (GRAD) {
-                        // Fh one row up: from the halo row for the strip's first
-                        // row, else carried from the previous row.
-                        if (i == 0) {
-                            const float uv[4] = {up.x, up.y, up.z, up.w};
-                            const float und[4] = {up_nd.x, up_nd.y, up_nd.z, up_nd.w};
-                            const float unw[4] = {up.y, up.z, up.w, up_right};
+                        float4 cur = lds4(Sc, r0 + 1, scol);
 #pragma unroll
-                            for (int j = 0; j < 4; ++j)
-                                Fh_up[j] = flux_from_up<V>(cv[j], uv[j], und[j], unw[j], h >= 1,
-                                                           has_nxt, wcol + j + 1 < pl.W, pl.eps,
-                                                           gn);
+                        for (int i = 0; i < R; ++i) {
+                            const float4 down = lds4(Sc, r0 + i + 2, scol);
+                            const float4 nxt = lds4(Sn, r0 + i + 1, scol);
+                            float right = __shfl_down_sync(0xffffffffu, cur.x, 1);
+                            if (lane == 31) right = lds1(Sc, r0 + i + 1, scol + 4);
+                            const bool vh = hbase + i + 1 < pl.H;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                float Fh, Fw, d0 = 0.f, d1 = 0.f, d2 = 0.f;
+                                voxel_flux<V, false, true>(comp(cur, j), comp(nxt, j), comp(down, j),
+                                                           j < 3 ? comp(cur, j + 1) : right, true, vh,
+                                                           vw[j], false, pl.eps, gn, Fd_prev[i][j],
+                                                           Fh, Fw, d0, d1, d2);
+                            }
+                            cur = down;
                         }
-                        // Fw one column left of the lane's first voxel.
-                        float lf = __shfl_up_sync(0xffffffffu, cur.w, 1);
-                        if (lane == 0) lf = lds1(Sc, srow, scol - 1);
+                    }
+                } else {
+                    // Left halo column (global column w0-1), lanes as rows.
+                    float fw_halo = 0.f;
+                    if (GRAD) {
+                        const float lf = lds1(Sc, hrow + 1, kHaloW - 1);
+                        const float v0 = lds1(Sc, hrow + 1, kHaloW);
                         float lf_nd = 0.f, lf_nh = 0.f;
                         if (V == QC_TV_ISO) {
-                            lf_nd = __shfl_up_sync(0xffffffffu, nxt.w, 1);
-                            lf_nh = __shfl_up_sync(0xffffffffu, down.w, 1);
-                            if (lane == 0) {
-                                lf_nd = has_nxt ? lds1(Sn, srow, scol - 1) : 0.f;
-                                lf_nh = lds1(Sc, srow + 1, scol - 1);
+                            lf_nd = lds1(Sn, hrow + 1, kHaloW - 1);
+                            lf_nh = lds1(Sc, hrow + 2, kHaloW - 1);
+                        }
+                        fw_halo = flux_from_left<V>(v0, lf, lf_nd, lf_nh, halo_left, has_nxt,
+                                                    hrow_vh, pl.eps, gn);
+                    }
+                    // Row above the strip (tile row r0-1 is smem row r0).
+                    float4 cur = lds4(Sc, r0 + 1, scol);
+                    float Fh_up[4] = {0.f, 0.f, 0.f, 0.f};
+                    if (GRAD) {
+                        const float4 up = lds4(Sc, r0, scol);
+                        float4 up_nd = make_float4(0.f, 0.f, 0.f, 0.f);
+                        float up_right = 0.f;
+                        if (V == QC_TV_ISO) {
+                            up_nd = lds4(Sn, r0, scol);
+                            up_right = __shfl_down_sync(0xffffffffu, up.x, 1);
+                            if (lane == 31) up_right = lds1(Sc, r0, scol + 4);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            Fh_up[j] = flux_from_up<V>(comp(cur, j), comp(up, j), comp(up_nd, j),
+                                                       j < 3 ? comp(up, j + 1) : up_right, has_up,
+                                                       has_nxt, vw[j], pl.eps, gn);
+                    }
+
+                    float *gp = gbase + (size_t)p * plane_elems;
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        const int h = hbase + i;
+                        const bool row_in = h < pl.H;
+                        const bool vh = h + 1 < pl.H;
+                        const float4 down = lds4(Sc, r0 + i + 2, scol);
+                        const float4 nxt =
+                            has_nxt ? lds4(Sn, r0 + i + 1, scol) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        float right = __shfl_down_sync(0xffffffffu, cur.x, 1);
+                        if (lane == 31) right = lds1(Sc, r0 + i + 1, scol + 4);
+                        const bool own = row_in && col_in;
+                        float Fd[4], Fh[4], Fw[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            voxel_flux<V, LOSS, GRAD>(comp(cur, j), comp(nxt, j), comp(down, j),
+                                                      j < 3 ? comp(cur, j + 1) : right, has_nxt, vh,
+                                                      vw[j], own, pl.eps, gn, Fd[j], Fh[j], Fw[j],
+                                                      l0, l1, l2);
+                        if (GRAD) {
+                            const float fw_from_lane = __shfl_up_sync(0xffffffffu, Fw[3], 1);
+                            const float fw_from_halo = __shfl_sync(0xffffffffu, fw_halo, i);
+                            const float Fw_left0 = lane == 0 ? fw_from_halo : fw_from_lane;
+                            float4 gv;
+                            gv.x = gn.gmul * ((Fd_prev[i][0] - Fd[0]) + (Fh_up[0] - Fh[0]) + (Fw_left0 - Fw[0]));
+                            gv.y = gn.gmul * ((Fd_prev[i][1] - Fd[1]) + (Fh_up[1] - Fh[1]) + (Fw[0] - Fw[1]));
+                            gv.z = gn.gmul * ((Fd_prev[i][2] - Fd[2]) + (Fh_up[2] - Fh[2]) + (Fw[1] - Fw[2]));
+                            gv.w = gn.gmul * ((Fd_prev[i][3] - Fd[3]) + (Fh_up[3] - Fh[3]) + (Fw[2] - Fw[3]));
+                            if (own) __stcs(reinterpret_cast<float4 *>(gp + (size_t)i * pl.W), gv);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                Fd_prev[i][j] = Fd[j];
+                                Fh_up[j] = Fh[j];
                             }
                         }
-                        const float Fw_left0 = flux_from_left<V>(cv[0], lf, lf_nd, lf_nh,
-                                                                 wcol >= 1, has_nxt, vh, pl.eps, gn);
-                        const float Fw_left[4] = {Fw_left0, Fw[0], Fw[1], Fw[2]};
-                        float gv[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            gv[j] = gn.gmul * ((Fd_prev[i][j] - Fd[j]) + (Fh_up[j] - Fh[j]) +
-                                               (Fw_left[j] - Fw[j]));
-                            Fd_prev[i][j] = Fd[j];
-                            Fh_up[j] = Fh[j];
-                        }
-                        if (owned && row_in && col_in) {
-                            const size_t idx =
-                                (((size_t)U.n * pl.Dp + p) * pl.H + h) * (size_t)pl.W + wcol;
-                            __stcs(reinterpret_cast<float4 *>(grad + idx),
-                                   make_float4(gv[0], gv[1], gv[2], gv[3]));
-                        }
+                        cur = down;
                     }
-                    cur = down;
                 }
                 if (LOSS) {
                     acc0 += (double)l0;
@@ -432,14 +488,14 @@ __global__ void __launch_bounds__(kSweepThreads) tv_sweep_tma_kernel(
                 }
                 // Release plane p's stage.
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.empty[qc % kStages]);
+                if (lane == 0) mbar_arrive(&sm.empty[qc % S]);
             }
             if (aborted(sm)) break;
             if (U.last == U.d_end) {
                 // The +1 halo plane was only ever a "next" plane: release it too.
-                const long long ql = q0 + (U.last - U.first);
+                const int ql = q0 + (U.last - U.first);
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.empty[ql % kStages]);
+                if (lane == 0) mbar_arrive(&sm.empty[ql % S]);
             }
             seq = q0 + (U.last - U.first + 1);
         }
@@ -448,7 +504,7 @@ __global__ void __launch_bounds__(kSweepThreads) tv_sweep_tma_kernel(
     griddep_launch_dependents();
 
     if (LOSS) {
-        if (warp < kConsumerWarps) {
+        if (warp < NW) {
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) {
                 acc0 += __shfl_xor_sync(0xffffffffu, acc0, off);
@@ -464,7 +520,7 @@ __global__ void __launch_bounds__(kSweepThreads) tv_sweep_tma_kernel(
         __syncthreads();
         if (threadIdx.x < kAccSlots) {
             double t = 0.0;
-            for (int w = 0; w < kConsumerWarps; ++w) t += sm.red[w][threadIdx.x];
+            for (int w = 0; w < NW; ++w) t += sm.red[w][threadIdx.x];
             partials[(size_t)blockIdx.x * kAccSlots + threadIdx.x] = t;
         }
     }
@@ -611,14 +667,13 @@ int get_encode_fn(EncodeTiledFn *fn) {
     return 0;
 }
 
-// Chooses the D-chunk of the chunk-major units. Time is modelled, in units of
-// one plane per CTA, as the larger of the critical path (rounds of units, each
-// chunk + halo planes long) and the bandwidth bound (all plane loads spread
-// over the CTAs it takes to saturate HBM, taken as 60% of the resident ones).
+// Chooses the D-chunk of the chunk-major units. Each CTA runs its units one
+// after another, so the time is modelled as rounds × (chunk + halo planes),
+// rounds = ceil(units / resident CTAs); ties go to the larger chunk (fewer
+// halo planes re-read from HBM).
 void choose_chunking(Plan &pl, int max_ctas, int halo_planes) {
     const int Dn = pl.d_hi - pl.d_lo;
-    const double sat = 0.6 * max_ctas;
-    double best = 1e300;
+    long long best = -1;
     int best_dc = Dn, prev_dc = -1;
     for (int nch = 1; nch <= Dn; ++nch) {
         const int dc = (Dn + nch - 1) / nch;
@@ -627,10 +682,8 @@ void choose_chunking(Plan &pl, int max_ctas, int halo_planes) {
         const int real_nch = (Dn + dc - 1) / dc;
         const long long U = (long long)real_nch * pl.n_cols;
         const long long rounds = (U + max_ctas - 1) / max_ctas;
-        const double path = (double)rounds * (dc + halo_planes);
-        const double bw = (double)U * (dc + halo_planes) / sat;
-        const double cost = path > bw ? path : bw;
-        if (cost < best * 0.999) {
+        const long long cost = rounds * (dc + halo_planes);
+        if (best < 0 || cost < best) {
             best = cost;
             best_dc = dc;
         }
@@ -641,19 +694,29 @@ void choose_chunking(Plan &pl, int max_ctas, int halo_planes) {
     pl.n_units = (long long)pl.n_chunks * pl.n_cols;
 }
 
+// Fast-path geometry: rows per consumer warp, consumer warps, ring stages and
+// the CTAs per SM that registers are budgeted for. QC_TV_R, QC_TV_NW, QC_TV_S
+// and QC_TV_MINB override it at build time.
+#ifdef QC_TV_R
+using FastGeom = Geom<QC_TV_R, QC_TV_NW, QC_TV_S, QC_TV_MINB>;
+#else
+using FastGeom = Geom<8, 4, 3, 3>;
+#endif
+
 template <int V, bool LOSS, bool GRAD>
 int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, double *partials,
                    Plan pl, int *grid_out, cudaStream_t stream) {
     int sms = 0;
     if (int st = device_sm_count(&sms)) return st;
     if (use_tma) {
+        using G = FastGeom;
         EncodeTiledFn encode = nullptr;
         if (int st = get_encode_fn(&encode)) return st;
         CUtensorMap map;
         const cuuint64_t dims[3] = {(cuuint64_t)pl.W, (cuuint64_t)pl.H,
                                     (cuuint64_t)pl.B * (cuuint64_t)pl.Dp};
         const cuuint64_t strides[2] = {(cuuint64_t)pl.W * 4, (cuuint64_t)pl.W * pl.H * 4};
-        const cuuint32_t box[3] = {kBoxW, kBoxH, 1};
+        const cuuint32_t box[3] = {kBoxW, G::BoxH, 1};
         const cuuint32_t estr[3] = {1, 1, 1};
         CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(vol),
                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -663,21 +726,25 @@ int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, 
             return set_error(QC_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled failed (CUresult %d) for "
                              "W=%d H=%d planes=%lld", (int)cr, pl.W, pl.H,
                              (long long)pl.B * pl.Dp);
-        auto kern = tv_sweep_tma_kernel<V, LOSS, GRAD>;
-        const size_t smem = sizeof(SweepSmem) + 128;  // below 48 KB: no opt-in needed
+        auto kern = tv_sweep_tma_kernel<V, LOSS, GRAD, G>;
+        const size_t smem = sizeof(SweepSmem<G>) + 128;
+        // Above 48 KB of dynamic shared memory needs an opt-in; it is a
+        // per-device function attribute, so set it on every launch (cheap).
+        QC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                    "cudaFuncSetAttribute(tv_sweep_tma_kernel)");
         int occ = 0;
-        QC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kSweepThreads, smem),
+        QC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, G::Threads, smem),
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
         int max_ctas = occ * sms;
         if (max_ctas > kMaxPartials) max_ctas = kMaxPartials;
         if (max_ctas < 1) max_ctas = 1;
-        pl.n_ht = (pl.H + kTileH - 1) / kTileH;
+        pl.n_ht = (pl.H + G::TileH - 1) / G::TileH;
         pl.n_wt = (pl.W + kTileW - 1) / kTileW;
         pl.n_cols = pl.B * pl.n_ht * pl.n_wt;
         choose_chunking(pl, max_ctas, 1 + (GRAD ? 1 : 0));
         const long long rounds = (pl.n_units + max_ctas - 1) / max_ctas;
         const int grid = (int)((pl.n_units + rounds - 1) / rounds);
-        kern<<<grid, kSweepThreads, smem, stream>>>(map, g, grad, partials, pl);
+        kern<<<grid, G::Threads, smem, stream>>>(map, g, grad, partials, pl);
         QC_CHECK_LAUNCH("tv_sweep_tma_kernel launch");
         *grid_out = grid;
     } else {

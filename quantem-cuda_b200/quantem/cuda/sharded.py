@@ -156,6 +156,7 @@ def kplanes_fwd_bwd_sharded(
     grad_out_local: Tensor,
     group=None,
     async_op: bool = False,
+    fwd_bwd: Callable | None = None,
 ):
     """Forward and backward of one K-Planes level over point-sharded ranks.
 
@@ -163,11 +164,16 @@ def kplanes_fwd_bwd_sharded(
     the plane and rotation gradients are summed over ranks with all_reduce
     (``work`` is the pending collective when ``async_op``, so that the next
     level's compute overlaps it; call ``work.wait()`` before reading them).
+    ``fwd_bwd(pts, rotations, plane, grad_out) -> (out, g_pts, g_rot, g_plane)``
+    replaces the CUDA ops (host-logic tests on CPU ranks).
     """
-    from quantem.cuda.core.ml._ops import _kplanes_tilted_fuse, _kplanes_tilted_fuse_bwd
+    if fwd_bwd is None:
+        from quantem.cuda.core.ml._ops import _kplanes_tilted_fuse, _kplanes_tilted_fuse_bwd
 
-    out = _kplanes_tilted_fuse(pts_local, rotations, plane)
-    g_pts, g_rot, g_plane = _kplanes_tilted_fuse_bwd(pts_local, rotations, plane, grad_out_local)
+        out = _kplanes_tilted_fuse(pts_local, rotations, plane)
+        g_pts, g_rot, g_plane = _kplanes_tilted_fuse_bwd(pts_local, rotations, plane, grad_out_local)
+    else:
+        out, g_pts, g_rot, g_plane = fwd_bwd(pts_local, rotations, plane, grad_out_local)
     work = None
     _, world = _rank_world(group)
     if world > 1:
