@@ -14,8 +14,7 @@
 // vector reductions, so a C=32 corner row (128 B, one L2 line) is one
 // instruction for 8 lanes. A warp holds 32/L groups, i.e. a tile of 32/L
 // consecutive points, and loops over the T rotations for its tile. Looping
-// rotations inside the warp keeps a point's gradient in registers (no
-// atomics on grad_pts) and writes a point's T·C outputs as full lines.
+// Each (point, rotation) output row of C floats is written as whole lines.
 //
 // The tap arithmetic (unnormalise, clamp, floor, bilinear weights, border
 // gradient mask) follows the operation order of the reference's make_tap
@@ -27,10 +26,10 @@
 //
 // Backward. Plane gradients go out as red.global.add.v4.f32 (one L2 atomic op
 // per 16 B instead of four); corners with zero bilinear weight are skipped.
-// Coordinate gradients are reduced over the group's lanes with xor shuffles,
-// mapped to dL/dr with the border masks, and accumulated into grad_pts in
-// registers across rotations; grad_R goes through per-CTA shared-memory
-// accumulators flushed once per CTA.
+// Coordinate gradients are reduced over the group's lanes with xor shuffles
+// and mapped to dL/dr with the border masks; grad_pts takes three scalar
+// reductions per (point, rotation); grad_R is accumulated in registers per
+// group and reduced across the block once, one global reduction per entry.
 #include "qc_common.cuh"
 
 namespace qc {
@@ -96,8 +95,22 @@ __device__ __forceinline__ void plane_coords(float rx, float ry, float rz, int p
 }
 
 // ── vectorised path: C == 4*L, L in {1, 2, 4, 8, 16, 32} ────────────────────
+//
+// Rotation-major grid: blockIdx.y is the rotation t and blockIdx.x strides
+// over points. Blocks are dispatched x-fastest, so the GPU works through the
+// rotations one after another and only the three planes of about one rotation
+// (and, backward, their three gradient planes) are live at a time: they stay
+// in L2 instead of being re-read from (or, for the gradient reductions,
+// read-modified-written in) HBM.
 
 constexpr int kThreads = 256;
+
+// Blocks per SM the backward's register budget is sized for (QC_KP_BWD_MINB
+// overrides it at build time).
+#ifndef QC_KP_BWD_MINB
+#define QC_KP_BWD_MINB 2
+#endif
+constexpr int kBwdMinBlocks = QC_KP_BWD_MINB;
 
 template <int L>
 __global__ void __launch_bounds__(kThreads) kpt_fwd_v4_kernel(const float *__restrict__ pts,
@@ -107,13 +120,15 @@ __global__ void __launch_bounds__(kThreads) kpt_fwd_v4_kernel(const float *__res
                                                               int T, int H, int W) {
     constexpr int C = 4 * L;
     constexpr int G = 32 / L;  // points per warp tile
-    extern __shared__ float sR[];
-    for (int i = threadIdx.x; i < T * 9; i += blockDim.x) sR[i] = R[i];
-    __syncthreads();
+    const int t = blockIdx.y;
+    float Rt[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) Rt[k] = __ldg(R + 9 * t + k);
 
     const int lane = threadIdx.x & 31;
     const int grp = lane / L, c4 = 4 * (lane % L);
     const long long planeHWC = (long long)H * W * C;
+    const float *g0 = grid + (long long)(3 * t) * planeHWC + c4;
     const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
 
@@ -122,32 +137,28 @@ __global__ void __launch_bounds__(kThreads) kpt_fwd_v4_kernel(const float *__res
         if (b >= B) continue;
         const float px = __ldg(pts + 3 * b), py = __ldg(pts + 3 * b + 1),
                     pz = __ldg(pts + 3 * b + 2);
-        float *orow = out + b * (long long)(T * C) + c4;
-#pragma unroll 2
-        for (int t = 0; t < T; ++t) {
-            float rx, ry, rz;
-            rotate(sR + 9 * t, px, py, pz, rx, ry, rz);
-            float4 s[3];
+        float rx, ry, rz;
+        rotate(Rt, px, py, pz, rx, ry, rz);
+        float4 s[3];
 #pragma unroll
-            for (int p = 0; p < 3; ++p) {
-                float gx, gy;
-                plane_coords(rx, ry, rz, p, gx, gy);
-                const Tap tp = make_tap(gx, gy, H, W);
-                const float *pc = grid + (long long)(3 * t + p) * planeHWC + c4;
-                const float4 v0 = ldg4(pc + tp.cell[0] * C), v1 = ldg4(pc + tp.cell[1] * C);
-                const float4 v2 = ldg4(pc + tp.cell[2] * C), v3 = ldg4(pc + tp.cell[3] * C);
-                s[p].x = bilerp(tp.w, v0.x, v1.x, v2.x, v3.x);
-                s[p].y = bilerp(tp.w, v0.y, v1.y, v2.y, v3.y);
-                s[p].z = bilerp(tp.w, v0.z, v1.z, v2.z, v3.z);
-                s[p].w = bilerp(tp.w, v0.w, v1.w, v2.w, v3.w);
-            }
-            float4 o;
-            o.x = __fmul_rn(__fmul_rn(s[0].x, s[1].x), s[2].x);
-            o.y = __fmul_rn(__fmul_rn(s[0].y, s[1].y), s[2].y);
-            o.z = __fmul_rn(__fmul_rn(s[0].z, s[1].z), s[2].z);
-            o.w = __fmul_rn(__fmul_rn(s[0].w, s[1].w), s[2].w);
-            __stcs(reinterpret_cast<float4 *>(orow + t * C), o);
+        for (int p = 0; p < 3; ++p) {
+            float gx, gy;
+            plane_coords(rx, ry, rz, p, gx, gy);
+            const Tap tp = make_tap(gx, gy, H, W);
+            const float *pc = g0 + p * planeHWC;
+            const float4 v0 = ldg4(pc + tp.cell[0] * C), v1 = ldg4(pc + tp.cell[1] * C);
+            const float4 v2 = ldg4(pc + tp.cell[2] * C), v3 = ldg4(pc + tp.cell[3] * C);
+            s[p].x = bilerp(tp.w, v0.x, v1.x, v2.x, v3.x);
+            s[p].y = bilerp(tp.w, v0.y, v1.y, v2.y, v3.y);
+            s[p].z = bilerp(tp.w, v0.z, v1.z, v2.z, v3.z);
+            s[p].w = bilerp(tp.w, v0.w, v1.w, v2.w, v3.w);
         }
+        float4 o;
+        o.x = __fmul_rn(__fmul_rn(s[0].x, s[1].x), s[2].x);
+        o.y = __fmul_rn(__fmul_rn(s[0].y, s[1].y), s[2].y);
+        o.z = __fmul_rn(__fmul_rn(s[0].z, s[1].z), s[2].z);
+        o.w = __fmul_rn(__fmul_rn(s[0].w, s[1].w), s[2].w);
+        __stcs(reinterpret_cast<float4 *>(out + b * (long long)(T * C) + t * C + c4), o);
     }
 }
 
@@ -158,27 +169,49 @@ __device__ __forceinline__ float group_sum(float v) {
     return v;
 }
 
+// Bilinear sample, ds/dix and ds/diy of one plane for this lane's 4 channels.
+// (ds/dix = (1-ty)(v1-v0) + ty(v3-v2), ds/diy = (1-tx)(v2-v0) + tx(v3-v1); a
+// clamped +1 corner only changes them where the border mask zeroes the result.)
+template <int C>
+__device__ __forceinline__ void sample_with_slopes(const float *pc, const Tap &tp, float4 &s,
+                                                   float4 &dx, float4 &dy) {
+    const float4 v0 = ldg4(pc + tp.cell[0] * C), v1 = ldg4(pc + tp.cell[1] * C);
+    const float4 v2 = ldg4(pc + tp.cell[2] * C), v3 = ldg4(pc + tp.cell[3] * C);
+    const float tx = tp.tx, ty = tp.ty;
+    s = make_float4(bilerp(tp.w, v0.x, v1.x, v2.x, v3.x), bilerp(tp.w, v0.y, v1.y, v2.y, v3.y),
+                    bilerp(tp.w, v0.z, v1.z, v2.z, v3.z), bilerp(tp.w, v0.w, v1.w, v2.w, v3.w));
+    dx.x = (1.f - ty) * (v1.x - v0.x) + ty * (v3.x - v2.x);
+    dx.y = (1.f - ty) * (v1.y - v0.y) + ty * (v3.y - v2.y);
+    dx.z = (1.f - ty) * (v1.z - v0.z) + ty * (v3.z - v2.z);
+    dx.w = (1.f - ty) * (v1.w - v0.w) + ty * (v3.w - v2.w);
+    dy.x = (1.f - tx) * (v2.x - v0.x) + tx * (v3.x - v1.x);
+    dy.y = (1.f - tx) * (v2.y - v0.y) + tx * (v3.y - v1.y);
+    dy.z = (1.f - tx) * (v2.z - v0.z) + tx * (v3.z - v1.z);
+    dy.w = (1.f - tx) * (v2.w - v0.w) + tx * (v3.w - v1.w);
+}
+
 template <int L>
-__global__ void __launch_bounds__(kThreads) kpt_bwd_v4_kernel(
+__global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
     const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
     const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
     float *__restrict__ gpts, long long B, int T, int H, int W) {
     constexpr int C = 4 * L;
     constexpr int G = 32 / L;
-    extern __shared__ float smem[];
-    float *sR = smem;
-    float *sgR = smem + 9 * T;
-    for (int i = threadIdx.x; i < T * 9; i += blockDim.x) {
-        sR[i] = R[i];
-        sgR[i] = 0.f;
-    }
-    __syncthreads();
+    constexpr int NWARP = kThreads / 32;
+    __shared__ float sred[NWARP][9];
+    const int t = blockIdx.y;
+    float Rt[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) Rt[k] = __ldg(R + 9 * t + k);
 
-    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = lane / L, lis = lane % L, c4 = 4 * lis;
     const long long planeHWC = (long long)H * W * C;
+    const float *g0 = grid + (long long)(3 * t) * planeHWC + c4;
+    float *gg0 = ggrid + (long long)(3 * t) * planeHWC + c4;
     const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    float gr[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // this group's dL/dR_t
 
     for (long long b0 = warp0 * G; b0 < B; b0 += nwarps * G) {
         const long long b_raw = b0 + grp;
@@ -186,106 +219,80 @@ __global__ void __launch_bounds__(kThreads) kpt_bwd_v4_kernel(
         const long long b = active ? b_raw : B - 1;  // keep addresses valid; contributions zeroed
         const float px = __ldg(pts + 3 * b), py = __ldg(pts + 3 * b + 1),
                     pz = __ldg(pts + 3 * b + 2);
-        const float *grow = gout + b * (long long)(T * C) + c4;
-        float gpx = 0.f, gpy = 0.f, gpz = 0.f;
+        float rx, ry, rz;
+        rotate(Rt, px, py, pz, rx, ry, rz);
+        float4 go = __ldcs(reinterpret_cast<const float4 *>(gout + b * (long long)(T * C) + t * C + c4));
+        if (!active) go = make_float4(0.f, 0.f, 0.f, 0.f);
 
-        for (int t = 0; t < T; ++t) {
-            const float *Rt = sR + 9 * t;
-            float rx, ry, rz;
-            rotate(Rt, px, py, pz, rx, ry, rz);
-            float4 go = __ldcs(reinterpret_cast<const float4 *>(grow + t * C));
-            if (!active) go = make_float4(0.f, 0.f, 0.f, 0.f);
-
-            Tap tap[3];
-            float4 s[3], dx[3], dy[3];
+        Tap tap[3];
+        float4 s[3], dx[3], dy[3];
 #pragma unroll
-            for (int p = 0; p < 3; ++p) {
-                float gx, gy;
-                plane_coords(rx, ry, rz, p, gx, gy);
-                tap[p] = make_tap(gx, gy, H, W);
-                const float *pc = grid + (long long)(3 * t + p) * planeHWC + c4;
-                const float4 v0 = ldg4(pc + tap[p].cell[0] * C), v1 = ldg4(pc + tap[p].cell[1] * C);
-                const float4 v2 = ldg4(pc + tap[p].cell[2] * C), v3 = ldg4(pc + tap[p].cell[3] * C);
-                const float *w = tap[p].w;
-                const float tx = tap[p].tx, ty = tap[p].ty;
-                s[p] = make_float4(bilerp(w, v0.x, v1.x, v2.x, v3.x), bilerp(w, v0.y, v1.y, v2.y, v3.y),
-                                   bilerp(w, v0.z, v1.z, v2.z, v3.z), bilerp(w, v0.w, v1.w, v2.w, v3.w));
-                // ds/dix = (1-ty)(v1-v0) + ty(v3-v2);  ds/diy = (1-tx)(v2-v0) + tx(v3-v1)
-                // (clamped +1 corners only differ where the border mask zeroes the result)
-                dx[p].x = (1.f - ty) * (v1.x - v0.x) + ty * (v3.x - v2.x);
-                dx[p].y = (1.f - ty) * (v1.y - v0.y) + ty * (v3.y - v2.y);
-                dx[p].z = (1.f - ty) * (v1.z - v0.z) + ty * (v3.z - v2.z);
-                dx[p].w = (1.f - ty) * (v1.w - v0.w) + ty * (v3.w - v2.w);
-                dy[p].x = (1.f - tx) * (v2.x - v0.x) + tx * (v3.x - v1.x);
-                dy[p].y = (1.f - tx) * (v2.y - v0.y) + tx * (v3.y - v1.y);
-                dy[p].z = (1.f - tx) * (v2.z - v0.z) + tx * (v3.z - v1.z);
-                dy[p].w = (1.f - tx) * (v2.w - v0.w) + tx * (v3.w - v1.w);
-            }
-
-            float dgx[3], dgy[3];
-#pragma unroll
-            for (int p = 0; p < 3; ++p) {
-                const float4 sa = s[(p + 1) % 3], sb = s[(p + 2) % 3];
-                float4 other;
-                other.x = sa.x * sb.x * go.x;
-                other.y = sa.y * sb.y * go.y;
-                other.z = sa.z * sb.z * go.z;
-                other.w = sa.w * sb.w * go.w;
-                float *gpc = ggrid + (long long)(3 * t + p) * planeHWC + c4;
-                if (active) {
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float wk = tap[p].w[k];
-                        if (wk != 0.f)
-                            red_add_v4(gpc + tap[p].cell[k] * C,
-                                       make_float4(other.x * wk, other.y * wk, other.z * wk,
-                                                   other.w * wk));
-                    }
-                }
-                dgx[p] = other.x * dx[p].x + other.y * dx[p].y + other.z * dx[p].z +
-                         other.w * dx[p].w;
-                dgy[p] = other.x * dy[p].x + other.y * dy[p].y + other.z * dy[p].z +
-                         other.w * dy[p].w;
-            }
-#pragma unroll
-            for (int p = 0; p < 3; ++p) {
-                dgx[p] = group_sum<L>(dgx[p]);
-                dgy[p] = group_sum<L>(dgy[p]);
-            }
-            // Back to the rotated point: XY=(rx,ry), ZX=(rz,rx), YZ=(ry,rz).
-            const float drx = dgx[0] * tap[0].gxm + dgy[1] * tap[1].gym;
-            const float dry = dgy[0] * tap[0].gym + dgx[2] * tap[2].gxm;
-            const float drz = dgx[1] * tap[1].gxm + dgy[2] * tap[2].gym;
-            // dL/dp += R_t^T dr
-            gpx += Rt[0] * drx + Rt[3] * dry + Rt[6] * drz;
-            gpy += Rt[1] * drx + Rt[4] * dry + Rt[7] * drz;
-            gpz += Rt[2] * drx + Rt[5] * dry + Rt[8] * drz;
-            // dL/dR_t[i, j] += dr_i * p_j
-            if (active && lis == 0) {
-                float *sg = sgR + 9 * t;
-                atomicAdd(sg + 0, drx * px);
-                atomicAdd(sg + 1, drx * py);
-                atomicAdd(sg + 2, drx * pz);
-                atomicAdd(sg + 3, dry * px);
-                atomicAdd(sg + 4, dry * py);
-                atomicAdd(sg + 5, dry * pz);
-                atomicAdd(sg + 6, drz * px);
-                atomicAdd(sg + 7, drz * py);
-                atomicAdd(sg + 8, drz * pz);
-            }
+        for (int p = 0; p < 3; ++p) {
+            float gx, gy;
+            plane_coords(rx, ry, rz, p, gx, gy);
+            tap[p] = make_tap(gx, gy, H, W);
+            sample_with_slopes<C>(g0 + p * planeHWC, tap[p], s[p], dx[p], dy[p]);
         }
+
+        float dgx[3], dgy[3];
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+            const float4 sa = s[(p + 1) % 3], sb = s[(p + 2) % 3];
+            float4 other;
+            other.x = sa.x * sb.x * go.x;
+            other.y = sa.y * sb.y * go.y;
+            other.z = sa.z * sb.z * go.z;
+            other.w = sa.w * sb.w * go.w;
+            float *gpc = gg0 + p * planeHWC;
+            if (active) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float wk = tap[p].w[k];
+                    if (wk != 0.f)
+                        red_add_v4(gpc + tap[p].cell[k] * C,
+                                   make_float4(other.x * wk, other.y * wk, other.z * wk, other.w * wk));
+                }
+            }
+            dgx[p] = other.x * dx[p].x + other.y * dx[p].y + other.z * dx[p].z + other.w * dx[p].w;
+            dgy[p] = other.x * dy[p].x + other.y * dy[p].y + other.z * dy[p].z + other.w * dy[p].w;
+        }
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+            dgx[p] = group_sum<L>(dgx[p]);
+            dgy[p] = group_sum<L>(dgy[p]);
+        }
+        // Back to the rotated point: XY=(rx,ry), ZX=(rz,rx), YZ=(ry,rz).
+        const float drx = dgx[0] * tap[0].gxm + dgy[1] * tap[1].gym;
+        const float dry = dgy[0] * tap[0].gym + dgx[2] * tap[2].gxm;
+        const float drz = dgx[1] * tap[1].gxm + dgy[2] * tap[2].gym;
         if (active && lis == 0) {
-            // This group alone owns point b: plain read-modify-write accumulates.
-            float *gp = gpts + 3 * b;
-            gp[0] += gpx;
-            gp[1] += gpy;
-            gp[2] += gpz;
+            // dL/dp += R_t^T dr (the point's T rotations run in different blocks)
+            atomicAdd(gpts + 3 * b, Rt[0] * drx + Rt[3] * dry + Rt[6] * drz);
+            atomicAdd(gpts + 3 * b + 1, Rt[1] * drx + Rt[4] * dry + Rt[7] * drz);
+            atomicAdd(gpts + 3 * b + 2, Rt[2] * drx + Rt[5] * dry + Rt[8] * drz);
+            // dL/dR_t[i, j] += dr_i * p_j, kept in registers
+            gr[0] += drx * px; gr[1] += drx * py; gr[2] += drx * pz;
+            gr[3] += dry * px; gr[4] += dry * py; gr[5] += dry * pz;
+            gr[6] += drz * px; gr[7] += drz * py; gr[8] += drz * pz;
         }
     }
 
+    // grad_R: groups of the warp (lanes 0, L, 2L, ...) then warps of the block,
+    // then one reduction per entry per block.
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+        float v = gr[k];
+#pragma unroll
+        for (int off = L; off < 32; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) sred[warp][k] = v;
+    }
     __syncthreads();
-    for (int i = threadIdx.x; i < T * 9; i += blockDim.x)
-        if (sgR[i] != 0.f) atomicAdd(gR + i, sgR[i]);
+    if (threadIdx.x < 9) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < NWARP; ++w) v += sred[w][threadIdx.x];
+        if (v != 0.f) atomicAdd(gR + 9 * t + threadIdx.x, v);
+    }
 }
 
 // ── generic path: any C (scalar channels, one warp per point) ─────────────
@@ -478,16 +485,31 @@ int grid_size(long long work_warps, int *grid) {
     return 0;
 }
 
+// Blocks per rotation for the rotation-major grids: about two waves of
+// resident blocks (so that one rotation's blocks fill the GPU before the next
+// rotation starts), never more than the point tiles.
+int rotation_grid_x(long long work_warps, int blocks_per_sm, int *gx) {
+    int sms = 0;
+    if (int st = device_sm_count(&sms)) return st;
+    const long long warps_per_block = kThreads / 32;
+    long long need = (work_warps + warps_per_block - 1) / warps_per_block;
+    long long cap = 2LL * sms * blocks_per_sm;
+    long long x = need < cap ? need : cap;
+    if (x < 1) x = 1;
+    *gx = (int)x;
+    return 0;
+}
+
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <int L>
 int fwd_v4(const float *pts, const float *R, const float *grid, float *out, long long B, int T,
            int H, int W, cudaStream_t stream) {
     constexpr int G = 32 / L;
-    int blocks = 0;
-    if (int st = grid_size((B + G - 1) / G, &blocks)) return st;
-    kpt_fwd_v4_kernel<L><<<blocks, kThreads, 9 * T * sizeof(float), stream>>>(pts, R, grid, out,
-                                                                              B, T, H, W);
+    int gx = 0;
+    if (int st = rotation_grid_x((B + G - 1) / G, 8, &gx)) return st;
+    QC_RETURN_IF(T > 65535, QC_ERR_INVALID_ARGUMENT, "kplanes: T=%d exceeds 65535", T);
+    kpt_fwd_v4_kernel<L><<<dim3(gx, T), kThreads, 0, stream>>>(pts, R, grid, out, B, T, H, W);
     QC_CHECK_LAUNCH("kpt_fwd_v4_kernel launch");
     return 0;
 }
@@ -496,10 +518,11 @@ template <int L>
 int bwd_v4(const float *pts, const float *R, const float *grid, const float *gout, float *ggrid,
            float *gR, float *gpts, long long B, int T, int H, int W, cudaStream_t stream) {
     constexpr int G = 32 / L;
-    int blocks = 0;
-    if (int st = grid_size((B + G - 1) / G, &blocks)) return st;
-    kpt_bwd_v4_kernel<L><<<blocks, kThreads, 18 * T * sizeof(float), stream>>>(
-        pts, R, grid, gout, ggrid, gR, gpts, B, T, H, W);
+    int gx = 0;
+    if (int st = rotation_grid_x((B + G - 1) / G, kBwdMinBlocks, &gx)) return st;
+    QC_RETURN_IF(T > 65535, QC_ERR_INVALID_ARGUMENT, "kplanes: T=%d exceeds 65535", T);
+    kpt_bwd_v4_kernel<L><<<dim3(gx, T), kThreads, 0, stream>>>(pts, R, grid, gout, ggrid, gR, gpts,
+                                                                B, T, H, W);
     QC_CHECK_LAUNCH("kpt_bwd_v4_kernel launch");
     return 0;
 }
