@@ -1,6 +1,6 @@
 """Python access to the CPU oracle (TEST INFRASTRUCTURE ONLY).
 
-This module is the parity checker: it wraps the C restatement of the
+This module is the oracle: it wraps the C restatement of the
 reference kernels (``tv_oracle.c``, ``kplanes_oracle.c``) and, when it has
 been built, the reference's own ``_core`` extension compiled from its sources
 into ``_ref/``. Only the tests, ``__graft_entry__.smoke()`` and the CPU-baseline

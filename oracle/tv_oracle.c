@@ -1,7 +1,7 @@
 /* tv_oracle.c — CPU oracle for the 3-D total-variation losses and gradients.
  *
- * TEST INFRASTRUCTURE ONLY. This file is the parity checker for the CUDA
- * kernels; nothing in the product links, loads or calls it. Only the tests,
+ * TEST INFRASTRUCTURE ONLY. This file is the oracle the CUDA
+ * kernels are tested against; nothing in the product links, loads or calls it. Only the tests,
  * the smoke check and the CPU-baseline leg of the benchmark use it.
  *
  * It restates, term by term, the reference kernels in

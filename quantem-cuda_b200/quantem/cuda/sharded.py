@@ -18,7 +18,7 @@ natural sharding of the work:
 
 The per-rank compute defaults to the CUDA kernels. ``slab_kernel`` exists so
 that the host logic (halo exchange, ownership flags, reductions) can be tested
-on CPU ranks with a checker in place of the device kernel.
+on CPU ranks with the CPU oracle in place of the device kernel.
 """
 
 from __future__ import annotations
