@@ -115,6 +115,21 @@ int tv_loss_l1_3d_fwd_grad_cuda(const float *d_vol, const float *d_g, float *d_a
                                 float *d_grad_vol, int B, int D, int H, int W, void *d_workspace,
                                 size_t workspace_bytes, cudaStream_t stream);
 
+/* tv_loss_iso_3d_fwd_grad_cuda for callers that cannot allocate device memory
+ * (code running where allocating or synchronising CUDA calls are not allowed,
+ * or whose device memory is owned up front by another allocator). No
+ * counterpart in the reference. The reduction scratch is a 48 KiB array
+ * statically allocated in the library's device code (held by every GPU that
+ * loads the library until exit); it covers every volume shape, and a request
+ * for more scratch than it holds is rejected with QC_ERR_WORKSPACE_TOO_SMALL.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current): make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU (other
+ * streams, other threads) race; nothing in it needs to start at zero. */
+int tv_loss_iso_3d_fwd_grad_noalloc_cuda(const float *d_vol, const float *d_g_scaled, float *d_acc,
+                                         float *d_grad_vol, int B, int D, int H, int W, float eps,
+                                         cudaStream_t stream);
+
 /* General D-slab form behind all TV entries, used directly by the sharded
  * (multi-GPU) path. The volume holds Dp physical planes per batch slice; planes
  * [d_lo, d_hi) are owned. has_prev / has_next say whether plane d_lo-1 / d_hi is

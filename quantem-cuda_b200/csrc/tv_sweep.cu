@@ -952,3 +952,61 @@ int quantem_cuda_device_fault_word(int device, unsigned int *word, int clear) {
 }
 
 }  // extern "C"
+
+// ── isotropic single sweep for callers that cannot allocate ────────────────
+//
+// Some callers of this library cannot call cudaMalloc (or any allocating
+// routine) at the point where they need the loss: code that runs inside a
+// host callback or another context where CUDA calls that may synchronise are
+// not allowed, and applications whose device memory is owned up front by a
+// single allocator (a framework's caching allocator, a fixed memory budget)
+// that another cudaMalloc would defeat or fail against. For them the
+// workspace of the deterministic reduction lives in this file instead: a
+// statically allocated device array, present on every GPU that loads the
+// library until the process exits.
+
+namespace qc {
+namespace tv {
+
+// 2048 CTA partial-sum slots × 3 fp64 = 48 KiB: the most the sweep planner
+// uses for any volume shape (its grid is capped at kMaxPartials CTAs).
+static __device__ __align__(256) double g_static_partials[kMaxPartials * kAccSlots];
+
+// Device address of g_static_partials on the current device. The host-side
+// name is only a stand-in for the array, so it must be translated once per
+// device, with that device current, before a kernel may be given it.
+int static_partials_address(double **out) {
+    static std::mutex mu;
+    static double *addr[64] = {nullptr};
+    int dev = 0;
+    QC_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && addr[dev] != nullptr) {
+        *out = addr[dev];
+        return 0;
+    }
+    double *p = nullptr;
+    QC_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&p), g_static_partials),
+                "cudaGetSymbolAddress(static TV scratch)");
+    if (dev >= 0 && dev < 64) addr[dev] = p;
+    *out = p;
+    return 0;
+}
+
+}  // namespace tv
+}  // namespace qc
+
+extern "C" int tv_loss_iso_3d_fwd_grad_noalloc_cuda(const float *d_vol, const float *d_g_scaled,
+                                                    float *d_acc, float *d_grad_vol, int B, int D,
+                                                    int H, int W, float eps, cudaStream_t stream) {
+    const size_t have = sizeof(qc::tv::g_static_partials);
+    const size_t need = tv_loss_3d_workspace_bytes(B, D, H, W);
+    QC_RETURN_IF(need > have, QC_ERR_WORKSPACE_TOO_SMALL,
+                 "tv_loss_iso_3d_fwd_grad_noalloc_cuda: [%d, %d, %d, %d] needs %zu bytes of "
+                 "scratch; the static scratch holds %zu",
+                 B, D, H, W, need, have);
+    double *scratch = nullptr;
+    if (int st = qc::tv::static_partials_address(&scratch)) return st;
+    return qc::tv::run(QC_TV_ISO, QC_TV_LOSS | QC_TV_GRAD, d_vol, d_g_scaled, d_acc, d_grad_vol, B,
+                       D, H, W, 0, D, 0, 0, eps, 1.0f, scratch, have, stream);
+}
