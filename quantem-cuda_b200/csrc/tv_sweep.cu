@@ -267,6 +267,66 @@ __device__ __forceinline__ float comp(const float4 &v, int j) {
     return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
 }
 
+// g·sign(d) with sign(0) = 0, as a sign transfer: g with its sign bit flipped
+// where d < 0 (one logic op) and a zero test.
+__device__ __forceinline__ float gsign_fast(float g, float d) {
+    const float f = __int_as_float((__float_as_int(d) & 0x80000000) ^ __float_as_int(g));
+    return d != 0.f ? f : 0.f;
+}
+
+// Loss terms and flux of the 4 voxels of one row of a lane (fast path).
+// Missing +D/+H/+W neighbours have already been replaced by the voxel itself
+// (edge replication) and out-of-volume voxels read as zero, so every invalid
+// squared or L1 term is an exact zero difference and needs no mask. For iso a
+// corner without all three neighbours carries eps = +inf: rsqrt(+inf) = 0
+// zeroes its flux, and its loss (s = x·rsqrt(x), not finite) is dropped by the
+// caller's row-level select or, for the 4th voxel, by s3_ok.
+template <int V, bool LOSS, bool GRAD>
+__device__ __forceinline__ void row_flux4(const float4 &c, const float4 &n, const float4 &dn,
+                                          float right, float eps_row, float eps3, bool s3_ok,
+                                          const Gains &gn, float Fd[4], float Fh[4], float Fw[4],
+                                          float &r0, float &r1, float &r2) {
+    const float cv[4] = {c.x, c.y, c.z, c.w};
+    const float nv[4] = {n.x, n.y, n.z, n.w};
+    const float hv[4] = {dn.x, dn.y, dn.z, dn.w};
+    const float wv[4] = {c.y, c.z, c.w, right};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float dd = nv[j] - cv[j], dh = hv[j] - cv[j], dw = wv[j] - cv[j];
+        if constexpr (V == QC_TV_SQ) {
+            if (LOSS) r0 = __fmaf_rn(dw, dw, __fmaf_rn(dh, dh, __fmaf_rn(dd, dd, r0)));
+            if (GRAD) {
+                Fd[j] = dd;
+                Fh[j] = dh;
+                Fw[j] = dw;
+            }
+        } else if constexpr (V == QC_TV_L1) {
+            if (LOSS) {
+                r0 += fabsf(dd);
+                r1 += fabsf(dh);
+                r2 += fabsf(dw);
+            }
+            if (GRAD) {
+                Fd[j] = gsign_fast(gn.gd, dd);
+                Fh[j] = gsign_fast(gn.gh, dh);
+                Fw[j] = gsign_fast(gn.gw, dw);
+            }
+        } else {
+            const float x = dd * dd + dh * dh + dw * dw + (j == 3 ? eps3 : eps_row);
+            const float r = rsqrt_approx(x);
+            if (LOSS) {
+                const float sv = x * r;
+                r0 += (j < 3 || s3_ok) ? sv : 0.f;
+            }
+            if (GRAD) {
+                Fd[j] = dd * r;
+                Fh[j] = dh * r;
+                Fw[j] = dw * r;
+            }
+        }
+    }
+}
+
 template <int V, bool LOSS, bool GRAD, class G>
 __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
     const __grid_constant__ CUtensorMap map, const float *__restrict__ g,
@@ -336,6 +396,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
         const int r0 = warp * R;             // first tile row of this warp's strip
         const int scol = kHaloW + 4 * lane;  // smem column of this lane's first voxel
         const size_t plane_elems = (size_t)pl.H * pl.W;
+        const float kInf = __int_as_float(0x7f800000);
         float Fd_prev[R][4];
         int seq = 0;
 
@@ -343,12 +404,13 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
             const Unit U = decode_unit<GRAD>(pl, u, G::TileH, kTileW);
             const int wcol = U.w0 + 4 * lane;  // global column of the lane's first voxel
             const int hbase = U.h0 + r0;       // global row of the strip's first row
-            // Per-unit masks (constant along D).
-            const bool col_in = wcol < pl.W;   // W % 4 == 0: the 4 voxels are all in or all out
-            bool vw[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) vw[j] = wcol + j + 1 < pl.W;
+            // Per-unit lane facts (constant along D). W % 4 == 0, so a lane's 4
+            // voxels are all inside or all outside, and only the 4th can lack
+            // its +W neighbour.
+            const bool lane_in = wcol < pl.W;
+            const bool last_quad = wcol + 4 == pl.W;
             const bool has_up = hbase >= 1;
+            const float eps_lane = lane_in ? pl.eps : kInf;
             // Lanes stand for rows when computing the left halo column.
             const int hrow = r0 + (lane < R ? lane : R - 1);  // tile row
             const bool hrow_vh = U.h0 + hrow + 1 < pl.H;
@@ -383,28 +445,28 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                 }
                 if (aborted(sm)) break;
                 const bool owned = p >= U.d_start;
+                const float eps_step = has_nxt ? eps_lane : kInf;
                 float l0 = 0.f, l1 = 0.f, l2 = 0.f;
 
                 if (!owned) {
                     // Halo plane below the chunk: only Fd is needed, for the
-                    // first owned plane's backward difference.
+                    // first owned plane's backward difference (plane p+1 exists).
                     if (GRAD) {
                         float4 cur = lds4(Sc, r0 + 1, scol);
 #pragma unroll
                         for (int i = 0; i < R; ++i) {
+                            const bool row_ok = hbase + i + 1 < pl.H;
                             const float4 down = lds4(Sc, r0 + i + 2, scol);
                             const float4 nxt = lds4(Sn, r0 + i + 1, scol);
                             float right = __shfl_down_sync(0xffffffffu, cur.x, 1);
                             if (lane == 31) right = lds1(Sc, r0 + i + 1, scol + 4);
-                            const bool vh = hbase + i + 1 < pl.H;
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                float Fh, Fw, d0 = 0.f, d1 = 0.f, d2 = 0.f;
-                                voxel_flux<V, false, true>(comp(cur, j), comp(nxt, j), comp(down, j),
-                                                           j < 3 ? comp(cur, j + 1) : right, true, vh,
-                                                           vw[j], false, pl.eps, gn, Fd_prev[i][j],
-                                                           Fh, Fw, d0, d1, d2);
-                            }
+                            if (last_quad) right = cur.w;
+                            const float4 dn = row_ok ? down : cur;
+                            const float eps_row = row_ok ? eps_step : kInf;
+                            float Fh[4], Fw[4], d0 = 0.f, d1 = 0.f, d2 = 0.f;
+                            row_flux4<V, false, true>(cur, nxt, dn, right, eps_row,
+                                                      last_quad ? kInf : eps_row, false, gn,
+                                                      Fd_prev[i], Fh, Fw, d0, d1, d2);
                             cur = down;
                         }
                     }
@@ -422,44 +484,61 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                         fw_halo = flux_from_left<V>(v0, lf, lf_nd, lf_nh, halo_left, has_nxt,
                                                     hrow_vh, pl.eps, gn);
                     }
-                    // Row above the strip (tile row r0-1 is smem row r0).
                     float4 cur = lds4(Sc, r0 + 1, scol);
+                    // Row above the strip (tile row r0-1 is smem row r0); at the
+                    // top of the volume it is replaced by the strip's first row.
                     float Fh_up[4] = {0.f, 0.f, 0.f, 0.f};
                     if (GRAD) {
-                        const float4 up = lds4(Sc, r0, scol);
-                        float4 up_nd = make_float4(0.f, 0.f, 0.f, 0.f);
-                        float up_right = 0.f;
-                        if (V == QC_TV_ISO) {
-                            up_nd = lds4(Sn, r0, scol);
-                            up_right = __shfl_down_sync(0xffffffffu, up.x, 1);
+                        const float4 up = has_up ? lds4(Sc, r0, scol) : cur;
+                        if constexpr (V == QC_TV_ISO) {
+                            const float4 up_nd = has_nxt ? lds4(Sn, r0, scol) : up;
+                            float up_right = __shfl_down_sync(0xffffffffu, up.x, 1);
                             if (lane == 31) up_right = lds1(Sc, r0, scol + 4);
+                            if (last_quad) up_right = up.w;
+                            const float e_up = has_up ? eps_step : kInf;
+                            float Fd_u[4], Fw_u[4], d0 = 0.f, d1 = 0.f, d2 = 0.f;
+                            row_flux4<V, false, true>(up, up_nd, cur, up_right, e_up,
+                                                      last_quad ? kInf : e_up, false, gn, Fd_u,
+                                                      Fh_up, Fw_u, d0, d1, d2);
+                        } else if constexpr (V == QC_TV_SQ) {
+                            Fh_up[0] = cur.x - up.x;
+                            Fh_up[1] = cur.y - up.y;
+                            Fh_up[2] = cur.z - up.z;
+                            Fh_up[3] = cur.w - up.w;
+                        } else {
+                            Fh_up[0] = gsign_fast(gn.gh, cur.x - up.x);
+                            Fh_up[1] = gsign_fast(gn.gh, cur.y - up.y);
+                            Fh_up[2] = gsign_fast(gn.gh, cur.z - up.z);
+                            Fh_up[3] = gsign_fast(gn.gh, cur.w - up.w);
                         }
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            Fh_up[j] = flux_from_up<V>(comp(cur, j), comp(up, j), comp(up_nd, j),
-                                                       j < 3 ? comp(up, j + 1) : up_right, has_up,
-                                                       has_nxt, vw[j], pl.eps, gn);
                     }
 
                     float *gp = gbase + (size_t)p * plane_elems;
 #pragma unroll
                     for (int i = 0; i < R; ++i) {
                         const int h = hbase + i;
-                        const bool row_in = h < pl.H;
-                        const bool vh = h + 1 < pl.H;
+                        const bool row_ok = h + 1 < pl.H;  // row has a +H neighbour
                         const float4 down = lds4(Sc, r0 + i + 2, scol);
-                        const float4 nxt =
-                            has_nxt ? lds4(Sn, r0 + i + 1, scol) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float4 nxt = has_nxt ? lds4(Sn, r0 + i + 1, scol) : cur;
                         float right = __shfl_down_sync(0xffffffffu, cur.x, 1);
                         if (lane == 31) right = lds1(Sc, r0 + i + 1, scol + 4);
-                        const bool own = row_in && col_in;
+                        if (last_quad) right = cur.w;
+                        const float4 dn = row_ok ? down : cur;
+                        const float eps_row = row_ok ? eps_step : kInf;
                         float Fd[4], Fh[4], Fw[4];
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            voxel_flux<V, LOSS, GRAD>(comp(cur, j), comp(nxt, j), comp(down, j),
-                                                      j < 3 ? comp(cur, j + 1) : right, has_nxt, vh,
-                                                      vw[j], own, pl.eps, gn, Fd[j], Fh[j], Fw[j],
-                                                      l0, l1, l2);
+                        float q0l = 0.f, q1l = 0.f, q2l = 0.f;
+                        row_flux4<V, LOSS, GRAD>(cur, nxt, dn, right, eps_row,
+                                                 last_quad ? kInf : eps_row, !last_quad, gn, Fd,
+                                                 Fh, Fw, q0l, q1l, q2l);
+                        if (LOSS) {
+                            if constexpr (V == QC_TV_ISO) {
+                                l0 += (row_ok && has_nxt && lane_in) ? q0l : 0.f;
+                            } else {
+                                l0 += q0l;
+                                l1 += q1l;
+                                l2 += q2l;
+                            }
+                        }
                         if (GRAD) {
                             const float fw_from_lane = __shfl_up_sync(0xffffffffu, Fw[3], 1);
                             const float fw_from_halo = __shfl_sync(0xffffffffu, fw_halo, i);
@@ -469,7 +548,8 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                             gv.y = gn.gmul * ((Fd_prev[i][1] - Fd[1]) + (Fh_up[1] - Fh[1]) + (Fw[0] - Fw[1]));
                             gv.z = gn.gmul * ((Fd_prev[i][2] - Fd[2]) + (Fh_up[2] - Fh[2]) + (Fw[1] - Fw[2]));
                             gv.w = gn.gmul * ((Fd_prev[i][3] - Fd[3]) + (Fh_up[3] - Fh[3]) + (Fw[2] - Fw[3]));
-                            if (own) __stcs(reinterpret_cast<float4 *>(gp + (size_t)i * pl.W), gv);
+                            if (lane_in && h < pl.H)
+                                __stcs(reinterpret_cast<float4 *>(gp + (size_t)i * pl.W), gv);
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
                                 Fd_prev[i][j] = Fd[j];
