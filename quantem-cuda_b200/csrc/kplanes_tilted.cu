@@ -450,6 +450,83 @@ __global__ void __launch_bounds__(kTT * 8) transpose_kernel(const float *__restr
     }
 }
 
+// Fast form for R % 4 == 0, S % 4 == 0 and 16-byte aligned pointers: tiles of
+// 32 rows (channels) × 128 columns (cells), 16-byte loads and stores on both
+// sides. The shared tile keeps element (c, x) at c·132 + (x ^ 4·((c/4) % 8)):
+// float4 groups stay together for the row-wise side, and the column-wise side
+// (lanes reading 4 consecutive rows of 8 columns) hits 32 distinct banks.
+constexpr int kTC = 32, kTS = 128, kTStride = kTS + 4;
+
+__device__ __forceinline__ int tswz(int c, int x) {
+    return c * kTStride + (x ^ (((c >> 2) & 7) << 2));
+}
+
+// TO_CL: [P, R, S] -> [P, S, R]; otherwise [P, S, R] -> [P, R, S].
+template <bool TO_CL>
+__global__ void __launch_bounds__(256) transpose_tile_kernel(const float *__restrict__ src,
+                                                            float *__restrict__ dst, int R, int S) {
+    __shared__ __align__(16) float tile[kTC * kTStride];
+    const long long base = (long long)blockIdx.z * R * S;
+    const int s0 = blockIdx.x * kTS, c0 = blockIdx.y * kTC;
+    const int t = threadIdx.x;
+    if (TO_CL) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int f = t + 256 * k;
+            const int c = f >> 5, x = (f & 31) * 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c0 + c < R && s0 + x < S)
+                v = __ldcs(reinterpret_cast<const float4 *>(src + base + (long long)(c0 + c) * S + s0 + x));
+            *reinterpret_cast<float4 *>(&tile[tswz(c, x)]) = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int f = t + 256 * k;
+            const int j = f >> 3, c = 4 * (f & 7);
+            if (s0 + j < S && c0 + c < R) {
+                const float4 v = make_float4(tile[tswz(c, j)], tile[tswz(c + 1, j)],
+                                             tile[tswz(c + 2, j)], tile[tswz(c + 3, j)]);
+                *reinterpret_cast<float4 *>(dst + base + (long long)(s0 + j) * R + c0 + c) = v;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int f = t + 256 * k;
+            const int j = f >> 3, c = 4 * (f & 7);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (s0 + j < S && c0 + c < R)
+                v = __ldcs(reinterpret_cast<const float4 *>(src + base + (long long)(s0 + j) * R + c0 + c));
+            tile[tswz(c, j)] = v.x;
+            tile[tswz(c + 1, j)] = v.y;
+            tile[tswz(c + 2, j)] = v.z;
+            tile[tswz(c + 3, j)] = v.w;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int f = t + 256 * k;
+            const int c = f >> 5, x = (f & 31) * 4;
+            if (c0 + c < R && s0 + x < S)
+                *reinterpret_cast<float4 *>(dst + base + (long long)(c0 + c) * S + s0 + x) =
+                    *reinterpret_cast<const float4 *>(&tile[tswz(c, x)]);
+        }
+    }
+}
+
+int launch_transpose_fast(const float *src, float *dst, int P, int R, int S, bool to_cl,
+                          cudaStream_t stream) {
+    const dim3 grid((S + kTS - 1) / kTS, (R + kTC - 1) / kTC, P);
+    QC_RETURN_IF(grid.y > 65535, QC_ERR_INVALID_ARGUMENT, "transpose: channel extent too large");
+    if (to_cl)
+        transpose_tile_kernel<true><<<grid, 256, 0, stream>>>(src, dst, R, S);
+    else
+        transpose_tile_kernel<false><<<grid, 256, 0, stream>>>(src, dst, R, S);
+    QC_CHECK_LAUNCH("transpose_tile_kernel launch");
+    return 0;
+}
+
 int launch_transpose(const float *src, float *dst, int P, int Rn, int Sn, cudaStream_t stream) {
     QC_RETURN_IF(P < 0 || Rn < 0 || Sn < 0, QC_ERR_INVALID_ARGUMENT, "transpose: negative shape");
     if ((long long)P * Rn * Sn == 0) return 0;
@@ -594,16 +671,30 @@ int kplanes_tilted_fuse_grad_cuda(const float *d_pts, const float *d_R, const fl
 
 int kplanes_planes_to_channels_last_cuda(const float *d_src, float *d_dst, int P, int C, int H,
                                          int W, cudaStream_t stream) {
+    QC_RETURN_IF(P < 0 || C < 0 || H < 0 || W < 0, QC_ERR_INVALID_ARGUMENT,
+                 "kplanes_planes_to_channels_last_cuda: negative shape");
     QC_RETURN_IF((long long)H * W >= (1LL << 31), QC_ERR_INVALID_ARGUMENT,
                  "kplanes_planes_to_channels_last_cuda: H*W too large");
-    return qc::kp::launch_transpose(d_src, d_dst, P, C, H * W, stream);
+    const int S = H * W;
+    if ((long long)P * C * S == 0) return 0;
+    QC_RETURN_IF(P > 65535, QC_ERR_INVALID_ARGUMENT, "transpose: more than 65535 planes");
+    if (C % 4 == 0 && S % 4 == 0 && qc::kp::aligned16(d_src) && qc::kp::aligned16(d_dst))
+        return qc::kp::launch_transpose_fast(d_src, d_dst, P, C, S, true, stream);
+    return qc::kp::launch_transpose(d_src, d_dst, P, C, S, stream);
 }
 
 int kplanes_planes_from_channels_last_cuda(const float *d_src, float *d_dst, int P, int C, int H,
                                            int W, cudaStream_t stream) {
+    QC_RETURN_IF(P < 0 || C < 0 || H < 0 || W < 0, QC_ERR_INVALID_ARGUMENT,
+                 "kplanes_planes_from_channels_last_cuda: negative shape");
     QC_RETURN_IF((long long)H * W >= (1LL << 31), QC_ERR_INVALID_ARGUMENT,
                  "kplanes_planes_from_channels_last_cuda: H*W too large");
-    return qc::kp::launch_transpose(d_src, d_dst, P, H * W, C, stream);
+    const int S = H * W;
+    if ((long long)P * C * S == 0) return 0;
+    QC_RETURN_IF(P > 65535, QC_ERR_INVALID_ARGUMENT, "transpose: more than 65535 planes");
+    if (C % 4 == 0 && S % 4 == 0 && qc::kp::aligned16(d_src) && qc::kp::aligned16(d_dst))
+        return qc::kp::launch_transpose_fast(d_src, d_dst, P, C, S, false, stream);
+    return qc::kp::launch_transpose(d_src, d_dst, P, S, C, stream);
 }
 
 }  // extern "C"

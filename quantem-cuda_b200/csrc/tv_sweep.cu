@@ -76,6 +76,13 @@ __device__ __forceinline__ float rsqrt_approx(float x) {
     return y;
 }
 
+// dd² + dh² + dw² + eps with one fixed FMA chain, used by every path (scalar,
+// paired, halo) so that a corner evaluates to the same bits wherever it is
+// computed.
+__device__ __forceinline__ float iso_x(float dd, float dh, float dw, float eps) {
+    return __fmaf_rn(dw, dw, __fmaf_rn(dh, dh, __fmaf_rn(dd, dd, eps)));
+}
+
 // g·sign(x) with sign(0) = 0: torch's convention for d|x|/dx (tv_loss.cu:434-436).
 __device__ __forceinline__ float gsign(float g, float x) {
     return x > 0.f ? g : (x < 0.f ? -g : 0.f);
@@ -119,7 +126,7 @@ __device__ __forceinline__ void voxel_flux(float v, float nd, float nh, float nw
         }
     } else {  // QC_TV_ISO
         const bool ok = vd && vh && vw;
-        const float x = dd * dd + dh * dh + dw * dw + eps;
+        const float x = iso_x(dd, dh, dw, eps);
         if (LOSS) l0 += (ok && own) ? sqrt_approx(x) : 0.f;
         if (GRAD) {
             const float inv = ok ? rsqrt_approx(x) : 0.f;
@@ -144,7 +151,7 @@ __device__ __forceinline__ float flux_from_up(float v, float up, float up_nd, fl
     } else {
         const bool ok = has_up && vd && vw_up;
         const float dd = up_nd - up, dw = up_nw - up;
-        const float inv = ok ? rsqrt_approx(dd * dd + dh * dh + dw * dw + eps) : 0.f;
+        const float inv = ok ? rsqrt_approx(iso_x(dd, dh, dw, eps)) : 0.f;
         return dh * inv;
     }
 }
@@ -163,7 +170,7 @@ __device__ __forceinline__ float flux_from_left(float v, float lf, float lf_nd, 
     } else {
         const bool ok = has_left && vd && vh;
         const float dd = lf_nd - lf, dh = lf_nh - lf;
-        const float inv = ok ? rsqrt_approx(dd * dd + dh * dh + dw * dw + eps) : 0.f;
+        const float inv = ok ? rsqrt_approx(iso_x(dd, dh, dw, eps)) : 0.f;
         return dw * inv;
     }
 }
@@ -274,6 +281,123 @@ __device__ __forceinline__ float gsign_fast(float g, float d) {
     return d != 0.f ? f : 0.f;
 }
 
+// ── packed fp32 pairs ─────────────────────────────────────────────────────
+// sm_100 executes two fp32 adds/multiplies/FMAs per instruction on a 64-bit
+// register pair (add/sub/mul/fma.rn.f32x2). A lane's 4 voxels arrive from
+// shared memory as two such pairs, (v0, v1) and (v2, v3); arithmetic that is
+// the same for all four runs on the pairs, and only the views shifted by one
+// column need packing moves.
+typedef unsigned long long f2;
+
+__device__ __forceinline__ f2 pk2(float lo, float hi) {
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float lo2(f2 v) {
+    float a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+    return a;
+}
+__device__ __forceinline__ float hi2(f2 v) {
+    float a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+    return b;
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+    f2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+    f2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ ulonglong2 lds_pairs(const float *s, int row, int col) {
+    return *reinterpret_cast<const ulonglong2 *>(s + row * kBoxW + col);
+}
+__device__ __forceinline__ void stcs_pairs(float *p, f2 a, f2 b) {
+    asm volatile("st.global.cs.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+// Loss terms and fluxes of one row of a lane's 4 voxels as pairs (c01, c23),
+// with edge-replicated neighbours as in row_flux4 below. The loss
+// accumulators are pairs (a01, a23) for SQ/iso, scalars for L1.
+template <int V, bool LOSS, bool GRAD>
+__device__ __forceinline__ void row_flux_pairs(const ulonglong2 &c, const ulonglong2 &n,
+                                               const ulonglong2 &dn, float right, f2 eps01,
+                                               f2 eps23, bool s3_ok, const Gains &gn,
+                                               ulonglong2 &Fd, ulonglong2 &Fh, ulonglong2 &Fw,
+                                               f2 &acc01, f2 &acc23, float &r1, float &r2) {
+    const f2 dd01 = sub2(n.x, c.x), dd23 = sub2(n.y, c.y);
+    const f2 dh01 = sub2(dn.x, c.x), dh23 = sub2(dn.y, c.y);
+    const f2 w01 = pk2(hi2(c.x), lo2(c.y)), w23 = pk2(hi2(c.y), right);
+    const f2 dw01 = sub2(w01, c.x), dw23 = sub2(w23, c.y);
+    if constexpr (V == QC_TV_SQ) {
+        if (LOSS) {
+            acc01 = fma2(dd01, dd01, acc01);
+            acc01 = fma2(dh01, dh01, acc01);
+            acc01 = fma2(dw01, dw01, acc01);
+            acc23 = fma2(dd23, dd23, acc23);
+            acc23 = fma2(dh23, dh23, acc23);
+            acc23 = fma2(dw23, dw23, acc23);
+        }
+        if (GRAD) {
+            Fd = make_ulonglong2(dd01, dd23);
+            Fh = make_ulonglong2(dh01, dh23);
+            Fw = make_ulonglong2(dw01, dw23);
+        }
+    } else if constexpr (V == QC_TV_L1) {
+        const float dd[4] = {lo2(dd01), hi2(dd01), lo2(dd23), hi2(dd23)};
+        const float dh[4] = {lo2(dh01), hi2(dh01), lo2(dh23), hi2(dh23)};
+        const float dw[4] = {lo2(dw01), hi2(dw01), lo2(dw23), hi2(dw23)};
+        if (LOSS) {
+            float a0 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                a0 += fabsf(dd[j]);
+                r1 += fabsf(dh[j]);
+                r2 += fabsf(dw[j]);
+            }
+            acc01 = add2(acc01, pk2(a0, 0.f));
+        }
+        if (GRAD) {
+            Fd = make_ulonglong2(pk2(gsign_fast(gn.gd, dd[0]), gsign_fast(gn.gd, dd[1])),
+                                 pk2(gsign_fast(gn.gd, dd[2]), gsign_fast(gn.gd, dd[3])));
+            Fh = make_ulonglong2(pk2(gsign_fast(gn.gh, dh[0]), gsign_fast(gn.gh, dh[1])),
+                                 pk2(gsign_fast(gn.gh, dh[2]), gsign_fast(gn.gh, dh[3])));
+            Fw = make_ulonglong2(pk2(gsign_fast(gn.gw, dw[0]), gsign_fast(gn.gw, dw[1])),
+                                 pk2(gsign_fast(gn.gw, dw[2]), gsign_fast(gn.gw, dw[3])));
+        }
+    } else {
+        const f2 x01 = fma2(dw01, dw01, fma2(dh01, dh01, fma2(dd01, dd01, eps01)));
+        const f2 x23 = fma2(dw23, dw23, fma2(dh23, dh23, fma2(dd23, dd23, eps23)));
+        const f2 r01 = pk2(rsqrt_approx(lo2(x01)), rsqrt_approx(hi2(x01)));
+        const f2 r23 = pk2(rsqrt_approx(lo2(x23)), rsqrt_approx(hi2(x23)));
+        if (LOSS) {
+            const f2 s01 = mul2(x01, r01), s23 = mul2(x23, r23);
+            acc01 = add2(acc01, s01);
+            acc23 = add2(acc23, s3_ok ? s23 : pk2(lo2(s23), 0.f));
+        }
+        if (GRAD) {
+            Fd = make_ulonglong2(mul2(dd01, r01), mul2(dd23, r23));
+            Fh = make_ulonglong2(mul2(dh01, r01), mul2(dh23, r23));
+            Fw = make_ulonglong2(mul2(dw01, r01), mul2(dw23, r23));
+        }
+    }
+}
+
 // Loss terms and flux of the 4 voxels of one row of a lane (fast path).
 // Missing +D/+H/+W neighbours have already been replaced by the voxel itself
 // (edge replication) and out-of-volume voxels read as zero, so every invalid
@@ -312,7 +436,7 @@ __device__ __forceinline__ void row_flux4(const float4 &c, const float4 &n, cons
                 Fw[j] = gsign_fast(gn.gw, dw);
             }
         } else {
-            const float x = dd * dd + dh * dh + dw * dw + (j == 3 ? eps3 : eps_row);
+            const float x = iso_x(dd, dh, dw, j == 3 ? eps3 : eps_row);
             const float r = rsqrt_approx(x);
             if (LOSS) {
                 const float sv = x * r;
@@ -397,7 +521,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
         const int scol = kHaloW + 4 * lane;  // smem column of this lane's first voxel
         const size_t plane_elems = (size_t)pl.H * pl.W;
         const float kInf = __int_as_float(0x7f800000);
-        float Fd_prev[R][4];
+        f2 Fd_prev[R][2];  // Fd of the previous plane, as pairs
         int seq = 0;
 
         for (long long u = blockIdx.x; u < pl.n_units; u += gridDim.x) {
@@ -418,9 +542,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
             float *gbase = grad + (((size_t)U.n * pl.Dp) * pl.H + hbase) * (size_t)pl.W + wcol;
 
 #pragma unroll
-            for (int i = 0; i < R; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) Fd_prev[i][j] = 0.f;
+            for (int i = 0; i < R; ++i) Fd_prev[i][0] = Fd_prev[i][1] = 0ull;
 
             const int q0 = seq;
             if (!mbar_wait_bounded(&sm.full[q0 % S], (uint32_t)((q0 / S) & 1), kWaitLimitNs)) {
@@ -463,10 +585,12 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                             if (last_quad) right = cur.w;
                             const float4 dn = row_ok ? down : cur;
                             const float eps_row = row_ok ? eps_step : kInf;
-                            float Fh[4], Fw[4], d0 = 0.f, d1 = 0.f, d2 = 0.f;
+                            float Fd[4], Fh[4], Fw[4], d0 = 0.f, d1 = 0.f, d2 = 0.f;
                             row_flux4<V, false, true>(cur, nxt, dn, right, eps_row,
-                                                      last_quad ? kInf : eps_row, false, gn,
-                                                      Fd_prev[i], Fh, Fw, d0, d1, d2);
+                                                      last_quad ? kInf : eps_row, false, gn, Fd,
+                                                      Fh, Fw, d0, d1, d2);
+                            Fd_prev[i][0] = pk2(Fd[0], Fd[1]);
+                            Fd_prev[i][1] = pk2(Fd[2], Fd[3]);
                             cur = down;
                         }
                     }
@@ -514,50 +638,61 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                     }
 
                     float *gp = gbase + (size_t)p * plane_elems;
+                    f2 la01 = 0ull, la23 = 0ull;  // paired loss sums of this plane (+0.0f pairs)
+                    f2 up01 = pk2(Fh_up[0], Fh_up[1]), up23 = pk2(Fh_up[2], Fh_up[3]);
+                    ulonglong2 curp = lds_pairs(Sc, r0 + 1, scol);
 #pragma unroll
                     for (int i = 0; i < R; ++i) {
                         const int h = hbase + i;
                         const bool row_ok = h + 1 < pl.H;  // row has a +H neighbour
-                        const float4 down = lds4(Sc, r0 + i + 2, scol);
-                        const float4 nxt = has_nxt ? lds4(Sn, r0 + i + 1, scol) : cur;
-                        float right = __shfl_down_sync(0xffffffffu, cur.x, 1);
+                        const ulonglong2 down = lds_pairs(Sc, r0 + i + 2, scol);
+                        const ulonglong2 nxt = has_nxt ? lds_pairs(Sn, r0 + i + 1, scol) : curp;
+                        float right = __shfl_down_sync(0xffffffffu, lo2(curp.x), 1);
                         if (lane == 31) right = lds1(Sc, r0 + i + 1, scol + 4);
-                        if (last_quad) right = cur.w;
-                        const float4 dn = row_ok ? down : cur;
+                        if (last_quad) right = hi2(curp.y);
+                        const ulonglong2 dn = row_ok ? down : curp;
                         const float eps_row = row_ok ? eps_step : kInf;
-                        float Fd[4], Fh[4], Fw[4];
-                        float q0l = 0.f, q1l = 0.f, q2l = 0.f;
-                        row_flux4<V, LOSS, GRAD>(cur, nxt, dn, right, eps_row,
-                                                 last_quad ? kInf : eps_row, !last_quad, gn, Fd,
-                                                 Fh, Fw, q0l, q1l, q2l);
+                        const f2 e01 = pk2(eps_row, eps_row);
+                        const f2 e23 = pk2(eps_row, last_quad ? kInf : eps_row);
+                        ulonglong2 Fd, Fh, Fw;
+                        f2 q01 = 0ull, q23 = 0ull;
+                        float q1l = 0.f, q2l = 0.f;
+                        row_flux_pairs<V, LOSS, GRAD>(curp, nxt, dn, right, e01, e23, !last_quad, gn,
+                                                      Fd, Fh, Fw, q01, q23, q1l, q2l);
                         if (LOSS) {
                             if constexpr (V == QC_TV_ISO) {
-                                l0 += (row_ok && has_nxt && lane_in) ? q0l : 0.f;
+                                if (row_ok && has_nxt && lane_in) {
+                                    la01 = add2(la01, q01);
+                                    la23 = add2(la23, q23);
+                                }
                             } else {
-                                l0 += q0l;
+                                la01 = add2(la01, q01);
+                                la23 = add2(la23, q23);
                                 l1 += q1l;
                                 l2 += q2l;
                             }
                         }
                         if (GRAD) {
-                            const float fw_from_lane = __shfl_up_sync(0xffffffffu, Fw[3], 1);
+                            const float fw_from_lane = __shfl_up_sync(0xffffffffu, hi2(Fw.y), 1);
                             const float fw_from_halo = __shfl_sync(0xffffffffu, fw_halo, i);
                             const float Fw_left0 = lane == 0 ? fw_from_halo : fw_from_lane;
-                            float4 gv;
-                            gv.x = gn.gmul * ((Fd_prev[i][0] - Fd[0]) + (Fh_up[0] - Fh[0]) + (Fw_left0 - Fw[0]));
-                            gv.y = gn.gmul * ((Fd_prev[i][1] - Fd[1]) + (Fh_up[1] - Fh[1]) + (Fw[0] - Fw[1]));
-                            gv.z = gn.gmul * ((Fd_prev[i][2] - Fd[2]) + (Fh_up[2] - Fh[2]) + (Fw[1] - Fw[2]));
-                            gv.w = gn.gmul * ((Fd_prev[i][3] - Fd[3]) + (Fh_up[3] - Fh[3]) + (Fw[2] - Fw[3]));
-                            if (lane_in && h < pl.H)
-                                __stcs(reinterpret_cast<float4 *>(gp + (size_t)i * pl.W), gv);
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                Fd_prev[i][j] = Fd[j];
-                                Fh_up[j] = Fh[j];
-                            }
+                            const f2 wl01 = pk2(Fw_left0, lo2(Fw.x));
+                            const f2 wl23 = pk2(hi2(Fw.x), lo2(Fw.y));
+                            const f2 gm = pk2(gn.gmul, gn.gmul);
+                            // gmul · ((Fd_prev − Fd) + (Fh_up − Fh) + (Fw_left − Fw))
+                            const f2 g01 = mul2(gm, add2(add2(sub2(Fd_prev[i][0], Fd.x), sub2(up01, Fh.x)),
+                                                         sub2(wl01, Fw.x)));
+                            const f2 g23 = mul2(gm, add2(add2(sub2(Fd_prev[i][1], Fd.y), sub2(up23, Fh.y)),
+                                                         sub2(wl23, Fw.y)));
+                            if (lane_in && h < pl.H) stcs_pairs(gp + (size_t)i * pl.W, g01, g23);
+                            Fd_prev[i][0] = Fd.x;
+                            Fd_prev[i][1] = Fd.y;
+                            up01 = Fh.x;
+                            up23 = Fh.y;
                         }
-                        cur = down;
+                        curp = down;
                     }
+                    if (LOSS) l0 += (lo2(la01) + hi2(la01)) + (lo2(la23) + hi2(la23));
                 }
                 if (LOSS) {
                     acc0 += (double)l0;
@@ -792,6 +927,13 @@ int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, 
         using G = FastGeom;
         EncodeTiledFn encode = nullptr;
         if (int st = get_encode_fn(&encode)) return st;
+        // The tensor map is encoded through the driver API, which needs a
+        // current context on this thread; a thread that has made no runtime
+        // call yet (autograd's backward thread, a fresh host thread) has none.
+        // cudaSetDevice on the current device binds its primary context.
+        int dev = 0;
+        QC_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+        QC_CUDA_TRY(cudaSetDevice(dev), "cudaSetDevice");
         CUtensorMap map;
         const cuuint64_t dims[3] = {(cuuint64_t)pl.W, (cuuint64_t)pl.H,
                                     (cuuint64_t)pl.B * (cuuint64_t)pl.Dp};

@@ -255,3 +255,19 @@ def test_benchmark_scale_properties():
         assert_rel_max(b, (2 * a).cpu().numpy(), 1e-5, "linearity")
     o_gp, _, _ = oracle.kplanes_bwd(pts[sample].numpy(), rot.numpy(), plane.numpy(), up[sample].numpy())
     assert_rel_max(g1[0][sample.cuda()], o_gp, 1e-4, "grad_pts sample")
+
+
+@pytest.mark.parametrize("shape", [(12, 32, 256, 256), (6, 8, 17, 20), (3, 5, 7, 9), (6, 132, 8, 8), (2, 40, 33, 36)])
+def test_plane_layout_transposes(shape):
+    """[P, C, H, W] <-> [P, H, W, C], tiled fast path (C, H*W multiples of 4) and
+    the general path, against torch's permute."""
+    P, C, H, W = shape
+    gen = torch.Generator().manual_seed(10)
+    x = torch.rand(shape, generator=gen).cuda()
+    cl = torch.empty((P, H, W, C), device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _core.kplanes_planes_to_channels_last_cuda(x.data_ptr(), cl.data_ptr(), P, C, H, W, st)
+    assert torch.equal(cl, x.permute(0, 2, 3, 1))
+    back = torch.empty_like(x)
+    _core.kplanes_planes_from_channels_last_cuda(cl.data_ptr(), back.data_ptr(), P, C, H, W, st)
+    assert torch.equal(back, x)

@@ -90,6 +90,12 @@ def test_autograd_gradients_match_oracle(shape):
     assert_grad_close(v.grad, oracle.tv_l1_grad(x, [0.7, 1.3, 0.2]))
 
 
+def assert_same_up_to_rounding(a: torch.Tensor, b: torch.Tensor):
+    # The single sweep and the gradient-only kernel evaluate the same formulas;
+    # they agree to about 1 ulp of the gradient's scale.
+    torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6 * b.abs().max().item())
+
+
 @pytest.mark.parametrize("shape", SHAPES)
 def test_single_sweep_matches_pair(shape):
     v = rand_vol(shape, 13).cuda()
@@ -98,20 +104,20 @@ def test_single_sweep_matches_pair(shape):
     ref = tv_loss_iso_3d(vv, eps=1e-8)
     (0.5 * ref).backward()
     torch.testing.assert_close(loss, ref.detach(), rtol=1e-6, atol=0)
-    torch.testing.assert_close(grad, vv.grad, rtol=1e-6, atol=1e-12)
+    assert_same_up_to_rounding(grad, vv.grad)
 
     loss, grad = tv_loss_sq_3d_fwd_grad(v, 3.0)
     vv.grad = None
     (3.0 * tv_loss_sq_3d(vv)).backward()
     torch.testing.assert_close(loss, tv_loss_sq_3d(v), rtol=1e-6, atol=0)
-    torch.testing.assert_close(grad, vv.grad, rtol=1e-6, atol=1e-12)
+    assert_same_up_to_rounding(grad, vv.grad)
 
     g3 = (0.7, 1.3, 0.2)
     sums, grad = tv_loss_l1_3d_fwd_grad(v, g3)
     vv.grad = None
     (tv_loss_l1_3d(vv) * torch.tensor(g3, device="cuda")).sum().backward()
     torch.testing.assert_close(sums, tv_loss_l1_3d(v), rtol=1e-6, atol=0)
-    torch.testing.assert_close(grad, vv.grad, rtol=1e-6, atol=1e-12)
+    assert_same_up_to_rounding(grad, vv.grad)
 
 
 def test_golden_fixtures(tv_golden):
@@ -305,3 +311,34 @@ def test_full_size_iso_l1_workload():
 def test_no_kernel_gave_up_waiting():
     torch.cuda.synchronize()
     assert _core.device_fault_word(torch.cuda.current_device()) == 0
+
+
+def test_first_cuda_work_on_a_fresh_host_thread():
+    """The fast path encodes its TMA descriptor through the driver API; it must
+    work on a thread that has made no CUDA runtime call yet (autograd runs
+    backward on such a thread)."""
+    import threading
+
+    v = rand_vol((2, 20, 24, 68), 18).cuda()
+    g = torch.ones(1, device="cuda")
+    x = v.cpu().numpy()
+    # same shapes once on this thread, so that the call on the new thread is
+    # served from the caching allocator and issues no torch CUDA call of its own
+    tv_loss_iso_3d_fwd_grad(v, g, eps=1e-8)
+    torch.cuda.synchronize()
+    box = {}
+
+    def work():
+        try:
+            loss, grad = tv_loss_iso_3d_fwd_grad(v, g, eps=1e-8)
+            torch.cuda.synchronize()
+            box["res"] = (loss.item(), grad.cpu())
+        except Exception as e:  # noqa: BLE001
+            box["err"] = e
+
+    th = threading.Thread(target=work)
+    th.start()
+    th.join()
+    assert "err" not in box, box.get("err")
+    np.testing.assert_allclose(box["res"][0], oracle.tv_iso_loss(x, 1e-8), rtol=FWD_RTOL)
+    assert_grad_close(box["res"][1], oracle.tv_iso_grad(x, 1.0 / n_corners(x.shape), 1e-8))
