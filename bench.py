@@ -303,7 +303,7 @@ def cpu_oracle():
     return oracle, oracle.threads()
 
 
-def cpu_tv_iso_l1(sample_d: int = 32, min_seconds: float = 10.0, reps: int | None = None):
+def cpu_tv_iso_l1(sample_d: int = 32, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
     oracle, threads = cpu_oracle()
     x = tv_iso_l1_volume(1, d=sample_d).numpy()
     voxels = x.size
@@ -316,7 +316,8 @@ def cpu_tv_iso_l1(sample_d: int = 32, min_seconds: float = 10.0, reps: int | Non
         oracle.tv_l1_loss(x)
         oracle.tv_l1_grad(x, [1.0, 1.0, 1.0])
 
-    step()
+    for _ in range(warmup):
+        step()
     t0 = time.perf_counter()
     k = 0
     while True:
@@ -332,11 +333,11 @@ def cpu_tv_iso_l1(sample_d: int = 32, min_seconds: float = 10.0, reps: int | Non
         "cores": threads,
         "kind": "port",
         "sample": f"[4, {sample_d}, 256, 256] slab of the workload volume (1/{256 // sample_d} of it): "
-        f"iso loss + iso grad + L1 sums + L1 grad with the C oracle (OpenMP), {k} reps, {el:.1f} s",
+        f"iso loss + iso grad + L1 sums + L1 grad with the C oracle (OpenMP), {k} reps, {el:.3f} s",
     }, per_step
 
 
-def cpu_kplanes(sample_n: int = 1 << 14, min_seconds: float = 10.0, reps: int | None = None):
+def cpu_kplanes(sample_n: int = 1 << 14, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
     oracle, threads = cpu_oracle()
     pts, rot, plane, up = kplanes_inputs(2)
     p, r, g, u = pts[:sample_n].numpy(), rot.numpy(), plane.numpy(), up[:sample_n].numpy()
@@ -345,7 +346,8 @@ def cpu_kplanes(sample_n: int = 1 << 14, min_seconds: float = 10.0, reps: int | 
         oracle.kplanes_fwd(p, r, g)
         oracle.kplanes_bwd(p, r, g, u)
 
-    step()
+    for _ in range(warmup):
+        step()
     t0 = time.perf_counter()
     k = 0
     while True:
@@ -361,7 +363,7 @@ def cpu_kplanes(sample_n: int = 1 << 14, min_seconds: float = 10.0, reps: int | 
         "cores": threads,
         "kind": "port",
         "sample": f"first {sample_n} of the 2^20 points, forward + backward with the C oracle "
-        f"(OpenMP), {k} reps, {el:.1f} s",
+        f"(OpenMP), {k} reps, {el:.3f} s",
     }, per_step
 
 
@@ -412,12 +414,11 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
     dom_ms = max(iso_ms, l1_ms)
     dom = "tv iso single sweep" if iso_ms >= l1_ms else "tv L1 single sweep"
 
-    # end to end: the public API from pinned host memory
-    e2e = None
+    # end to end: the public API from pinned host memory (each rank copies
+    # its own slab in, and reads the global losses back, every step)
+    host = vol_cpu.pin_memory()
+    res_host = torch.empty(4, pin_memory=True)
     if ctx.world == 1:
-        host = vol_cpu.pin_memory()
-        res_host = torch.empty(4, pin_memory=True)
-
         def e2e_step():
             v = host.to(dev, non_blocking=True)
             li, _ = tv_loss_iso_3d_fwd_grad(v, g1, eps=1e-8)
@@ -425,14 +426,23 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
             res_host[:1].copy_(li.reshape(1), non_blocking=True)
             res_host[1:].copy_(ls, non_blocking=True)
             torch.cuda.current_stream().synchronize()
+    else:
+        def e2e_step():
+            slab[:, 1 : D_LOCAL + 1].copy_(host, non_blocking=True)
+            sharded.exchange_halos(slab)
+            li, _ = sharded.tv_loss_slab_fwd_grad(sharded.ISO, slab, g1, global_d, 1e-8, exchange=False)
+            ls, _ = sharded.tv_loss_slab_fwd_grad(sharded.L1, slab, g3, global_d, exchange=False)
+            res_host[:1].copy_(li.reshape(1), non_blocking=True)
+            res_host[1:].copy_(ls, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
 
-        e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
-        e2e = {
-            "value": voxels_local / (e2e_ms / steps / 1e3),
-            "unit": "voxels/s",
-            "h2d_bytes_per_step": host.numel() * 4,
-            "d2h_bytes_per_step": 16,
-        }
+    e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
+    e2e = {
+        "value": voxels_local * ctx.world / (e2e_ms / steps / 1e3),
+        "unit": "voxels/s",
+        "h2d_bytes_per_step": host.numel() * 4 * ctx.world,
+        "d2h_bytes_per_step": 16 * ctx.world,
+    }
 
     peak, peak_kind = measured_hbm_peak()
     algo_bytes = 8.0 * voxels_local  # single sweep: read 4 B + write 4 B per voxel
@@ -445,7 +455,7 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
         "ms_per_step": ms_step,
         "gpu_launches": launches_per_step * steps,
         "config": {
-            "workload": "tv_iso_l1: tv_loss_iso_3d (eps 1e-8) + tv_loss_l1_3d single-sweep fwd+grad",
+            "workload": DESCRIPTIONS["tv_iso_l1"],
             "shape_per_gpu": [4, D_LOCAL, 256, 256],
             "global_shape": [4, D_LOCAL * ctx.world, 256, 256],
             "parallelism": f"d-slab{ctx.world}" if ctx.world > 1 else "single GPU",
@@ -495,7 +505,7 @@ def run_tv_sq_128(ctx: Ctx, steps: int, warmup: int) -> dict:
         "unit": "voxels/s",
         "ms_per_step": k_ms,
         "gpu_launches": 2 * steps,
-        "config": {"workload": "tv_sq_128: tv_loss_sq_3d single-sweep fwd+grad on [128,128,128]",
+        "config": {"workload": DESCRIPTIONS["tv_sq_128"],
                    "l2": "L2 flushed (192 MB write) between steps; value uses the op's event time",
                    "step_ms_with_flush": ms / steps},
         "roofline": {"bound": "hbm", "kernel": "tv sq single sweep", "achieved": algo / (k_ms / 1e3) / 1e9,
@@ -532,7 +542,7 @@ def run_tv_1024(ctx: Ctx, steps: int, warmup: int) -> dict:
         "unit": "voxels/s",
         "ms_per_step": ms_step,
         "gpu_launches": 4 * steps,
-        "config": {"workload": "tv_1024: tv_loss_sq_3d + tv_loss_iso_3d single-sweep fwd+grad on [1024]^3 blobs",
+        "config": {"workload": DESCRIPTIONS["tv_1024"],
                    "l2": "inputs larger than L2 (4 GiB)",
                    "per_loss_ms": {"sq": t_sq.mean_ms(steps), "iso": t_iso.mean_ms(steps)}},
         "roofline": {"bound": "hbm", "kernel": "tv single sweep", "achieved": algo / (dom_ms / 1e3) / 1e9,
@@ -602,7 +612,7 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         "unit": "points/s",
         "ms_per_step": ms_step,
         "gpu_launches": 7 * steps,
-        "config": {"workload": "kplanes: kplanes_tilted_fuse fwd + bwd ops, N=2^20, T=4, C=32, 256^2",
+        "config": {"workload": DESCRIPTIONS["kplanes"],
                    "points_per_gpu": N, "parallelism": f"points{ctx.world}" if ctx.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (512 MiB output + 512 MiB upstream gradient per step)",
                    "fwd_op_ms": f_ms, "bwd_op_ms": b_ms},
@@ -618,6 +628,13 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
     }
 
 
+DESCRIPTIONS = {
+    "tv_iso_l1": "tv_iso_l1: tv_loss_iso_3d (eps 1e-8) + tv_loss_l1_3d single-sweep fwd+grad",
+    "tv_sq_128": "tv_sq_128: tv_loss_sq_3d single-sweep fwd+grad on [128,128,128]",
+    "tv_1024": "tv_1024: tv_loss_sq_3d + tv_loss_iso_3d single-sweep fwd+grad on [1024]^3 blobs",
+    "kplanes": "kplanes: kplanes_tilted_fuse fwd + bwd ops, N=2^20, T=4, C=32, 256^2",
+}
+
 WORKLOADS = {
     "tv_iso_l1": run_tv_iso_l1,
     "tv_sq_128": run_tv_sq_128,
@@ -632,11 +649,12 @@ WORKLOADS = {
 def run_reference(ctx: Ctx, args) -> dict | None:
     if ctx.rank != 0:
         return None
+    warmup = max(args.warmup, 3)
     if args.workload in ("kplanes",):
-        cb, per_step = cpu_kplanes(reps=args.steps)
+        cb, per_step = cpu_kplanes(reps=args.steps, warmup=warmup)
         metric = "K-Planes fwd+bwd points/sec"
     else:
-        cb, per_step = cpu_tv_iso_l1(reps=args.steps)
+        cb, per_step = cpu_tv_iso_l1(reps=args.steps, warmup=warmup)
         metric = "TV fwd+grad voxels/sec"
     return {
         "metric": metric,
@@ -644,7 +662,7 @@ def run_reference(ctx: Ctx, args) -> dict | None:
         "unit": cb["unit"],
         "impl": "reference",
         "ms_per_step": per_step * 1e3,
-        "config": {"workload": args.workload, "sample": cb["sample"]},
+        "config": {"workload": DESCRIPTIONS[args.workload], "sample": cb["sample"]},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "dtype": "f32",
