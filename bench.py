@@ -585,6 +585,8 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
     fwd_bytes = 12 * N + P + 4 * N * T * C
     bwd_bytes = 12 * N + 4 * N * T * C + P + P + 12 * N
     peak, peak_kind = measured_hbm_peak()
+    tr = ncu_traffic("kplanes")
+    kp_traffic = None if tr is None else tr["bytes_per_unit"] * N
 
     e2e = None
     if ctx.world == 1:
@@ -619,7 +621,7 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         "roofline": {"bound": "hbm", "kernel": "kplanes backward op",
                      "achieved": bwd_bytes / (b_ms / 1e3) / 1e9, "peak": peak,
                      "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
-                     "frac": bwd_bytes / (b_ms / 1e3) / 1e9 / peak, "traffic": None,
+                     "frac": bwd_bytes / (b_ms / 1e3) / 1e9 / peak, "traffic": kp_traffic,
                      "algorithmic_bytes": bwd_bytes, "step_algorithmic_bytes": fwd_bytes + bwd_bytes,
                      "step_frac": (fwd_bytes + bwd_bytes) / (ms_step / 1e3) / 1e9 / peak},
         "clocks": sampler.summary(),
