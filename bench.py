@@ -392,6 +392,22 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
             iso(vol)
             l1(vol)
 
+    elif ctx.args.tv_transport == "peer":
+        # halos and loss sums over peer memory: kernels only, no collective
+        global_d = D_LOCAL * ctx.world
+        ps = sharded.PeerSlab(4, global_d, 256, 256, device=dev)
+        ps.owned.copy_(vol_cpu.to(dev))
+        slab = ps.slab
+        grads = [torch.empty_like(slab), torch.empty_like(slab)]
+        iso = t_iso.wrap(lambda: ps.fwd_grad(sharded.ISO, g1, 1e-8, grad=grads[0], exchange=False))
+        l1 = t_l1.wrap(lambda: ps.fwd_grad(sharded.L1, g3, grad=grads[1], exchange=False))
+        launches_per_step = 5  # halo exchange, two sweeps, two cross-rank finalize kernels
+
+        def step():
+            ps.exchange_halos()
+            iso()
+            l1()
+
     else:
         global_d = D_LOCAL * ctx.world
         slab = torch.zeros((4, D_LOCAL + 2, 256, 256), device=dev)
@@ -403,8 +419,6 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
             sharded.exchange_halos(slab)
             iso()
             l1()
-
-        vol = slab
 
     sampler = ClockSampler(ctx.local_rank)
     ms = time_steps(ctx, step, steps, warmup, sampler)
@@ -426,6 +440,14 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
             res_host[:1].copy_(li.reshape(1), non_blocking=True)
             res_host[1:].copy_(ls, non_blocking=True)
             torch.cuda.current_stream().synchronize()
+    elif ctx.args.tv_transport == "peer":
+        def e2e_step():
+            ps.owned.copy_(host, non_blocking=True)
+            li, _ = ps.fwd_grad(sharded.ISO, g1, 1e-8, grad=grads[0])
+            ls, _ = ps.fwd_grad(sharded.L1, g3, grad=grads[1], exchange=False)
+            res_host[:1].copy_(li.reshape(1), non_blocking=True)
+            res_host[1:].copy_(ls, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
     else:
         def e2e_step():
             slab[:, 1 : D_LOCAL + 1].copy_(host, non_blocking=True)
@@ -437,6 +459,8 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
             torch.cuda.current_stream().synchronize()
 
     e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
+    if ctx.world > 1 and ctx.args.tv_transport == "peer":
+        ps.close()
     e2e = {
         "value": voxels_local * ctx.world / (e2e_ms / steps / 1e3),
         "unit": "voxels/s",
@@ -458,7 +482,7 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
             "workload": DESCRIPTIONS["tv_iso_l1"],
             "shape_per_gpu": [4, D_LOCAL, 256, 256],
             "global_shape": [4, D_LOCAL * ctx.world, 256, 256],
-            "parallelism": f"d-slab{ctx.world}" if ctx.world > 1 else "single GPU",
+            "parallelism": f"d-slab{ctx.world} ({ctx.args.tv_transport})" if ctx.world > 1 else "single GPU",
             "l2": "inputs larger than L2 (268 MB volume per GPU, 2 x 268 MB of gradients written per step)",
             "per_loss_ms": {"iso": iso_ms, "l1": l1_ms},
         },
@@ -571,20 +595,24 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
             fwd()
             bwd()
     else:
+        # per-rotation backward with each rotation's plane-gradient all_reduce
+        # overlapping the next rotation's backward
+        fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u))
+
         def step():
-            fwd()
-            g_pts, g_r, g_p = bwd()
-            dist.all_reduce(g_p)
-            dist.all_reduce(g_r)
+            fb()
 
     sampler = ClockSampler(ctx.local_rank)
     ms = time_steps(ctx, step, steps, warmup, sampler)
     ms_step = ms / steps
     f_ms, b_ms = t_f.mean_ms(steps), t_b.mean_ms(steps)
+    if ctx.world > 1:
+        f_ms = None  # b_ms covers the whole sharded forward + backward
     P = 3 * T * C * plane.shape[2] * plane.shape[3] * 4
     fwd_bytes = 12 * N + P + 4 * N * T * C
     bwd_bytes = 12 * N + 4 * N * T * C + P + P + 12 * N
     peak, peak_kind = measured_hbm_peak()
+    roof_bytes = bwd_bytes if ctx.world == 1 else fwd_bytes + bwd_bytes
     tr = ncu_traffic("kplanes")
     kp_traffic = None if tr is None else tr["bytes_per_unit"] * N
 
@@ -613,16 +641,18 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         "value": N * ctx.world / (ms_step / 1e3),
         "unit": "points/s",
         "ms_per_step": ms_step,
-        "gpu_launches": 7 * steps,
+        "gpu_launches": (7 if ctx.world == 1 else 2 + 2 * T) * steps,
         "config": {"workload": DESCRIPTIONS["kplanes"],
                    "points_per_gpu": N, "parallelism": f"points{ctx.world}" if ctx.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (512 MiB output + 512 MiB upstream gradient per step)",
                    "fwd_op_ms": f_ms, "bwd_op_ms": b_ms},
-        "roofline": {"bound": "hbm", "kernel": "kplanes backward op",
-                     "achieved": bwd_bytes / (b_ms / 1e3) / 1e9, "peak": peak,
+        "roofline": {"bound": "hbm",
+                     "kernel": "kplanes backward op" if ctx.world == 1 else "kplanes sharded fwd+bwd (per rank)",
+                     "achieved": roof_bytes / (b_ms / 1e3) / 1e9, "peak": peak,
                      "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
-                     "frac": bwd_bytes / (b_ms / 1e3) / 1e9 / peak, "traffic": kp_traffic,
-                     "algorithmic_bytes": bwd_bytes, "step_algorithmic_bytes": fwd_bytes + bwd_bytes,
+                     "frac": roof_bytes / (b_ms / 1e3) / 1e9 / peak,
+                     "traffic": kp_traffic if ctx.world == 1 else None,
+                     "algorithmic_bytes": roof_bytes, "step_algorithmic_bytes": fwd_bytes + bwd_bytes,
                      "step_frac": (fwd_bytes + bwd_bytes) / (ms_step / 1e3) / 1e9 / peak},
         "clocks": sampler.summary(),
         "e2e": e2e,
@@ -679,6 +709,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tv_iso_l1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tv-transport", choices=("peer", "nccl"), default="peer",
+                    help="multi-GPU TV: halos and loss sums over peer memory, or NCCL send/recv + all_gather")
     args = ap.parse_args()
     ctx = Ctx(args)
     warmup = max(args.warmup, 3)

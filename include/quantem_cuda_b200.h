@@ -154,6 +154,71 @@ int tv_loss_3d_slab_cuda(int variant, int flags, const float *d_vol, const float
                          int has_prev, int has_next, float eps, float acc_scale, void *d_workspace,
                          size_t workspace_bytes, cudaStream_t stream);
 
+/* ── D-slabs over peer memory (one process per GPU, GPUs of one node) ──────
+ *
+ * No counterpart in the reference, which is single-GPU. Each rank keeps its
+ * slab [B, Dp, H, W] (planes 1..Dp-2 owned, halos 0 and Dp-1) and a small
+ * communication block in memory allocated with quantem_cuda_peer_alloc and
+ * mapped into its neighbours with CUDA IPC. The halo exchange and the
+ * cross-rank loss reduction are kernels that store into the peers' memory
+ * over NVLink and signal with release/acquire flags, so a step issues no
+ * library collective and never synchronises the host.
+ *
+ * Every rank makes the same sequence of calls. `seq` numbers the calls of one
+ * entry point (the halo exchange and the reduction keep separate counters):
+ * 1 for the first call, +1 for each later call, the same on every rank. Waits
+ * on another rank give up after `timeout_ns` (0: 10 s), set
+ * QC_FAULT_PEER_WAIT in the device fault word and (for the reduction) store
+ * NaN in the loss, so a rank that stops never hangs the others. */
+#define QC_MAX_PEER_RANKS 8
+#define QC_IPC_HANDLE_BYTES 64
+#define QC_FAULT_TMA_WAIT 0x1u  /* a kernel gave up waiting for its own TMA copies */
+#define QC_FAULT_PEER_WAIT 0x2u /* a kernel gave up waiting for another rank */
+
+typedef struct qc_tv_peers {
+    int rank;                          /* this rank, 0 <= rank < world */
+    int world;                         /* ranks in the D split, <= QC_MAX_PEER_RANKS */
+    unsigned long long timeout_ns;     /* bound on every wait for another rank (0: 10 s) */
+    void *comm[QC_MAX_PEER_RANKS];     /* every rank's communication block, mapped in this
+                                          process (comm[rank] is this rank's own) */
+    float *prev_slab;                  /* rank-1's slab mapped here (NULL on rank 0) */
+    float *next_slab;                  /* rank+1's slab mapped here (NULL on the last rank) */
+    int prev_dp;                       /* Dp of rank-1's slab */
+    int next_dp;                       /* Dp of rank+1's slab */
+} qc_tv_peers;
+
+/* Device memory that other processes can map: cudaMalloc, zero-filled before
+ * returning (synchronous). Free with quantem_cuda_peer_free. */
+int quantem_cuda_peer_alloc(size_t bytes, void **d_ptr);
+int quantem_cuda_peer_free(void *d_ptr);
+/* CUDA IPC handle (QC_IPC_HANDLE_BYTES bytes) of a quantem_cuda_peer_alloc
+ * allocation, and its mapping in another process (with peer access enabled). */
+int quantem_cuda_ipc_handle(void *d_ptr, void *handle_out);
+int quantem_cuda_ipc_open(const void *handle, void **d_ptr);
+int quantem_cuda_ipc_close(void *d_ptr);
+
+/* Bytes of one rank's communication block (flags and reduction slots). */
+size_t tv_peer_comm_bytes(void);
+
+/* Fills the halo planes of d_slab [B, Dp, H, W] (this rank's own slab, which
+ * its neighbours have mapped): plane 1 goes into rank-1's plane prev_dp-1 and
+ * plane Dp-2 into rank+1's plane 0, each after that neighbour has signalled
+ * that its earlier work on the stream is done; returns (on the GPU) once both
+ * neighbours' planes have arrived here. The sweeps that read the halos must be
+ * on the same stream as the next exchange. */
+int tv_slab_halo_exchange_cuda(const qc_tv_peers *peers, unsigned long long seq, float *d_slab,
+                               int B, int Dp, int H, int W, cudaStream_t stream);
+
+/* tv_loss_3d_slab_cuda with the loss summed over all ranks inside the
+ * finalize kernel: each rank's fixed-order fp64 total goes to every rank's
+ * communication block, and every rank adds the totals in rank order, so d_acc
+ * holds the same bits on every rank. flags must include QC_TV_LOSS. */
+int tv_loss_3d_slab_peer_cuda(const qc_tv_peers *peers, unsigned long long seq, int variant,
+                              int flags, const float *d_vol, const float *d_g, float *d_acc,
+                              float *d_grad_vol, int B, int Dp, int H, int W, int d_lo, int d_hi,
+                              int has_prev, int has_next, float eps, float acc_scale,
+                              void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* ── tilted K-Planes ────────────────────────────────────────────────────── */
 
 /* out[b, t*C + c] = Π_{p∈XY,ZX,YZ} bilinear(grid[t*3+p], (R_t·pts_b) pair p), with
@@ -171,6 +236,19 @@ int kplanes_tilted_fuse_cuda(const float *d_pts, const float *d_R, const float *
 int kplanes_tilted_fuse_grad_cuda(const float *d_pts, const float *d_R, const float *d_grid,
                                   const float *d_gout, float *d_ggrid, float *d_gR, float *d_gpts,
                                   long B, int T, int C, int H, int W, cudaStream_t stream);
+
+/* The backward restricted to rotations [t_begin, t_end): accumulates the
+ * gradient of those rotations' planes (grid planes 3*t_begin .. 3*t_end-1) and
+ * rows of gR, and their share of gpts; the other outputs are not touched.
+ * Summing the calls over a partition of [0, T) gives the full backward (up to
+ * the order of the gpts additions). No counterpart in the reference: it lets a
+ * multi-GPU caller start reducing one rotation's plane gradient across ranks
+ * while the next rotation's backward runs. */
+int kplanes_tilted_fuse_grad_rotations_cuda(const float *d_pts, const float *d_R,
+                                            const float *d_grid, const float *d_gout,
+                                            float *d_ggrid, float *d_gR, float *d_gpts, long B,
+                                            int T, int C, int H, int W, int t_begin, int t_end,
+                                            cudaStream_t stream);
 
 /* Plane layout conversion [P, C, H, W] -> [P, H, W, C] and back. Replaces the
  * torch permute+contiguous of the reference's op layer

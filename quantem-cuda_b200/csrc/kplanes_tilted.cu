@@ -194,12 +194,12 @@ template <int L>
 __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
     const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
     const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
-    float *__restrict__ gpts, long long B, int T, int H, int W) {
+    float *__restrict__ gpts, long long B, int T, int H, int W, int t0) {
     constexpr int C = 4 * L;
     constexpr int G = 32 / L;
     constexpr int NWARP = kThreads / 32;
     __shared__ float sred[NWARP][9];
-    const int t = blockIdx.y;
+    const int t = t0 + blockIdx.y;
     float Rt[9];
 #pragma unroll
     for (int k = 0; k < 9; ++k) Rt[k] = __ldg(R + 9 * t + k);
@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(kThreads) kpt_fwd_generic_kernel(
 __global__ void __launch_bounds__(kThreads) kpt_bwd_generic_kernel(
     const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
     const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
-    float *__restrict__ gpts, long long B, int T, int C, int H, int W) {
+    float *__restrict__ gpts, long long B, int T, int C, int H, int W, int t0, int t1) {
     extern __shared__ float smem[];
     float *sR = smem;
     float *sgR = smem + 9 * T;
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kThreads) kpt_bwd_generic_kernel(
     for (long long b = warp0; b < B; b += nwarps) {
         const float px = pts[3 * b], py = pts[3 * b + 1], pz = pts[3 * b + 2];
         float gpx = 0.f, gpy = 0.f, gpz = 0.f;
-        for (int t = 0; t < T; ++t) {
+        for (int t = t0; t < t1; ++t) {
             const float *Rt = sR + 9 * t;
             float rx, ry, rz;
             rotate(Rt, px, py, pz, rx, ry, rz);
@@ -593,13 +593,15 @@ int fwd_v4(const float *pts, const float *R, const float *grid, float *out, long
 
 template <int L>
 int bwd_v4(const float *pts, const float *R, const float *grid, const float *gout, float *ggrid,
-           float *gR, float *gpts, long long B, int T, int H, int W, cudaStream_t stream) {
+           float *gR, float *gpts, long long B, int T, int H, int W, int t0, int t1,
+           cudaStream_t stream) {
     constexpr int G = 32 / L;
     int gx = 0;
     if (int st = rotation_grid_x((B + G - 1) / G, kBwdMinBlocks, &gx)) return st;
-    QC_RETURN_IF(T > 65535, QC_ERR_INVALID_ARGUMENT, "kplanes: T=%d exceeds 65535", T);
-    kpt_bwd_v4_kernel<L><<<dim3(gx, T), kThreads, 0, stream>>>(pts, R, grid, gout, ggrid, gR, gpts,
-                                                                B, T, H, W);
+    QC_RETURN_IF(t1 - t0 > 65535, QC_ERR_INVALID_ARGUMENT, "kplanes: %d rotations exceed 65535",
+                 t1 - t0);
+    kpt_bwd_v4_kernel<L><<<dim3(gx, t1 - t0), kThreads, 0, stream>>>(pts, R, grid, gout, ggrid, gR,
+                                                                      gpts, B, T, H, W, t0);
     QC_CHECK_LAUNCH("kpt_bwd_v4_kernel launch");
     return 0;
 }
@@ -638,35 +640,49 @@ int kplanes_tilted_fuse_cuda(const float *d_pts, const float *d_R, const float *
     return 0;
 }
 
-int kplanes_tilted_fuse_grad_cuda(const float *d_pts, const float *d_R, const float *d_grid,
-                                  const float *d_gout, float *d_ggrid, float *d_gR, float *d_gpts,
-                                  long B, int T, int C, int H, int W, cudaStream_t stream) {
+int kplanes_tilted_fuse_grad_rotations_cuda(const float *d_pts, const float *d_R,
+                                            const float *d_grid, const float *d_gout,
+                                            float *d_ggrid, float *d_gR, float *d_gpts, long B,
+                                            int T, int C, int H, int W, int t_begin, int t_end,
+                                            cudaStream_t stream) {
     using namespace qc::kp;
     if (int st = check_shapes("kplanes_tilted_fuse_grad_cuda", B, T, C, H, W)) return st;
-    if (B == 0 || T == 0 || C == 0) return 0;
+    QC_RETURN_IF(t_begin < 0 || t_end > T || t_begin > t_end, QC_ERR_INVALID_ARGUMENT,
+                 "kplanes_tilted_fuse_grad_cuda: rotations [%d, %d) outside [0, %d)", t_begin,
+                 t_end, T);
+    if (B == 0 || t_begin == t_end || C == 0) return 0;
     QC_RETURN_IF(H == 0 || W == 0, QC_ERR_INVALID_ARGUMENT,
                  "kplanes_tilted_fuse_grad_cuda: empty plane");
     QC_RETURN_IF(!d_pts || !d_R || !d_grid || !d_gout || !d_ggrid || !d_gR || !d_gpts,
                  QC_ERR_INVALID_ARGUMENT, "kplanes_tilted_fuse_grad_cuda: null pointer");
     const bool vec = (C % 4 == 0) && C <= 128 && aligned16(d_grid) && aligned16(d_gout) &&
                      aligned16(d_ggrid);
+    const int t0 = t_begin, t1 = t_end;
     if (vec) {
         switch (C / 4) {
-            case 1: return bwd_v4<1>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
-            case 2: return bwd_v4<2>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
-            case 4: return bwd_v4<4>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
-            case 8: return bwd_v4<8>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
-            case 16: return bwd_v4<16>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
-            case 32: return bwd_v4<32>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, stream);
+            case 1: return bwd_v4<1>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
+            case 2: return bwd_v4<2>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
+            case 4: return bwd_v4<4>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
+            case 8: return bwd_v4<8>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
+            case 16: return bwd_v4<16>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
+            case 32: return bwd_v4<32>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
             default: break;
         }
     }
     int blocks = 0;
     if (int st = grid_size(B, &blocks)) return st;
     kpt_bwd_generic_kernel<<<blocks, kThreads, 18 * T * sizeof(float), stream>>>(
-        d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, C, H, W);
+        d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, C, H, W, t0, t1);
     QC_CHECK_LAUNCH("kpt_bwd_generic_kernel launch");
     return 0;
+}
+
+int kplanes_tilted_fuse_grad_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                                  const float *d_gout, float *d_ggrid, float *d_gR, float *d_gpts,
+                                  long B, int T, int C, int H, int W, cudaStream_t stream) {
+    return kplanes_tilted_fuse_grad_rotations_cuda(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR,
+                                                   d_gpts, B, T, C, H, W, 0, T < 0 ? 0 : T,
+                                                   stream);
 }
 
 int kplanes_planes_to_channels_last_cuda(const float *d_src, float *d_dst, int P, int C, int H,

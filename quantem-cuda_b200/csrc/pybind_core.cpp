@@ -6,10 +6,12 @@
 // csrc/bindings/core/ml.cpp:89-128). A non-zero status raises RuntimeError,
 // which is what the reference's std::runtime_error becomes in Python.
 #include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
 
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "quantem_cuda_b200.h"
 
@@ -29,6 +31,25 @@ T *ptr(uintptr_t v) {
 }
 
 cudaStream_t stream_of(uintptr_t v) { return reinterpret_cast<cudaStream_t>(v); }
+
+qc_tv_peers make_peers(int rank, int world, unsigned long long timeout_ns,
+                       const std::vector<uintptr_t> &comm, uintptr_t prev_slab, int prev_dp,
+                       uintptr_t next_slab, int next_dp) {
+    if (world < 1 || world > QC_MAX_PEER_RANKS || (int)comm.size() != world)
+        throw std::invalid_argument("TvPeers: need 1 <= world <= " +
+                                    std::to_string(QC_MAX_PEER_RANKS) +
+                                    " and one communication block per rank");
+    qc_tv_peers p{};
+    p.rank = rank;
+    p.world = world;
+    p.timeout_ns = timeout_ns;
+    for (int q = 0; q < world; ++q) p.comm[q] = ptr<void>(comm[q]);
+    p.prev_slab = ptr<float>(prev_slab);
+    p.prev_dp = prev_dp;
+    p.next_slab = ptr<float>(next_slab);
+    p.next_dp = next_dp;
+    return p;
+}
 
 }  // namespace
 
@@ -153,6 +174,22 @@ PYBIND11_MODULE(_core, m) {
         py::arg("C"), py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
 
     m.def(
+        "kplanes_tilted_fuse_grad_rotations_cuda",
+        [](uintptr_t pts, uintptr_t r, uintptr_t grid, uintptr_t gout, uintptr_t ggrid,
+           uintptr_t gr, uintptr_t gpts, long B, int T, int C, int H, int W, int t_begin,
+           int t_end, uintptr_t stream) {
+            check(kplanes_tilted_fuse_grad_rotations_cuda(
+                ptr<const float>(pts), ptr<const float>(r), ptr<const float>(grid),
+                ptr<const float>(gout), ptr<float>(ggrid), ptr<float>(gr), ptr<float>(gpts), B, T,
+                C, H, W, t_begin, t_end, stream_of(stream)));
+        },
+        "kplanes_tilted_fuse_grad_cuda restricted to rotations [t_begin, t_end).",
+        py::arg("pts_ptr"), py::arg("r_ptr"), py::arg("grid_ptr"), py::arg("gout_ptr"),
+        py::arg("ggrid_ptr"), py::arg("gr_ptr"), py::arg("gpts_ptr"), py::arg("B"), py::arg("T"),
+        py::arg("C"), py::arg("H"), py::arg("W"), py::arg("t_begin"), py::arg("t_end"),
+        py::arg("stream_ptr"));
+
+    m.def(
         "kplanes_planes_to_channels_last_cuda",
         [](uintptr_t src, uintptr_t dst, int P, int C, int H, int W, uintptr_t stream) {
             check(kplanes_planes_to_channels_last_cuda(ptr<const float>(src), ptr<float>(dst), P, C,
@@ -178,4 +215,77 @@ PYBIND11_MODULE(_core, m) {
             return w;
         },
         py::arg("device"), py::arg("clear") = false);
+
+    // ── peer memory and the D-slab exchange over it ──
+    m.attr("MAX_PEER_RANKS") = QC_MAX_PEER_RANKS;
+    m.attr("FAULT_TMA_WAIT") = QC_FAULT_TMA_WAIT;
+    m.attr("FAULT_PEER_WAIT") = QC_FAULT_PEER_WAIT;
+    m.def("tv_peer_comm_bytes", &tv_peer_comm_bytes);
+    m.def(
+        "peer_alloc",
+        [](size_t bytes) {
+            void *p = nullptr;
+            check(quantem_cuda_peer_alloc(bytes, &p));
+            return reinterpret_cast<uintptr_t>(p);
+        },
+        py::arg("bytes"));
+    m.def("peer_free", [](uintptr_t p) { check(quantem_cuda_peer_free(ptr<void>(p))); },
+          py::arg("ptr"));
+    m.def(
+        "ipc_handle",
+        [](uintptr_t p) {
+            char h[QC_IPC_HANDLE_BYTES];
+            check(quantem_cuda_ipc_handle(ptr<void>(p), h));
+            return py::bytes(h, QC_IPC_HANDLE_BYTES);
+        },
+        py::arg("ptr"));
+    m.def(
+        "ipc_open",
+        [](py::bytes handle) {
+            std::string h = handle;
+            if (h.size() != QC_IPC_HANDLE_BYTES)
+                throw std::invalid_argument("ipc_open: handle must be " +
+                                            std::to_string(QC_IPC_HANDLE_BYTES) + " bytes");
+            void *p = nullptr;
+            check(quantem_cuda_ipc_open(h.data(), &p));
+            return reinterpret_cast<uintptr_t>(p);
+        },
+        py::arg("handle"));
+    m.def("ipc_close", [](uintptr_t p) { check(quantem_cuda_ipc_close(ptr<void>(p))); },
+          py::arg("ptr"));
+
+    py::class_<qc_tv_peers>(m, "TvPeers")
+        .def(py::init(&make_peers), py::arg("rank"), py::arg("world"), py::arg("timeout_ns"),
+             py::arg("comm"), py::arg("prev_slab"), py::arg("prev_dp"), py::arg("next_slab"),
+             py::arg("next_dp"))
+        .def_readonly("rank", &qc_tv_peers::rank)
+        .def_readonly("world", &qc_tv_peers::world)
+        .def_readonly("timeout_ns", &qc_tv_peers::timeout_ns);
+
+    m.def(
+        "tv_slab_halo_exchange_cuda",
+        [](const qc_tv_peers &peers, unsigned long long seq, uintptr_t slab, int B, int Dp, int H,
+           int W, uintptr_t stream) {
+            check(tv_slab_halo_exchange_cuda(&peers, seq, ptr<float>(slab), B, Dp, H, W,
+                                             stream_of(stream)));
+        },
+        py::arg("peers"), py::arg("seq"), py::arg("slab_ptr"), py::arg("B"), py::arg("Dp"),
+        py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_3d_slab_peer_cuda",
+        [](const qc_tv_peers &peers, unsigned long long seq, int variant, int flags,
+           uintptr_t vol, uintptr_t g, uintptr_t acc, uintptr_t grad, int B, int Dp, int H, int W,
+           int d_lo, int d_hi, int has_prev, int has_next, float eps, float scale, uintptr_t ws,
+           size_t ws_bytes, uintptr_t stream) {
+            check(tv_loss_3d_slab_peer_cuda(&peers, seq, variant, flags, ptr<const float>(vol),
+                                            ptr<const float>(g), ptr<float>(acc), ptr<float>(grad),
+                                            B, Dp, H, W, d_lo, d_hi, has_prev, has_next, eps,
+                                            scale, ptr<void>(ws), ws_bytes, stream_of(stream)));
+        },
+        py::arg("peers"), py::arg("seq"), py::arg("variant"), py::arg("flags"), py::arg("vol_ptr"),
+        py::arg("g_ptr"), py::arg("acc_ptr"), py::arg("grad_ptr"), py::arg("B"), py::arg("Dp"),
+        py::arg("H"), py::arg("W"), py::arg("d_lo"), py::arg("d_hi"), py::arg("has_prev"),
+        py::arg("has_next"), py::arg("eps"), py::arg("acc_scale"), py::arg("ws_ptr"),
+        py::arg("ws_bytes"), py::arg("stream_ptr"));
 }

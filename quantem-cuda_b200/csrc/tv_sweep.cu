@@ -54,10 +54,12 @@
 namespace qc {
 namespace tv {
 
-// Set (bit 0) by a TMA-ring wait that gave up instead of hanging.
+// Set by a wait that gave up instead of hanging: QC_FAULT_TMA_WAIT by the
+// TMA ring, QC_FAULT_PEER_WAIT by a wait for another rank.
 __device__ unsigned int g_tv_fault_word = 0;
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per barrier wait
+constexpr uint64_t kWaitLimitNs = 2000000000ull;       // 2 s per barrier wait
+constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;  // default bound of a wait for another rank
 
 constexpr int kMaxPartials = 2048;  // CTA partial-sum slots in the workspace
 constexpr int kAccSlots = 3;        // L1 keeps one sum per axis
@@ -492,7 +494,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                     if (seq >= S) {
                         const uint32_t par = (uint32_t)(((seq / S) - 1) & 1);
                         if (!mbar_wait_bounded(&sm.empty[s], par, kWaitLimitNs)) {
-                            atomicOr(&g_tv_fault_word, 1u);
+                            atomicOr(&g_tv_fault_word, QC_FAULT_TMA_WAIT);
                             sm.abort = 1;
                             break;
                         }
@@ -511,7 +513,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                 if (last_seq[s] < 0) continue;
                 const uint32_t par = (uint32_t)((last_seq[s] / S) & 1);
                 if (!mbar_wait_bounded(&sm.full[s], par, kWaitLimitNs))
-                    atomicOr(&g_tv_fault_word, 1u);
+                    atomicOr(&g_tv_fault_word, QC_FAULT_TMA_WAIT);
             }
         }
     } else {
@@ -546,7 +548,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
 
             const int q0 = seq;
             if (!mbar_wait_bounded(&sm.full[q0 % S], (uint32_t)((q0 / S) & 1), kWaitLimitNs)) {
-                atomicOr(&g_tv_fault_word, 1u);
+                atomicOr(&g_tv_fault_word, QC_FAULT_TMA_WAIT);
                 sm.abort = 1;
             }
             if (aborted(sm)) break;
@@ -560,7 +562,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                     const int qn = qc + 1;
                     if (!mbar_wait_bounded(&sm.full[qn % S], (uint32_t)((qn / S) & 1),
                                            kWaitLimitNs)) {
-                        atomicOr(&g_tv_fault_word, 1u);
+                        atomicOr(&g_tv_fault_word, QC_FAULT_TMA_WAIT);
                         sm.abort = 1;
                     }
                     Sn = sm.stage[qn % S];
@@ -858,6 +860,110 @@ __global__ void __launch_bounds__(kFinThreads) tv_finalize_kernel(const double *
     }
 }
 
+// ── cross-rank flags over peer memory ─────────────────────────────────────
+//
+// One communication block per rank, in memory its peers have mapped. Flags
+// hold the sequence number of the last call that set them; a waiter compares
+// with >= so a flag that has moved on to a later call still releases it.
+// Data goes into a peer's block with plain stores, then (one thread per CTA,
+// after a CTA barrier and a system-scope fence) the flag is stored with
+// release semantics; the waiter loads it with acquire semantics.
+
+struct PeerComm {
+    unsigned long long ready[2];   // [s]: neighbour on side s (0 = rank-1, 1 = rank+1) lets
+                                   // this rank store into that neighbour's halo for the call
+    unsigned long long filled[2];  // [s]: neighbour on side s has filled this rank's halo s
+    unsigned int arrive;           // CTAs of this rank's exchange launch done storing
+    unsigned int pad0[7];
+    unsigned long long red_flag[QC_MAX_PEER_RANKS];   // [q]: rank q's total is in the slot
+    double partials[2][QC_MAX_PEER_RANKS][4];         // [call & 1][q][accumulator]
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ double ld_relaxed_sys_f64(const double *p) {
+    double v;
+    asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until *flag >= seq, for at most limit_ns. Returns false if it gave up.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned long long *flag, unsigned long long seq,
+                                              uint64_t limit_ns) {
+    if (ld_acquire_sys(flag) >= seq) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        __nanosleep(64);
+        if (ld_acquire_sys(flag) >= seq) return true;
+        if (global_timer_ns() - t0 > limit_ns) return false;
+    }
+}
+
+__device__ __forceinline__ uint64_t peer_limit(const qc_tv_peers &p) {
+    return p.timeout_ns ? p.timeout_ns : kPeerWaitLimitNs;
+}
+
+// The finalize of a D-sharded loss: the fixed-order total of this rank's CTA
+// partials goes into slot [seq & 1][rank] of every rank's block; after all
+// ranks' flags show `seq`, every rank adds the slots in rank order. A slot is
+// rewritten two calls later at the earliest, and a rank gets there only after
+// every rank has finished reading it (its own call seq+1 waited for all).
+__global__ void __launch_bounds__(kFinThreads) tv_finalize_peer_kernel(
+    const double *__restrict__ partials, int n_partials, int n_acc, float *__restrict__ acc,
+    float scale, int overwrite, qc_tv_peers peers, unsigned long long seq) {
+    griddep_wait();
+    __shared__ double red[kAccSlots][kFinThreads];
+    __shared__ int gave_up;
+    for (int a = 0; a < n_acc; ++a) {
+        double t = 0.0;
+        for (int i = threadIdx.x; i < n_partials; i += kFinThreads)
+            t += partials[(size_t)i * kAccSlots + a];
+        red[a][threadIdx.x] = t;
+    }
+    if (threadIdx.x == 0) gave_up = 0;
+    __syncthreads();
+    for (int s = kFinThreads / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s)
+            for (int a = 0; a < n_acc; ++a) red[a][threadIdx.x] += red[a][threadIdx.x + s];
+        __syncthreads();
+    }
+    const int slot = (int)(seq & 1ull);
+    if (threadIdx.x < n_acc) {
+        const double v = red[threadIdx.x][0];
+        for (int q = 0; q < peers.world; ++q)
+            static_cast<PeerComm *>(peers.comm[q])->partials[slot][peers.rank][threadIdx.x] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int q = 0; q < peers.world; ++q)
+            st_release_sys(&static_cast<PeerComm *>(peers.comm[q])->red_flag[peers.rank], seq);
+    }
+    PeerComm *self = static_cast<PeerComm *>(peers.comm[peers.rank]);
+    if (threadIdx.x < peers.world) {
+        if (!wait_flag_geq(&self->red_flag[threadIdx.x], seq, peer_limit(peers))) {
+            atomicOr(&gave_up, 1);
+            atomicOr(&g_tv_fault_word, QC_FAULT_PEER_WAIT);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < n_acc) {
+        double t = 0.0;
+        for (int q = 0; q < peers.world; ++q)
+            t += ld_relaxed_sys_f64(&self->partials[slot][q][threadIdx.x]);
+        const float v = gave_up ? __int_as_float(0x7fc00000) : (float)(t * (double)scale);
+        acc[threadIdx.x] = overwrite ? v : acc[threadIdx.x] + v;
+    }
+}
+
 // ── host side ────────────────────────────────────────────────────────────
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -1003,7 +1109,8 @@ size_t workspace_bytes() { return (size_t)kMaxPartials * kAccSlots * sizeof(doub
 
 int run(int variant, int flags, const float *vol, const float *g, float *acc, float *grad, int B,
         int Dp, int H, int W, int d_lo, int d_hi, int has_prev, int has_next, float eps,
-        float acc_scale, void *ws, size_t ws_bytes, cudaStream_t stream) {
+        float acc_scale, void *ws, size_t ws_bytes, cudaStream_t stream,
+        const qc_tv_peers *peers = nullptr, unsigned long long seq = 0) {
     const bool want_loss = flags & QC_TV_LOSS, want_grad = flags & QC_TV_GRAD;
     QC_RETURN_IF(variant < QC_TV_SQ || variant > QC_TV_L1, QC_ERR_INVALID_ARGUMENT,
                  "tv: unknown variant %d", variant);
@@ -1033,7 +1140,7 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     }
     QC_RETURN_IF(!empty && vol == nullptr, QC_ERR_INVALID_ARGUMENT, "tv: null volume");
 
-    if (empty) {
+    if (empty && peers == nullptr) {
         if (want_loss && (flags & QC_TV_ACC_OVERWRITE))
             QC_CUDA_TRY(cudaMemsetAsync(acc, 0, n_acc * sizeof(float), stream), "cudaMemsetAsync(acc)");
         return 0;
@@ -1058,7 +1165,9 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     double *partials = reinterpret_cast<double *>(ws);
     int grid = 0;
     int st = 0;
-    switch (variant) {
+    if (empty) {
+        // a rank that owns no planes still takes part in the cross-rank sum
+    } else switch (variant) {
         case QC_TV_SQ: st = dispatch_mode<QC_TV_SQ>(flags, use_tma, vol, g, grad, partials, pl, &grid, stream); break;
         case QC_TV_ISO: st = dispatch_mode<QC_TV_ISO>(flags, use_tma, vol, g, grad, partials, pl, &grid, stream); break;
         default: st = dispatch_mode<QC_TV_L1>(flags, use_tma, vol, g, grad, partials, pl, &grid, stream); break;
@@ -1076,9 +1185,17 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_kernel, (const double *)partials, grid, n_acc,
-                                       acc, acc_scale, (flags & QC_TV_ACC_OVERWRITE) ? 1 : 0),
-                    "tv_finalize_kernel launch");
+        if (peers != nullptr) {
+            QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_peer_kernel, (const double *)partials,
+                                           grid, n_acc, acc, acc_scale,
+                                           (flags & QC_TV_ACC_OVERWRITE) ? 1 : 0, *peers, seq),
+                        "tv_finalize_peer_kernel launch");
+        } else {
+            QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_kernel, (const double *)partials, grid,
+                                           n_acc, acc, acc_scale,
+                                           (flags & QC_TV_ACC_OVERWRITE) ? 1 : 0),
+                        "tv_finalize_kernel launch");
+        }
     }
     return 0;
 }
@@ -1232,3 +1349,147 @@ extern "C" int tv_loss_iso_3d_fwd_grad_noalloc_cuda(const float *d_vol, const fl
     return qc::tv::run(QC_TV_ISO, QC_TV_LOSS | QC_TV_GRAD, d_vol, d_g_scaled, d_acc, d_grad_vol, B,
                        D, H, W, 0, D, 0, 0, eps, 1.0f, scratch, have, stream);
 }
+
+// ── D-slabs over peer memory: halo exchange and the C ABI ─────────────────
+
+namespace qc {
+namespace tv {
+
+constexpr int kHaloThreads = 256;
+
+// Stores this rank's boundary planes into its neighbours' halos (plane 1 into
+// rank-1's plane prev_dp-1, plane Dp-2 into rank+1's plane 0) and waits for
+// theirs. Every CTA first tells both neighbours that this rank's halos may be
+// overwritten (everything earlier on this stream, the sweeps that read the
+// old halos included, has completed), then waits for the same word from the
+// neighbours it stores into, so no CTA depends on another CTA being resident.
+// The last CTA to finish storing raises the neighbours' `filled` flags and
+// waits for this rank's own.
+__global__ void __launch_bounds__(kHaloThreads) tv_halo_exchange_kernel(
+    qc_tv_peers peers, unsigned long long seq, const float *__restrict__ slab, int B, int Dp,
+    long long plane, int vec4) {
+    const bool has_prev = peers.rank > 0, has_next = peers.rank < peers.world - 1;
+    PeerComm *self = static_cast<PeerComm *>(peers.comm[peers.rank]);
+    PeerComm *prevc = has_prev ? static_cast<PeerComm *>(peers.comm[peers.rank - 1]) : nullptr;
+    PeerComm *nextc = has_next ? static_cast<PeerComm *>(peers.comm[peers.rank + 1]) : nullptr;
+    const uint64_t limit = peer_limit(peers);
+    __shared__ int go;
+    if (threadIdx.x == 0) {
+        if (has_prev) st_release_sys(&prevc->ready[1], seq);
+        if (has_next) st_release_sys(&nextc->ready[0], seq);
+        bool ok = true;
+        if (has_prev) ok = wait_flag_geq(&self->ready[0], seq, limit) && ok;
+        if (has_next) ok = wait_flag_geq(&self->ready[1], seq, limit) && ok;
+        if (!ok) atomicOr(&g_tv_fault_word, QC_FAULT_PEER_WAIT);
+        go = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (go) {
+        // work items: side (prev, next) × batch slice × plane elements (or float4s)
+        const long long per = vec4 ? plane / 4 : plane;
+        const long long per_side = (long long)B * per;
+        const long long n = per_side * 2;
+        const long long stride = (long long)gridDim.x * blockDim.x;
+        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+            const int side = i >= per_side;
+            if (side == 0 ? !has_prev : !has_next) continue;
+            const long long j = i - side * per_side;
+            const long long b = j / per, e = j - b * per;
+            const long long src_plane = (long long)b * Dp + (side == 0 ? 1 : Dp - 2);
+            const long long dst_plane = side == 0 ? (long long)b * peers.prev_dp + peers.prev_dp - 1
+                                                  : (long long)b * peers.next_dp;
+            float *dst = side == 0 ? peers.prev_slab : peers.next_slab;
+            if (vec4) {
+                const float4 v = ldg4(slab + src_plane * plane + e * 4);
+                *reinterpret_cast<float4 *>(dst + dst_plane * plane + e * 4) = v;
+            } else {
+                dst[dst_plane * plane + e] = __ldg(slab + src_plane * plane + e);
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const unsigned int before = atomicAdd(&self->arrive, 1u);
+        if (before == gridDim.x - 1) {
+            self->arrive = 0;  // the next exchange on this stream starts after this grid
+            __threadfence_system();
+            if (has_prev) st_release_sys(&prevc->filled[1], seq);
+            if (has_next) st_release_sys(&nextc->filled[0], seq);
+            bool ok = true;
+            if (has_prev) ok = wait_flag_geq(&self->filled[0], seq, limit) && ok;
+            if (has_next) ok = wait_flag_geq(&self->filled[1], seq, limit) && ok;
+            if (!ok) atomicOr(&g_tv_fault_word, QC_FAULT_PEER_WAIT);
+            // the sweeps read the halos with TMA (the async proxy)
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+    }
+}
+
+int check_peers(const qc_tv_peers *p, unsigned long long seq) {
+    QC_RETURN_IF(p == nullptr, QC_ERR_INVALID_ARGUMENT, "tv peers: null peers");
+    QC_RETURN_IF(p->world < 1 || p->world > QC_MAX_PEER_RANKS, QC_ERR_INVALID_ARGUMENT,
+                 "tv peers: world %d outside [1, %d]", p->world, QC_MAX_PEER_RANKS);
+    QC_RETURN_IF(p->rank < 0 || p->rank >= p->world, QC_ERR_INVALID_ARGUMENT,
+                 "tv peers: rank %d outside [0, %d)", p->rank, p->world);
+    QC_RETURN_IF(seq == 0, QC_ERR_INVALID_ARGUMENT, "tv peers: seq starts at 1");
+    for (int q = 0; q < p->world; ++q)
+        QC_RETURN_IF(p->comm[q] == nullptr, QC_ERR_INVALID_ARGUMENT,
+                     "tv peers: null communication block of rank %d", q);
+    return 0;
+}
+
+}  // namespace tv
+}  // namespace qc
+
+extern "C" {
+
+size_t tv_peer_comm_bytes(void) { return sizeof(qc::tv::PeerComm); }
+
+int tv_slab_halo_exchange_cuda(const qc_tv_peers *peers, unsigned long long seq, float *d_slab,
+                               int B, int Dp, int H, int W, cudaStream_t stream) {
+    using namespace qc::tv;
+    if (int st = check_peers(peers, seq)) return st;
+    const bool has_prev = peers->rank > 0, has_next = peers->rank < peers->world - 1;
+    QC_RETURN_IF(B < 0 || H < 0 || W < 0, QC_ERR_INVALID_ARGUMENT,
+                 "tv_slab_halo_exchange_cuda: negative shape");
+    QC_RETURN_IF(Dp < 3, QC_ERR_INVALID_ARGUMENT,
+                 "tv_slab_halo_exchange_cuda: a slab needs a halo on each side and an owned "
+                 "plane (Dp = %d)", Dp);
+    QC_RETURN_IF(has_prev && (peers->prev_slab == nullptr || peers->prev_dp < 3),
+                 QC_ERR_INVALID_ARGUMENT, "tv_slab_halo_exchange_cuda: rank-1's slab missing");
+    QC_RETURN_IF(has_next && (peers->next_slab == nullptr || peers->next_dp < 3),
+                 QC_ERR_INVALID_ARGUMENT, "tv_slab_halo_exchange_cuda: rank+1's slab missing");
+    QC_RETURN_IF(d_slab == nullptr, QC_ERR_INVALID_ARGUMENT, "tv_slab_halo_exchange_cuda: null slab");
+    if (peers->world == 1) return 0;
+    const long long plane = (long long)H * W;
+    const bool vec4 = plane % 4 == 0 && reinterpret_cast<uintptr_t>(d_slab) % 16 == 0 &&
+                      (!has_prev || reinterpret_cast<uintptr_t>(peers->prev_slab) % 16 == 0) &&
+                      (!has_next || reinterpret_cast<uintptr_t>(peers->next_slab) % 16 == 0);
+    const long long items = 2LL * B * (vec4 ? plane / 4 : plane);
+    int sms = 0;
+    if (int st = qc::device_sm_count(&sms)) return st;
+    long long grid = (items + kHaloThreads - 1) / kHaloThreads;
+    if (grid > 2LL * sms) grid = 2LL * sms;
+    if (grid < 1) grid = 1;
+    tv_halo_exchange_kernel<<<(unsigned)grid, kHaloThreads, 0, stream>>>(*peers, seq, d_slab, B, Dp,
+                                                                          plane, vec4 ? 1 : 0);
+    QC_CHECK_LAUNCH("tv_halo_exchange_kernel launch");
+    return 0;
+}
+
+int tv_loss_3d_slab_peer_cuda(const qc_tv_peers *peers, unsigned long long seq, int variant,
+                              int flags, const float *d_vol, const float *d_g, float *d_acc,
+                              float *d_grad_vol, int B, int Dp, int H, int W, int d_lo, int d_hi,
+                              int has_prev, int has_next, float eps, float acc_scale,
+                              void *d_workspace, size_t workspace_bytes, cudaStream_t stream) {
+    using namespace qc::tv;
+    if (int st = check_peers(peers, seq)) return st;
+    QC_RETURN_IF(!(flags & QC_TV_LOSS), QC_ERR_INVALID_ARGUMENT,
+                 "tv_loss_3d_slab_peer_cuda: flags must include QC_TV_LOSS (use "
+                 "tv_loss_3d_slab_cuda for the gradient alone)");
+    return run(variant, flags, d_vol, d_g, d_acc, d_grad_vol, B, Dp, H, W, d_lo, d_hi, has_prev,
+               has_next, eps, acc_scale, d_workspace, workspace_bytes, stream, peers, seq);
+}
+
+}  // extern "C"

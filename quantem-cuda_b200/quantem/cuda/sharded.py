@@ -6,11 +6,20 @@ natural sharding of the work:
 
 * TV over D-slabs. Each rank owns a contiguous range of planes of every batch
   slice, stored with one halo plane on each side: ``slab [B, D_local + 2, H, W]``
-  (planes 1..D_local owned). :func:`exchange_halos` fills the halo planes from
-  the neighbouring ranks; the single-sweep kernel then computes the loss terms
-  anchored at owned planes and the gradient of owned planes
-  (``tv_loss_3d_slab_cuda``). The per-rank sums are all-gathered and added in
-  rank order, so the total is deterministic and identical on every rank.
+  (planes 1..D_local owned). The halo planes are filled from the neighbouring
+  ranks; the single-sweep kernel then computes the loss terms anchored at
+  owned planes and the gradient of owned planes (``tv_loss_3d_slab_cuda``).
+  The per-rank sums are added in rank order, so the total is deterministic
+  and identical on every rank. Two transports:
+
+  - :class:`PeerSlab` (GPUs of one node): the slab and a small flag block
+    live in memory mapped into the neighbours with CUDA IPC. A kernel stores
+    the boundary planes straight into the neighbours' halos over NVLink, and
+    the loss's finalize kernel stores each rank's fp64 total into every rank
+    and adds them in rank order; a step is kernels only, with no library
+    collective and no host synchronisation.
+  - :func:`exchange_halos` + :func:`tv_loss_slab_fwd_grad`: any
+    torch.distributed backend (NCCL send/recv and all_gather, or gloo on CPU).
 
 * K-Planes over points. Each rank evaluates its own points against the
   replicated planes and rotations; point gradients stay local, and the plane
@@ -23,6 +32,7 @@ on CPU ranks with the CPU oracle in place of the device kernel.
 
 from __future__ import annotations
 
+import weakref
 from typing import Callable
 
 import torch
@@ -166,21 +176,27 @@ def kplanes_fwd_bwd_sharded(
     level's compute overlaps it; call ``work.wait()`` before reading them).
     ``fwd_bwd(pts, rotations, plane, grad_out) -> (out, g_pts, g_rot, g_plane)``
     replaces the CUDA ops (host-logic tests on CPU ranks).
-    """
-    if fwd_bwd is None:
-        from quantem.cuda.core.ml._ops import _kplanes_tilted_fuse, _kplanes_tilted_fuse_bwd
 
-        out = _kplanes_tilted_fuse(pts_local, rotations, plane)
-        g_pts, g_rot, g_plane = _kplanes_tilted_fuse_bwd(pts_local, rotations, plane, grad_out_local)
-    else:
-        out, g_pts, g_rot, g_plane = fwd_bwd(pts_local, rotations, plane, grad_out_local)
-    work = None
+    On CUDA the planes are converted to channels-last once for both passes, and
+    the backward runs one rotation at a time: each rotation's three plane
+    gradients are put back in the parameter's layout and their all_reduce is
+    enqueued at once, so it runs on NCCL's stream while the next rotation's
+    backward computes, and only the last rotation's reduction is exposed.
+    """
     _, world = _rank_world(group)
-    if world > 1:
-        works = [
-            dist.all_reduce(g_plane, group=group, async_op=True),
-            dist.all_reduce(g_rot, group=group, async_op=True),
-        ]
+    if fwd_bwd is not None:
+        out, g_pts, g_rot, g_plane = fwd_bwd(pts_local, rotations, plane, grad_out_local)
+        works = []
+        if world > 1:
+            works = [
+                dist.all_reduce(g_plane, group=group, async_op=True),
+                dist.all_reduce(g_rot, group=group, async_op=True),
+            ]
+    else:
+        out, g_pts, g_rot, g_plane, works = _kplanes_fwd_bwd_bucketed(
+            pts_local, rotations, plane, grad_out_local, group, world)
+    work = None
+    if works:
 
         class _Pending:
             def wait(self):
@@ -192,3 +208,202 @@ def kplanes_fwd_bwd_sharded(
             work.wait()
             work = None
     return out, g_pts, g_rot, g_plane, work
+
+
+def _kplanes_fwd_bwd_bucketed(pts, rotations, plane, grad_out, group, world):
+    from quantem.cuda import _core
+    from quantem.cuda.core.ml._ops import _channels_last
+
+    dev = pts.device
+    p = pts.contiguous()
+    r = rotations.contiguous()
+    t_count = r.shape[0]
+    c, h, w = plane.shape[1:]
+    n = p.shape[0]
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    works = []
+    with torch.cuda.device(dev):
+        g = _channels_last(plane, stream)
+        out = torch.empty((n, t_count * c), dtype=torch.float32, device=dev)
+        _core.kplanes_tilted_fuse_cuda(p.data_ptr(), r.data_ptr(), g.data_ptr(), out.data_ptr(),
+                                       n, t_count, c, h, w, stream)
+        gout = grad_out.detach().to(dtype=torch.float32, device=dev).contiguous()
+        g_pts = torch.zeros_like(p)
+        g_rot = torch.zeros_like(r)
+        g_cl = torch.zeros(g.shape, dtype=torch.float32, device=dev)
+        keep_cl = plane.permute(0, 2, 3, 1).is_contiguous()
+        g_plane = g_cl.permute(0, 3, 1, 2) if keep_cl else torch.empty(
+            (3 * t_count, c, h, w), dtype=torch.float32, device=dev)
+        for t in range(t_count):
+            _core.kplanes_tilted_fuse_grad_rotations_cuda(
+                p.data_ptr(), r.data_ptr(), g.data_ptr(), gout.data_ptr(), g_cl.data_ptr(),
+                g_rot.data_ptr(), g_pts.data_ptr(), n, t_count, c, h, w, t, t + 1, stream)
+            if keep_cl:
+                bucket = g_cl[3 * t : 3 * t + 3]
+            else:
+                bucket = g_plane[3 * t : 3 * t + 3]
+                _core.kplanes_planes_from_channels_last_cuda(g_cl[3 * t].data_ptr(), bucket.data_ptr(),
+                                                             3, c, h, w, stream)
+            if world > 1:
+                works.append(dist.all_reduce(bucket, group=group, async_op=True))
+        if world > 1:
+            works.append(dist.all_reduce(g_rot, group=group, async_op=True))
+    return out, g_pts, g_rot, g_plane, works
+
+
+# ── D-slabs over peer memory ────────────────────────────────────────────────
+
+
+class _PeerAllocation:
+    """One ``quantem_cuda_peer_alloc`` allocation (zero-filled, IPC-exportable),
+    viewable as a torch tensor through ``__cuda_array_interface__``; freed when
+    the last tensor viewing it is gone."""
+
+    def __init__(self, shape: tuple[int, ...], typestr: str, itemsize: int, device: torch.device):
+        from quantem.cuda import _core
+
+        n = 1
+        for d in shape:
+            n *= int(d)
+        self.device = device
+        with torch.cuda.device(device):
+            self.ptr = int(_core.peer_alloc(max(1, n * itemsize)))
+        self.__cuda_array_interface__ = {
+            "shape": tuple(int(d) for d in shape),
+            "typestr": typestr,
+            "data": (self.ptr, False),
+            "version": 3,
+            "strides": None,
+            "stream": None,
+        }
+        self._finalizer = weakref.finalize(self, _free_peer, self.ptr, device)
+
+
+def _free_peer(ptr: int, device: torch.device) -> None:
+    from quantem.cuda import _core
+
+    with torch.cuda.device(device):
+        _core.peer_free(ptr)
+
+
+class PeerSlab:
+    """This rank's D-slab of a ``[B, global_d, H, W]`` volume, with its halo
+    planes and loss sums exchanged over peer memory (CUDA IPC on the GPUs of
+    one node, stores over NVLink).
+
+    ``slab`` is ``[B, D_local + 2, H, W]``; write the owned planes
+    (``owned``, global planes ``d_lo..d_hi-1``) and call :meth:`fwd_grad`.
+    Every rank of ``group`` must construct it together and make the same calls
+    in the same order, on one stream per rank. A wait for another rank gives
+    up after ``timeout_s`` (the loss becomes NaN and the device fault word
+    gets ``FAULT_PEER_WAIT``) instead of hanging.
+    """
+
+    def __init__(self, batch: int, global_d: int, height: int, width: int, group=None,
+                 device: torch.device | None = None, timeout_s: float = 10.0):
+        from quantem.cuda import _core
+
+        rank, world = _rank_world(group)
+        if world > _core.MAX_PEER_RANKS:
+            raise ValueError(f"PeerSlab supports at most {_core.MAX_PEER_RANKS} ranks, got {world}")
+        lo, hi = slab_bounds(global_d, rank, world)
+        if hi - lo < 1:
+            raise ValueError(f"global_d={global_d} leaves rank {rank} of {world} without planes")
+        self.group, self.rank, self.world = group, rank, world
+        self.global_d, self.d_lo, self.d_hi = global_d, lo, hi
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        dp = hi - lo + 2
+        self.shape = (batch, dp, height, width)
+        self._slab_mem = _PeerAllocation(self.shape, "<f4", 4, self.device)
+        self._comm_mem = _PeerAllocation((int(_core.tv_peer_comm_bytes()),), "|u1", 1, self.device)
+        self.slab = torch.as_tensor(self._slab_mem, device=self.device)
+        with torch.cuda.device(self.device):
+            mine = (rank, dp, _core.ipc_handle(self._slab_mem.ptr), _core.ipc_handle(self._comm_mem.ptr))
+        infos = [None] * world
+        dist.all_gather_object(infos, mine, group=group)
+        self._mapped: list[int] = []
+        comm, prev_ptr, prev_dp, next_ptr, next_dp = [], 0, 0, 0, 0
+        with torch.cuda.device(self.device):
+            for q, (_, dq, slab_h, comm_h) in enumerate(infos):
+                if q == rank:
+                    comm.append(self._comm_mem.ptr)
+                    continue
+                c = int(_core.ipc_open(comm_h))
+                self._mapped.append(c)
+                comm.append(c)
+                if q == rank - 1 or q == rank + 1:
+                    sp = int(_core.ipc_open(slab_h))
+                    self._mapped.append(sp)
+                    if q == rank - 1:
+                        prev_ptr, prev_dp = sp, dq
+                    else:
+                        next_ptr, next_dp = sp, dq
+        self._peers = _core.TvPeers(rank, world, int(timeout_s * 1e9), comm, prev_ptr, prev_dp,
+                                    next_ptr, next_dp)
+        from quantem.cuda._common import _workspace
+
+        self._ws = _workspace(self.device)
+        self._halo_seq = 0
+        self._red_seq = 0
+        dist.barrier(group=group)
+
+    @property
+    def owned(self) -> Tensor:
+        """The owned planes, ``slab[:, 1:-1]`` (a view)."""
+        return self.slab[:, 1:-1]
+
+    def exchange_halos(self) -> None:
+        """Fills the halo planes from the neighbours (kernel on the current
+        stream; returns at once)."""
+        from quantem.cuda import _core
+
+        self._halo_seq += 1
+        b, dp, h, w = self.shape
+        with torch.cuda.device(self.device):
+            _core.tv_slab_halo_exchange_cuda(self._peers, self._halo_seq, self._slab_mem.ptr, b, dp, h, w,
+                                             torch.cuda.current_stream(self.device).cuda_stream)
+
+    def fwd_grad(self, variant: int, grad_out: Tensor, eps: float = 1e-8, grad: Tensor | None = None,
+                 exchange: bool = True) -> tuple[Tensor, Tensor]:
+        """Global loss and this rank's gradient for one TV variant (the same
+        contract as :func:`tv_loss_slab_fwd_grad`). ``grad`` (``slab``'s shape)
+        is written if given; its owned planes receive the gradient."""
+        from quantem.cuda import _core
+
+        if exchange:
+            self.exchange_halos()
+        b, dp, h, w = self.shape
+        scale = 1.0
+        if variant == ISO:
+            scale = 1.0 / max(1, b * (self.global_d - 1) * (h - 1) * (w - 1))
+        if grad is None:
+            grad = torch.empty(self.shape, dtype=torch.float32, device=self.device)
+        elif tuple(grad.shape) != self.shape or not grad.is_contiguous() or grad.dtype != torch.float32:
+            raise ValueError(f"grad must be a contiguous fp32 tensor of shape {self.shape}")
+        g = grad_out.to(device=self.device, dtype=torch.float32).contiguous()
+        if g.numel() != _N_ACC[variant]:
+            raise ValueError(f"grad_out needs {_N_ACC[variant]} element(s), got {g.numel()}")
+        acc = torch.empty(_N_ACC[variant], dtype=torch.float32, device=self.device)
+        self._red_seq += 1
+        with torch.cuda.device(self.device):
+            _core.tv_loss_3d_slab_peer_cuda(
+                self._peers, self._red_seq, variant, _LOSS | _GRAD | _OVERWRITE, self._slab_mem.ptr,
+                g.data_ptr(), acc.data_ptr(), grad.data_ptr(), b, dp, h, w, 1, dp - 1,
+                int(self.rank > 0), int(self.rank < self.world - 1), float(eps), float(scale),
+                self._ws.data_ptr(), self._ws.numel(), torch.cuda.current_stream(self.device).cuda_stream)
+        return (acc.squeeze(0) if variant != L1 else acc), grad
+
+    def close(self) -> None:
+        """Unmaps the peers' memory after every rank has finished with it.
+        Collective: every rank calls it."""
+        from quantem.cuda import _core
+
+        if self._mapped is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._mapped:
+                _core.ipc_close(p)
+        self._mapped = None
+        dist.barrier(group=self.group)

@@ -95,3 +95,25 @@ def test_core_binding_has_reference_names():
     assert int(_core.__cudart_version__) >= 12000
     with pytest.raises(RuntimeError, match="QC_ERR_INVALID_ARGUMENT"):
         _core.tv_loss_3d_slab_cuda(9, 1, 0, 0, 0, 0, 1, 2, 2, 2, 0, 2, 0, 0, 0.0, 1.0, 0, 0, 0)
+
+
+def test_peer_entries_reject_bad_arguments_without_a_device():
+    from quantem.cuda import _core
+
+    with pytest.raises(ValueError):
+        _core.TvPeers(0, _core.MAX_PEER_RANKS + 1, 0, [1] * (_core.MAX_PEER_RANKS + 1), 0, 0, 0, 0)
+    with pytest.raises(ValueError):
+        _core.TvPeers(0, 2, 0, [1], 0, 0, 0, 0)  # one block per rank
+    good = _core.TvPeers(0, 2, 0, [16, 32], 0, 0, 64, 5)
+    with pytest.raises(RuntimeError, match="seq starts at 1"):
+        _core.tv_slab_halo_exchange_cuda(good, 0, 128, 1, 5, 4, 4, 0)
+    with pytest.raises(RuntimeError, match="null communication block"):
+        _core.tv_slab_halo_exchange_cuda(_core.TvPeers(0, 2, 0, [16, 0], 0, 0, 64, 5), 1, 128, 1, 5, 4, 4, 0)
+    with pytest.raises(RuntimeError, match="rank 2 outside"):
+        _core.tv_slab_halo_exchange_cuda(_core.TvPeers(2, 2, 0, [16, 32], 0, 0, 0, 0), 1, 128, 1, 5, 4, 4, 0)
+    with pytest.raises(RuntimeError, match="rank\\+1's slab missing"):
+        _core.tv_slab_halo_exchange_cuda(_core.TvPeers(0, 2, 0, [16, 32], 0, 0, 0, 0), 1, 128, 1, 5, 4, 4, 0)
+    with pytest.raises(RuntimeError, match="must include QC_TV_LOSS"):
+        _core.tv_loss_3d_slab_peer_cuda(good, 1, _core.TV_SQ, _core.TV_GRAD, 128, 0, 0, 256, 1, 5, 4, 4, 1, 4,
+                                        0, 1, 0.0, 1.0, 0, 0, 0)
+    assert _core.tv_peer_comm_bytes() >= 8 * 2 * 4 * 8

@@ -271,3 +271,37 @@ def test_plane_layout_transposes(shape):
     back = torch.empty_like(x)
     _core.kplanes_planes_from_channels_last_cuda(cl.data_ptr(), back.data_ptr(), P, C, H, W, st)
     assert torch.equal(back, x)
+
+
+@pytest.mark.parametrize("cfg", [(2000, 4, 32, 50, 33), (500, 3, 5, 9, 7), (300, 2, 16, 16, 16)])
+@pytest.mark.parametrize("channels_last", [False, True])
+def test_per_rotation_backward_matches_whole_backward(cfg, channels_last):
+    """The multi-GPU path's per-rotation backward (one launch per rotation of
+    kplanes_tilted_fuse_grad_rotations_cuda, each rotation's plane gradient put
+    back in the parameter's layout at once) against the op on all rotations."""
+    from quantem.cuda import sharded
+
+    N, T, C, H, W = cfg
+    pts, rot, plane, up = make_inputs(N, T, C, H, W, seed=41)
+    p, r, u = pts.cuda(), rot.cuda(), up.cuda()
+    g = plane.cuda()
+    if channels_last:
+        g = g.contiguous(memory_format=torch.channels_last)
+    out, g_pts, g_rot, g_plane, works = sharded._kplanes_fwd_bwd_bucketed(p, r, g, u, None, 1)
+    assert works == []
+    ref_out = torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, g)
+    ref_pts, ref_rot, ref_plane = torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, g, u)
+    assert torch.equal(out, ref_out)
+    # plane and rotation gradients are accumulated in the same order per
+    # rotation; the point gradient sums the rotations in another order
+    torch.testing.assert_close(g_plane, ref_plane, rtol=1e-5, atol=1e-6 * ref_plane.abs().max().item())
+    torch.testing.assert_close(g_rot, ref_rot, rtol=1e-4, atol=1e-5 * ref_rot.abs().max().item())
+    torch.testing.assert_close(g_pts, ref_pts, rtol=1e-4, atol=1e-5 * ref_pts.abs().max().item())
+    assert g_plane.stride() == ref_plane.stride()
+
+
+def test_rotation_range_validation():
+    z = torch.zeros(16, device="cuda")
+    with pytest.raises(RuntimeError, match="rotations \\[2, 5\\) outside \\[0, 4\\)"):
+        _core.kplanes_tilted_fuse_grad_rotations_cuda(*(z.data_ptr(),) * 7, 1, 4, 4, 2, 2, 2, 5,
+                                                     torch.cuda.current_stream().cuda_stream)

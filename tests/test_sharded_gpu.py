@@ -82,3 +82,145 @@ def test_dslab_over_nccl_matches_single_gpu():
             r_loss, r_grad = out[variant]
             np.testing.assert_allclose(np.atleast_1d(r_loss), np.atleast_1d(loss), rtol=1e-5)
             np.testing.assert_allclose(r_grad, grad[:, lo:hi], rtol=1e-5, atol=1e-6 * np.abs(grad).max())
+
+
+# ── D-slabs over peer memory (CUDA IPC, stores over NVLink) ──────────────────
+
+PEER_SHAPE = (2, 45, 40, 132)  # D split 23 + 22: slabs of different depth
+PEER_STEPS = 3
+PEER_CASES = ((0, [1.5], 0.0), (1, [0.75], 1e-6), (2, [0.3, 1.1, 0.6], 0.0))  # SQ, ISO, L1
+
+
+def _peer_volume(step: int):
+    gen = torch.Generator().manual_seed(100 + step)
+    return torch.rand(PEER_SHAPE, generator=gen)
+
+
+def _peer_worker(rank, world, port, queue):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ps = None
+    try:
+        from quantem.cuda import _core, sharded
+
+        B, D, H, W = PEER_SHAPE
+        ps = sharded.PeerSlab(B, D, H, W, timeout_s=20.0)
+        lo, hi = ps.d_lo, ps.d_hi
+        out = []
+        for step in range(PEER_STEPS):
+            # the volume changes between steps, so stale halos would show
+            ps.owned.copy_(_peer_volume(step)[:, lo:hi].cuda())
+            per = {}
+            for variant, g, eps in PEER_CASES:
+                loss, grad = ps.fwd_grad(variant, torch.tensor(g), eps)
+                per[variant] = (loss.cpu().numpy(), grad[:, 1:-1].cpu().numpy())
+            out.append(per)
+        fault = _core.device_fault_word(rank)
+        queue.put((rank, lo, hi, out, fault))
+        ps.close()
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_slab_matches_single_gpu_over_steps():
+    from quantem.cuda.core import tv_loss_iso_3d_fwd_grad, tv_loss_l1_3d_fwd_grad, tv_loss_sq_3d_fwd_grad
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=240) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, _, _, _, fault in res:
+        assert fault == 0, f"rank {rank} gave up waiting (fault word {fault:#x})"
+    fns = {0: tv_loss_sq_3d_fwd_grad, 1: tv_loss_iso_3d_fwd_grad, 2: tv_loss_l1_3d_fwd_grad}
+    for step in range(PEER_STEPS):
+        v = _peer_volume(step).cuda()
+        for variant, g, eps in PEER_CASES:
+            kw = {"eps": eps} if variant == 1 else {}
+            loss, grad = fns[variant](v, g[0] if len(g) == 1 else tuple(g), **kw)
+            loss, grad = np.atleast_1d(loss.cpu().numpy()), grad.cpu().numpy()
+            losses = []
+            for rank, lo, hi, out, _ in res:
+                r_loss, r_grad = out[step][variant]
+                losses.append(np.atleast_1d(r_loss))
+                np.testing.assert_allclose(np.atleast_1d(r_loss), loss, rtol=1e-5)
+                np.testing.assert_allclose(r_grad, grad[:, lo:hi], rtol=1e-5, atol=1e-6 * np.abs(grad).max())
+            # the rank-ordered sum gives every rank the same bits
+            assert all(np.array_equal(losses[0], x) for x in losses[1:])
+
+
+# ── K-Planes over points, per-rotation gradient all_reduce ───────────────────
+
+KP_CFG = (6000, 4, 32, 40, 36)  # N, T, C, H, W
+
+
+def _kp_inputs():
+    N, T, C, H, W = KP_CFG
+    gen = torch.Generator().manual_seed(77)
+    pts = torch.empty((N, 3)).uniform_(-1.1, 1.1, generator=gen)
+    rot = torch.empty((T, 3, 3)).uniform_(-1.0, 1.0, generator=gen)
+    plane = torch.empty((3 * T, C, H, W)).uniform_(0.1, 0.5, generator=gen)
+    up = torch.randn((N, T * C), generator=gen)
+    return pts, rot, plane, up
+
+
+def _kp_worker(rank, world, port, queue):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from quantem.cuda import sharded
+
+        pts, rot, plane, up = _kp_inputs()
+        lo, hi = sharded.slab_bounds(pts.shape[0], rank, world)
+        out, g_pts, g_rot, g_plane, work = sharded.kplanes_fwd_bwd_sharded(
+            pts[lo:hi].cuda(), rot.cuda(), plane.cuda(), up[lo:hi].cuda(), async_op=True)
+        work.wait()
+        queue.put((rank, lo, hi, out.cpu(), g_pts.cpu(), g_rot.cpu(), g_plane.cpu()))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_kplanes_point_sharding_matches_single_gpu():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_kp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=240) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    pts, rot, plane, up = (t.cuda() for t in _kp_inputs())
+    out = torch.ops.quantem_cuda.kplanes_tilted_fuse(pts, rot, plane).cpu()
+    ref_pts, ref_rot, ref_plane = (t.cpu() for t in torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(pts, rot, plane, up))
+    for rank, lo, hi, r_out, r_pts, r_rot, r_plane in res:
+        assert torch.equal(r_out, out[lo:hi])
+        torch.testing.assert_close(r_pts, ref_pts[lo:hi], rtol=1e-4, atol=1e-5 * ref_pts.abs().max().item())
+        torch.testing.assert_close(r_rot, ref_rot, rtol=1e-4, atol=1e-4 * ref_rot.abs().max().item())
+        torch.testing.assert_close(r_plane, ref_plane, rtol=1e-4, atol=1e-5 * ref_plane.abs().max().item())
+    # the all_reduce gives every rank the same gradients
+    assert torch.equal(res[0][5], res[1][5]) and torch.equal(res[0][6], res[1][6])
