@@ -399,12 +399,12 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
         ps.owned.copy_(vol_cpu.to(dev))
         slab = ps.slab
         grads = [torch.empty_like(slab), torch.empty_like(slab)]
-        iso = t_iso.wrap(lambda: ps.fwd_grad(sharded.ISO, g1, 1e-8, grad=grads[0], exchange=False))
+        # the iso sweep exchanges the halos itself; the L1 sweep reuses them
+        iso = t_iso.wrap(lambda: ps.fwd_grad(sharded.ISO, g1, 1e-8, grad=grads[0], exchange=True))
         l1 = t_l1.wrap(lambda: ps.fwd_grad(sharded.L1, g3, grad=grads[1], exchange=False))
-        launches_per_step = 5  # halo exchange, two sweeps, two cross-rank finalize kernels
+        launches_per_step = 4  # two sweeps, two cross-rank finalize kernels
 
         def step():
-            ps.exchange_halos()
             iso()
             l1()
 
@@ -595,9 +595,10 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
             fwd()
             bwd()
     else:
-        # per-rotation backward with each rotation's plane-gradient all_reduce
-        # overlapping the next rotation's backward
-        fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u))
+        # one channels-last copy of the planes for both passes, one backward
+        # launch, then the plane- and rotation-gradient all_reduce
+        # (--kp-buckets > 1 overlaps per-bucket all_reduces with the backward)
+        fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u, buckets=ctx.args.kp_buckets))
 
         def step():
             fb()
@@ -641,9 +642,10 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         "value": N * ctx.world / (ms_step / 1e3),
         "unit": "points/s",
         "ms_per_step": ms_step,
-        "gpu_launches": (7 if ctx.world == 1 else 2 + 2 * T) * steps,
+        "gpu_launches": (5 if ctx.world == 1 else 2 + 2 * min(max(ctx.args.kp_buckets, 1), T)) * steps,
         "config": {"workload": DESCRIPTIONS["kplanes"],
-                   "points_per_gpu": N, "parallelism": f"points{ctx.world}" if ctx.world > 1 else "single GPU",
+                   "points_per_gpu": N,
+                   "parallelism": f"points{ctx.world} (gradient buckets {ctx.args.kp_buckets})" if ctx.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (512 MiB output + 512 MiB upstream gradient per step)",
                    "fwd_op_ms": f_ms, "bwd_op_ms": b_ms},
         "roofline": {"bound": "hbm",
@@ -709,6 +711,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tv_iso_l1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kp-buckets", type=int, default=1,
+                    help="multi-GPU K-Planes: backward launches whose gradient all_reduce overlaps the next")
     ap.add_argument("--tv-transport", choices=("peer", "nccl"), default="peer",
                     help="multi-GPU TV: halos and loss sums over peer memory, or NCCL send/recv + all_gather")
     args = ap.parse_args()
@@ -725,6 +729,10 @@ def main() -> None:
         return
 
     if ctx.world > 1:
+        # NCCL's version banner (NCCL_DEBUG=VERSION) would land on stdout next
+        # to the one JSON line this script prints
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(ctx.local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", ctx.local_rank))

@@ -212,12 +212,19 @@ int tv_slab_halo_exchange_cuda(const qc_tv_peers *peers, unsigned long long seq,
 /* tv_loss_3d_slab_cuda with the loss summed over all ranks inside the
  * finalize kernel: each rank's fixed-order fp64 total goes to every rank's
  * communication block, and every rank adds the totals in rank order, so d_acc
- * holds the same bits on every rank. flags must include QC_TV_LOSS. */
-int tv_loss_3d_slab_peer_cuda(const qc_tv_peers *peers, unsigned long long seq, int variant,
-                              int flags, const float *d_vol, const float *d_g, float *d_acc,
-                              float *d_grad_vol, int B, int Dp, int H, int W, int d_lo, int d_hi,
-                              int has_prev, int has_next, float eps, float acc_scale,
-                              void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+ * holds the same bits on every rank. flags must include QC_TV_LOSS; `seq`
+ * numbers the reductions. If halo_seq != 0 the call first exchanges the halos
+ * (what tv_slab_halo_exchange_cuda does with that sequence number; d_vol is
+ * then this rank's slab with owned planes [1, Dp-1)): on the TMA path the
+ * sweep kernel itself stores the boundary planes into the neighbours at its
+ * start and waits for each halo plane just before it loads it, so the
+ * exchange costs no separate launch and overlaps the interior of the sweep. */
+int tv_loss_3d_slab_peer_cuda(const qc_tv_peers *peers, unsigned long long halo_seq,
+                              unsigned long long seq, int variant, int flags, const float *d_vol,
+                              const float *d_g, float *d_acc, float *d_grad_vol, int B, int Dp,
+                              int H, int W, int d_lo, int d_hi, int has_prev, int has_next,
+                              float eps, float acc_scale, void *d_workspace,
+                              size_t workspace_bytes, cudaStream_t stream);
 
 /* ── tilted K-Planes ────────────────────────────────────────────────────── */
 
@@ -249,6 +256,25 @@ int kplanes_tilted_fuse_grad_rotations_cuda(const float *d_pts, const float *d_R
                                             float *d_ggrid, float *d_gR, float *d_gpts, long B,
                                             int T, int C, int H, int W, int t_begin, int t_end,
                                             cudaStream_t stream);
+
+/* Tilted K-Planes at four taps for finite-difference TV regularisation:
+ * out[k, b, t*C + c] samples at R_t·p (k = 0, bit-identical to
+ * kplanes_tilted_fuse_cuda) and at R_t·p + h·R_t[:, k-1] (k = 1, 2, 3); out is
+ * [4, N, T*C], fully written. Replaces kplanes_tilted_tv_fuse_cuda (reference
+ * csrc/ops/core/ml.h:51-62, csrc/cuda/core/ml/kplanes_tilted.cu:329-425). */
+int kplanes_tilted_tv_fuse_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                                float *d_out, long B, int T, int C, int H, int W, float h,
+                                cudaStream_t stream);
+
+/* Backward of the four-tap form: gout is [4, N, T*C]; ggrid, gR and gpts are
+ * accumulated into as in kplanes_tilted_fuse_grad_cuda. R_t receives both the
+ * R_t·p term of every tap and, for taps 1..3, h·dL/dr in column k-1. Replaces
+ * kplanes_tilted_tv_fuse_grad_cuda (reference csrc/ops/core/ml.h:64-77,
+ * kplanes_tilted.cu:427-612). */
+int kplanes_tilted_tv_fuse_grad_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                                     const float *d_gout, float *d_ggrid, float *d_gR,
+                                     float *d_gpts, long B, int T, int C, int H, int W, float h,
+                                     cudaStream_t stream);
 
 /* Plane layout conversion [P, C, H, W] -> [P, H, W, C] and back. Replaces the
  * torch permute+contiguous of the reference's op layer

@@ -13,6 +13,10 @@
  *   backward            :141-281  ggrid += w_k·s_{p+1}·s_{p+2}·go;
  *                                 dL/dr via ds/dix, ds/diy and the border masks;
  *                                 gR_t += dr ⊗ p;  gpts += R_tᵀ·dr
+ *   tv taps             :329-612  the same at R_t·p and at R_t·p + h·R_t[:, k-1]
+ *                                 (k = 1..3; h·R_t rounded, then added), output
+ *                                 [4, N, T*C]; backward adds h·dr_k to column
+ *                                 k-1 of gR_t for taps k >= 1
  * with the plane read in its parameter layout [3T, C, H, W] (the reference's
  * op layer permutes to channels-last only for the GPU; _ops.py:21-25).
  *
@@ -83,16 +87,31 @@ static float obilerp(const float w[4], float v0, float v1, float v2, float v3) {
     return fmaf(w[3], v3, fmaf(w[2], v2, fmaf(w[0], v0, w[1] * v1)));
 }
 
-/* pts [N,3], R [T,3,3], plane [3T,C,H,W] -> out [N, T*C] */
-void oracle_kplanes_fwd(const float *pts, const float *R, const float *plane, float *out, long N,
-                        int T, int C, int H, int W) {
+/* Sample point of tap k: r itself (k = 0) or r + h·R_t[:, k-1]. */
+static void otap_point(const float *Rt, const float r[3], int k, float h, float a[3]) {
+    for (int i = 0; i < 3; ++i) {
+        if (k == 0) {
+            a[i] = r[i];
+        } else {
+            const float off = h * Rt[3 * i + (k - 1)];
+            a[i] = r[i] + off;
+        }
+    }
+}
+
+/* ntap = 1: pts [N,3], R [T,3,3], plane [3T,C,H,W] -> out [N, T*C].
+ * ntap = 4: out [4, N, T*C], tap k at R_t·p (+ h·R_t[:, k-1]). */
+static void kp_fwd(const float *pts, const float *R, const float *plane, float *out, long N,
+                   int T, int C, int H, int W, int ntap, float h) {
     const size_t HW = (size_t)H * W, planeCHW = (size_t)C * HW;
 #pragma omp parallel for schedule(dynamic, 256)
     for (long b = 0; b < N; ++b) {
         const float px = pts[3 * b], py = pts[3 * b + 1], pz = pts[3 * b + 2];
-        for (int t = 0; t < T; ++t) {
-            float r[3];
-            orotate(R + 9 * t, px, py, pz, r);
+        for (int t = 0; t < T; ++t)
+        for (int k = 0; k < ntap; ++k) {
+            float r0[3], r[3];
+            orotate(R + 9 * t, px, py, pz, r0);
+            otap_point(R + 9 * t, r0, k, h, r);
             OTap tp[3];
             for (int p = 0; p < 3; ++p) {
                 float gx, gy;
@@ -106,17 +125,27 @@ void oracle_kplanes_fwd(const float *pts, const float *R, const float *plane, fl
                     prod *= obilerp(tp[p].w, pc[tp[p].cell[0]], pc[tp[p].cell[1]],
                                     pc[tp[p].cell[2]], pc[tp[p].cell[3]]);
                 }
-                out[(size_t)b * T * C + (size_t)t * C + c] = prod;
+                out[((size_t)k * N + b) * T * C + (size_t)t * C + c] = prod;
             }
         }
     }
 }
 
+void oracle_kplanes_fwd(const float *pts, const float *R, const float *plane, float *out, long N,
+                        int T, int C, int H, int W) {
+    kp_fwd(pts, R, plane, out, N, T, C, H, W, 1, 0.f);
+}
+
+void oracle_kplanes_tv_fwd(const float *pts, const float *R, const float *plane, float *out,
+                           long N, int T, int C, int H, int W, float h) {
+    kp_fwd(pts, R, plane, out, N, T, C, H, W, 4, h);
+}
+
 /* Gradients of Σ out·gout. gpts [N,3], gR [T,3,3], gplane [3T,C,H,W] are
  * overwritten. */
-void oracle_kplanes_bwd(const float *pts, const float *R, const float *plane, const float *gout,
-                        float *gpts, float *gR, float *gplane, long N, int T, int C, int H,
-                        int W) {
+static void kp_bwd(const float *pts, const float *R, const float *plane, const float *gout,
+                   float *gpts, float *gR, float *gplane, long N, int T, int C, int H, int W,
+                   int ntap, float h) {
     const size_t HW = (size_t)H * W, planeCHW = (size_t)C * HW;
     const size_t P = (size_t)3 * T * planeCHW;
     double *acc = (double *)calloc(P > 0 ? P : 1, sizeof(double));
@@ -130,10 +159,12 @@ void oracle_kplanes_bwd(const float *pts, const float *R, const float *plane, co
         for (long b = 0; b < N; ++b) {
             const float px = pts[3 * b], py = pts[3 * b + 1], pz = pts[3 * b + 2];
             double gp[3] = {0.0, 0.0, 0.0};
-            for (int t = 0; t < T; ++t) {
+            for (int t = 0; t < T; ++t)
+            for (int kt = 0; kt < ntap; ++kt) {
                 const float *Rt = R + 9 * t;
-                float r[3];
-                orotate(Rt, px, py, pz, r);
+                float r0[3], r[3];
+                orotate(Rt, px, py, pz, r0);
+                otap_point(Rt, r0, kt, h, r);
                 OTap tp[3];
                 for (int p = 0; p < 3; ++p) {
                     float gx, gy;
@@ -142,7 +173,7 @@ void oracle_kplanes_bwd(const float *pts, const float *R, const float *plane, co
                 }
                 double dgx[3] = {0, 0, 0}, dgy[3] = {0, 0, 0};
                 for (int c = 0; c < C; ++c) {
-                    const float go = gout[(size_t)b * T * C + (size_t)t * C + c];
+                    const float go = gout[((size_t)kt * N + b) * T * C + (size_t)t * C + c];
                     float v[3][4], s[3];
                     for (int p = 0; p < 3; ++p) {
                         const float *pc = plane + (size_t)(3 * t + p) * planeCHW + (size_t)c * HW;
@@ -182,6 +213,11 @@ void oracle_kplanes_bwd(const float *pts, const float *R, const float *plane, co
                 g9[6] += drz * px;
                 g9[7] += drz * py;
                 g9[8] += drz * pz;
+                if (kt > 0) {
+                    g9[kt - 1] += (double)h * drx;
+                    g9[3 + kt - 1] += (double)h * dry;
+                    g9[6 + kt - 1] += (double)h * drz;
+                }
             }
             gpts[3 * b] = (float)gp[0];
             gpts[3 * b + 1] = (float)gp[1];
@@ -194,4 +230,16 @@ void oracle_kplanes_bwd(const float *pts, const float *R, const float *plane, co
     for (int i = 0; i < 9 * T; ++i) gR[i] = (float)gR_acc[i];
     for (size_t i = 0; i < P; ++i) gplane[i] = (float)acc[i];
     free(acc);
+}
+
+void oracle_kplanes_bwd(const float *pts, const float *R, const float *plane, const float *gout,
+                        float *gpts, float *gR, float *gplane, long N, int T, int C, int H,
+                        int W) {
+    kp_bwd(pts, R, plane, gout, gpts, gR, gplane, N, T, C, H, W, 1, 0.f);
+}
+
+void oracle_kplanes_tv_bwd(const float *pts, const float *R, const float *plane,
+                           const float *gout, float *gpts, float *gR, float *gplane, long N, int T,
+                           int C, int H, int W, float h) {
+    kp_bwd(pts, R, plane, gout, gpts, gR, gplane, N, T, C, H, W, 4, h);
 }

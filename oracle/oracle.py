@@ -54,6 +54,8 @@ def _load():
         "oracle_tv_l1_grad": [_f32p, _f32p, _f32p, i, i, i, i],
         "oracle_kplanes_fwd": [_f32p, _f32p, _f32p, _f32p, L, i, i, i, i],
         "oracle_kplanes_bwd": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, L, i, i, i, i],
+        "oracle_kplanes_tv_fwd": [_f32p, _f32p, _f32p, _f32p, L, i, i, i, i, f],
+        "oracle_kplanes_tv_bwd": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, L, i, i, i, i, f],
         "oracle_set_threads": [i],
         "oracle_get_threads": [],
     }
@@ -167,6 +169,29 @@ def kplanes_bwd(pts, R, plane, gout):
     return gp, gr, gg
 
 
+def kplanes_tv_fwd(pts, R, plane, h: float) -> np.ndarray:
+    """Four-tap form: out [4, N, T*C], tap k at R_t·p (+ h·R_t[:, k-1])."""
+    p, r, g = _f32(pts), _f32(R), _f32(plane)
+    n, t = p.shape[0], r.shape[0]
+    c, hh, w = g.shape[1:]
+    out = np.empty((4, n, t * c), np.float32)
+    _load().oracle_kplanes_tv_fwd(_p(p), _p(r), _p(g), _p(out), n, t, c, hh, w, float(h))
+    return out
+
+
+def kplanes_tv_bwd(pts, R, plane, gout, h: float):
+    """(grad_pts, grad_R, grad_plane) of Σ out·gout for the four-tap form."""
+    p, r, g, go = _f32(pts), _f32(R), _f32(plane), _f32(gout)
+    n, t = p.shape[0], r.shape[0]
+    c, hh, w = g.shape[1:]
+    gp = np.empty_like(p)
+    gr = np.empty_like(r)
+    gg = np.empty_like(g)
+    _load().oracle_kplanes_tv_bwd(_p(p), _p(r), _p(g), _p(go), _p(gp), _p(gr), _p(gg), n, t, c, hh, w,
+                                  float(h))
+    return gp, gr, gg
+
+
 # ── the reference's own CUDA `_core`, built from its sources ────────────────
 
 _ref_core = None
@@ -206,6 +231,8 @@ __all__ = [
     "tv_l1_grad",
     "kplanes_fwd",
     "kplanes_bwd",
+    "kplanes_tv_fwd",
+    "kplanes_tv_bwd",
     "ref_core",
     "available_cores",
 ]

@@ -87,6 +87,29 @@ __device__ __forceinline__ float bilerp(const float w[4], float v0, float v1, fl
     return __fmaf_rn(w[3], v3, __fmaf_rn(w[2], v2, __fmaf_rn(w[0], v0, __fmul_rn(w[1], v1))));
 }
 
+// The tv-tap variant's tap k (1..3) samples at R_t·p + h·R_t[:, k-1]; the
+// column offset is rounded on its own and then added, as the reference kernel
+// stages h·R_t in shared memory before adding it (kplanes_tilted.cu:367-400).
+__device__ __forceinline__ void tap_offsets(const float Rt[9], float h, float hc[9]) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+#pragma unroll
+        for (int i = 0; i < 3; ++i) hc[3 * j + i] = __fmul_rn(h, Rt[3 * i + j]);
+}
+
+__device__ __forceinline__ void tap_point(const float hc[9], int k, float rx, float ry, float rz,
+                                          float &ax, float &ay, float &az) {
+    if (k == 0) {
+        ax = rx;
+        ay = ry;
+        az = rz;
+    } else {
+        ax = __fadd_rn(rx, hc[3 * (k - 1)]);
+        ay = __fadd_rn(ry, hc[3 * (k - 1) + 1]);
+        az = __fadd_rn(rz, hc[3 * (k - 1) + 2]);
+    }
+}
+
 __device__ __forceinline__ void plane_coords(float rx, float ry, float rz, int p, float &gx,
                                              float &gy) {
     // p: 0 = XY (rx, ry), 1 = ZX (rz, rx), 2 = YZ (ry, rz).
@@ -112,18 +135,23 @@ constexpr int kThreads = 256;
 #endif
 constexpr int kBwdMinBlocks = QC_KP_BWD_MINB;
 
-template <int L>
+// NT = 1: kplanes_tilted_fuse. NT = 4: kplanes_tilted_tv_fuse, the same
+// interpolation at R_t·p and at the three offsets R_t·p + h·R_t[:, k-1], written
+// to out[k] of a [4, B, T*C] output (tap 0 is bit-identical to NT = 1).
+template <int L, int NT>
 __global__ void __launch_bounds__(kThreads) kpt_fwd_v4_kernel(const float *__restrict__ pts,
                                                               const float *__restrict__ R,
                                                               const float *__restrict__ grid,
                                                               float *__restrict__ out, long long B,
-                                                              int T, int H, int W) {
+                                                              int T, int H, int W, float h) {
     constexpr int C = 4 * L;
     constexpr int G = 32 / L;  // points per warp tile
     const int t = blockIdx.y;
     float Rt[9];
 #pragma unroll
     for (int k = 0; k < 9; ++k) Rt[k] = __ldg(R + 9 * t + k);
+    float hc[9];
+    if (NT > 1) tap_offsets(Rt, h, hc);
 
     const int lane = threadIdx.x & 31;
     const int grp = lane / L, c4 = 4 * (lane % L);
@@ -139,26 +167,33 @@ __global__ void __launch_bounds__(kThreads) kpt_fwd_v4_kernel(const float *__res
                     pz = __ldg(pts + 3 * b + 2);
         float rx, ry, rz;
         rotate(Rt, px, py, pz, rx, ry, rz);
-        float4 s[3];
+#pragma unroll 1
+        for (int k = 0; k < NT; ++k) {
+            float ax, ay, az;
+            tap_point(hc, k, rx, ry, rz, ax, ay, az);
+            float4 s[3];
 #pragma unroll
-        for (int p = 0; p < 3; ++p) {
-            float gx, gy;
-            plane_coords(rx, ry, rz, p, gx, gy);
-            const Tap tp = make_tap(gx, gy, H, W);
-            const float *pc = g0 + p * planeHWC;
-            const float4 v0 = ldg4(pc + tp.cell[0] * C), v1 = ldg4(pc + tp.cell[1] * C);
-            const float4 v2 = ldg4(pc + tp.cell[2] * C), v3 = ldg4(pc + tp.cell[3] * C);
-            s[p].x = bilerp(tp.w, v0.x, v1.x, v2.x, v3.x);
-            s[p].y = bilerp(tp.w, v0.y, v1.y, v2.y, v3.y);
-            s[p].z = bilerp(tp.w, v0.z, v1.z, v2.z, v3.z);
-            s[p].w = bilerp(tp.w, v0.w, v1.w, v2.w, v3.w);
+            for (int p = 0; p < 3; ++p) {
+                float gx, gy;
+                plane_coords(ax, ay, az, p, gx, gy);
+                const Tap tp = make_tap(gx, gy, H, W);
+                const float *pc = g0 + p * planeHWC;
+                const float4 v0 = ldg4(pc + tp.cell[0] * C), v1 = ldg4(pc + tp.cell[1] * C);
+                const float4 v2 = ldg4(pc + tp.cell[2] * C), v3 = ldg4(pc + tp.cell[3] * C);
+                s[p].x = bilerp(tp.w, v0.x, v1.x, v2.x, v3.x);
+                s[p].y = bilerp(tp.w, v0.y, v1.y, v2.y, v3.y);
+                s[p].z = bilerp(tp.w, v0.z, v1.z, v2.z, v3.z);
+                s[p].w = bilerp(tp.w, v0.w, v1.w, v2.w, v3.w);
+            }
+            float4 o;
+            o.x = __fmul_rn(__fmul_rn(s[0].x, s[1].x), s[2].x);
+            o.y = __fmul_rn(__fmul_rn(s[0].y, s[1].y), s[2].y);
+            o.z = __fmul_rn(__fmul_rn(s[0].z, s[1].z), s[2].z);
+            o.w = __fmul_rn(__fmul_rn(s[0].w, s[1].w), s[2].w);
+            __stcs(reinterpret_cast<float4 *>(out + ((long long)k * B + b) * (long long)(T * C) +
+                                              t * C + c4),
+                   o);
         }
-        float4 o;
-        o.x = __fmul_rn(__fmul_rn(s[0].x, s[1].x), s[2].x);
-        o.y = __fmul_rn(__fmul_rn(s[0].y, s[1].y), s[2].y);
-        o.z = __fmul_rn(__fmul_rn(s[0].z, s[1].z), s[2].z);
-        o.w = __fmul_rn(__fmul_rn(s[0].w, s[1].w), s[2].w);
-        __stcs(reinterpret_cast<float4 *>(out + b * (long long)(T * C) + t * C + c4), o);
     }
 }
 
@@ -190,11 +225,15 @@ __device__ __forceinline__ void sample_with_slopes(const float *pc, const Tap &t
     dy.w = (1.f - tx) * (v2.w - v0.w) + tx * (v3.w - v1.w);
 }
 
-template <int L>
+// NT = 4 (tv taps): each tap's coordinate gradient dr_k reaches R_t twice —
+// through R_t·p (dr_k ⊗ p, like the base op) and, for k >= 1, through the
+// offset h·R_t[:, k-1] (h·dr_k into column k-1) — and reaches p through
+// R_t^T dr_k; the taps' dr are summed before the point and R_t·p terms.
+template <int L, int NT>
 __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
     const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
     const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
-    float *__restrict__ gpts, long long B, int T, int H, int W, int t0) {
+    float *__restrict__ gpts, long long B, int T, int H, int W, int t0, float h) {
     constexpr int C = 4 * L;
     constexpr int G = 32 / L;
     constexpr int NWARP = kThreads / 32;
@@ -212,6 +251,8 @@ __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
     const long long warp0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
     float gr[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // this group's dL/dR_t
+    float hc[9];
+    if (NT > 1) tap_offsets(Rt, h, hc);
 
     for (long long b0 = warp0 * G; b0 < B; b0 += nwarps * G) {
         const long long b_raw = b0 + grp;
@@ -221,7 +262,13 @@ __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
                     pz = __ldg(pts + 3 * b + 2);
         float rx, ry, rz;
         rotate(Rt, px, py, pz, rx, ry, rz);
-        float4 go = __ldcs(reinterpret_cast<const float4 *>(gout + b * (long long)(T * C) + t * C + c4));
+        float sx = 0.f, sy = 0.f, sz = 0.f;  // Σ over taps of dL/dr
+#pragma unroll 1
+        for (int kt = 0; kt < NT; ++kt) {
+        float ax, ay, az;
+        tap_point(hc, kt, rx, ry, rz, ax, ay, az);
+        float4 go = __ldcs(reinterpret_cast<const float4 *>(
+            gout + ((long long)kt * B + b) * (long long)(T * C) + t * C + c4));
         if (!active) go = make_float4(0.f, 0.f, 0.f, 0.f);
 
         Tap tap[3];
@@ -229,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
             float gx, gy;
-            plane_coords(rx, ry, rz, p, gx, gy);
+            plane_coords(ax, ay, az, p, gx, gy);
             tap[p] = make_tap(gx, gy, H, W);
             sample_with_slopes<C>(g0 + p * planeHWC, tap[p], s[p], dx[p], dy[p]);
         }
@@ -265,15 +312,31 @@ __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
         const float drx = dgx[0] * tap[0].gxm + dgy[1] * tap[1].gym;
         const float dry = dgy[0] * tap[0].gym + dgx[2] * tap[2].gxm;
         const float drz = dgx[1] * tap[1].gxm + dgy[2] * tap[2].gym;
+        if (NT == 1) {
+            sx = drx;
+            sy = dry;
+            sz = drz;
+        } else {
+            sx += drx;
+            sy += dry;
+            sz += drz;
+            if (kt > 0 && active && lis == 0) {
+                // the offset h·R_t[:, kt-1]: dL/dR_t[i, kt-1] += h · dr_i
+                gr[kt - 1] += h * drx;
+                gr[3 + kt - 1] += h * dry;
+                gr[6 + kt - 1] += h * drz;
+            }
+        }
+        }  // taps
         if (active && lis == 0) {
             // dL/dp += R_t^T dr (the point's T rotations run in different blocks)
-            atomicAdd(gpts + 3 * b, Rt[0] * drx + Rt[3] * dry + Rt[6] * drz);
-            atomicAdd(gpts + 3 * b + 1, Rt[1] * drx + Rt[4] * dry + Rt[7] * drz);
-            atomicAdd(gpts + 3 * b + 2, Rt[2] * drx + Rt[5] * dry + Rt[8] * drz);
+            atomicAdd(gpts + 3 * b, Rt[0] * sx + Rt[3] * sy + Rt[6] * sz);
+            atomicAdd(gpts + 3 * b + 1, Rt[1] * sx + Rt[4] * sy + Rt[7] * sz);
+            atomicAdd(gpts + 3 * b + 2, Rt[2] * sx + Rt[5] * sy + Rt[8] * sz);
             // dL/dR_t[i, j] += dr_i * p_j, kept in registers
-            gr[0] += drx * px; gr[1] += drx * py; gr[2] += drx * pz;
-            gr[3] += dry * px; gr[4] += dry * py; gr[5] += dry * pz;
-            gr[6] += drz * px; gr[7] += drz * py; gr[8] += drz * pz;
+            gr[0] += sx * px; gr[1] += sx * py; gr[2] += sx * pz;
+            gr[3] += sy * px; gr[4] += sy * py; gr[5] += sy * pz;
+            gr[6] += sz * px; gr[7] += sz * py; gr[8] += sz * pz;
         }
     }
 
@@ -297,9 +360,10 @@ __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
 
 // ── generic path: any C (scalar channels, one warp per point) ─────────────
 
+template <int NT>
 __global__ void __launch_bounds__(kThreads) kpt_fwd_generic_kernel(
     const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
-    float *__restrict__ out, long long B, int T, int C, int H, int W) {
+    float *__restrict__ out, long long B, int T, int C, int H, int W, float h) {
     extern __shared__ float sR[];
     for (int i = threadIdx.x; i < T * 9; i += blockDim.x) sR[i] = R[i];
     __syncthreads();
@@ -312,34 +376,41 @@ __global__ void __launch_bounds__(kThreads) kpt_fwd_generic_kernel(
         for (int t = 0; t < T; ++t) {
             float rx, ry, rz;
             rotate(sR + 9 * t, px, py, pz, rx, ry, rz);
-            Tap tp[3];
-#pragma unroll
-            for (int p = 0; p < 3; ++p) {
-                float gx, gy;
-                plane_coords(rx, ry, rz, p, gx, gy);
-                tp[p] = make_tap(gx, gy, H, W);
-            }
-            for (int c = lane; c < C; c += 32) {
-                float s[3];
+            float hc[9];
+            if (NT > 1) tap_offsets(sR + 9 * t, h, hc);
+            for (int k = 0; k < NT; ++k) {
+                float ax, ay, az;
+                tap_point(hc, k, rx, ry, rz, ax, ay, az);
+                Tap tp[3];
 #pragma unroll
                 for (int p = 0; p < 3; ++p) {
-                    const float *pc = grid + (long long)(3 * t + p) * planeHWC + c;
-                    s[p] = bilerp(tp[p].w, __ldg(pc + (long long)tp[p].cell[0] * C),
-                                  __ldg(pc + (long long)tp[p].cell[1] * C),
-                                  __ldg(pc + (long long)tp[p].cell[2] * C),
-                                  __ldg(pc + (long long)tp[p].cell[3] * C));
+                    float gx, gy;
+                    plane_coords(ax, ay, az, p, gx, gy);
+                    tp[p] = make_tap(gx, gy, H, W);
                 }
-                out[b * (long long)(T * C) + (long long)t * C + c] =
-                    __fmul_rn(__fmul_rn(s[0], s[1]), s[2]);
+                for (int c = lane; c < C; c += 32) {
+                    float s[3];
+#pragma unroll
+                    for (int p = 0; p < 3; ++p) {
+                        const float *pc = grid + (long long)(3 * t + p) * planeHWC + c;
+                        s[p] = bilerp(tp[p].w, __ldg(pc + (long long)tp[p].cell[0] * C),
+                                      __ldg(pc + (long long)tp[p].cell[1] * C),
+                                      __ldg(pc + (long long)tp[p].cell[2] * C),
+                                      __ldg(pc + (long long)tp[p].cell[3] * C));
+                    }
+                    out[((long long)k * B + b) * (long long)(T * C) + (long long)t * C + c] =
+                        __fmul_rn(__fmul_rn(s[0], s[1]), s[2]);
+                }
             }
         }
     }
 }
 
+template <int NT>
 __global__ void __launch_bounds__(kThreads) kpt_bwd_generic_kernel(
     const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
     const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
-    float *__restrict__ gpts, long long B, int T, int C, int H, int W, int t0, int t1) {
+    float *__restrict__ gpts, long long B, int T, int C, int H, int W, int t0, int t1, float h) {
     extern __shared__ float smem[];
     float *sR = smem;
     float *sgR = smem + 9 * T;
@@ -359,16 +430,21 @@ __global__ void __launch_bounds__(kThreads) kpt_bwd_generic_kernel(
             const float *Rt = sR + 9 * t;
             float rx, ry, rz;
             rotate(Rt, px, py, pz, rx, ry, rz);
+            float hc[9];
+            if (NT > 1) tap_offsets(Rt, h, hc);
+            for (int kt = 0; kt < NT; ++kt) {
+            float ax, ay, az;
+            tap_point(hc, kt, rx, ry, rz, ax, ay, az);
             Tap tp[3];
 #pragma unroll
             for (int p = 0; p < 3; ++p) {
                 float gx, gy;
-                plane_coords(rx, ry, rz, p, gx, gy);
+                plane_coords(ax, ay, az, p, gx, gy);
                 tp[p] = make_tap(gx, gy, H, W);
             }
             float dgx[3] = {0.f, 0.f, 0.f}, dgy[3] = {0.f, 0.f, 0.f};
             for (int c = lane; c < C; c += 32) {
-                const float go = gout[b * (long long)(T * C) + (long long)t * C + c];
+                const float go = gout[((long long)kt * B + b) * (long long)(T * C) + (long long)t * C + c];
                 float v[3][4], s[3];
 #pragma unroll
                 for (int p = 0; p < 3; ++p) {
@@ -416,7 +492,13 @@ __global__ void __launch_bounds__(kThreads) kpt_bwd_generic_kernel(
                 atomicAdd(sg + 6, drz * px);
                 atomicAdd(sg + 7, drz * py);
                 atomicAdd(sg + 8, drz * pz);
+                if (NT > 1 && kt > 0) {
+                    atomicAdd(sg + kt - 1, h * drx);
+                    atomicAdd(sg + 3 + kt - 1, h * dry);
+                    atomicAdd(sg + 6 + kt - 1, h * drz);
+                }
             }
+            }  // taps
         }
         if (lane == 0) {
             gpts[3 * b] += gpx;
@@ -579,30 +661,91 @@ int rotation_grid_x(long long work_warps, int blocks_per_sm, int *gx) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int L>
+template <int L, int NT>
 int fwd_v4(const float *pts, const float *R, const float *grid, float *out, long long B, int T,
-           int H, int W, cudaStream_t stream) {
+           int H, int W, float h, cudaStream_t stream) {
     constexpr int G = 32 / L;
     int gx = 0;
     if (int st = rotation_grid_x((B + G - 1) / G, 8, &gx)) return st;
     QC_RETURN_IF(T > 65535, QC_ERR_INVALID_ARGUMENT, "kplanes: T=%d exceeds 65535", T);
-    kpt_fwd_v4_kernel<L><<<dim3(gx, T), kThreads, 0, stream>>>(pts, R, grid, out, B, T, H, W);
+    kpt_fwd_v4_kernel<L, NT><<<dim3(gx, T), kThreads, 0, stream>>>(pts, R, grid, out, B, T, H, W, h);
     QC_CHECK_LAUNCH("kpt_fwd_v4_kernel launch");
     return 0;
 }
 
-template <int L>
+template <int L, int NT>
 int bwd_v4(const float *pts, const float *R, const float *grid, const float *gout, float *ggrid,
-           float *gR, float *gpts, long long B, int T, int H, int W, int t0, int t1,
+           float *gR, float *gpts, long long B, int T, int H, int W, int t0, int t1, float h,
            cudaStream_t stream) {
     constexpr int G = 32 / L;
     int gx = 0;
     if (int st = rotation_grid_x((B + G - 1) / G, kBwdMinBlocks, &gx)) return st;
     QC_RETURN_IF(t1 - t0 > 65535, QC_ERR_INVALID_ARGUMENT, "kplanes: %d rotations exceed 65535",
                  t1 - t0);
-    kpt_bwd_v4_kernel<L><<<dim3(gx, t1 - t0), kThreads, 0, stream>>>(pts, R, grid, gout, ggrid, gR,
-                                                                      gpts, B, T, H, W, t0);
+    kpt_bwd_v4_kernel<L, NT><<<dim3(gx, t1 - t0), kThreads, 0, stream>>>(
+        pts, R, grid, gout, ggrid, gR, gpts, B, T, H, W, t0, h);
     QC_CHECK_LAUNCH("kpt_bwd_v4_kernel launch");
+    return 0;
+}
+
+template <int NT>
+int forward(const char *who, const float *d_pts, const float *d_R, const float *d_grid,
+            float *d_out, long B, int T, int C, int H, int W, float h, cudaStream_t stream) {
+    if (int st = check_shapes(who, B, T, C, H, W)) return st;
+    if (B == 0 || T == 0 || C == 0) return 0;
+    QC_RETURN_IF(H == 0 || W == 0, QC_ERR_INVALID_ARGUMENT, "%s: empty plane", who);
+    QC_RETURN_IF(!d_pts || !d_R || !d_grid || !d_out, QC_ERR_INVALID_ARGUMENT, "%s: null pointer",
+                 who);
+    const bool vec = (C % 4 == 0) && C <= 128 && aligned16(d_grid) && aligned16(d_out);
+    if (vec) {
+        switch (C / 4) {
+            case 1: return fwd_v4<1, NT>(d_pts, d_R, d_grid, d_out, B, T, H, W, h, stream);
+            case 2: return fwd_v4<2, NT>(d_pts, d_R, d_grid, d_out, B, T, H, W, h, stream);
+            case 4: return fwd_v4<4, NT>(d_pts, d_R, d_grid, d_out, B, T, H, W, h, stream);
+            case 8: return fwd_v4<8, NT>(d_pts, d_R, d_grid, d_out, B, T, H, W, h, stream);
+            case 16: return fwd_v4<16, NT>(d_pts, d_R, d_grid, d_out, B, T, H, W, h, stream);
+            case 32: return fwd_v4<32, NT>(d_pts, d_R, d_grid, d_out, B, T, H, W, h, stream);
+            default: break;
+        }
+    }
+    int blocks = 0;
+    if (int st = grid_size(B, &blocks)) return st;
+    kpt_fwd_generic_kernel<NT><<<blocks, kThreads, 9 * T * sizeof(float), stream>>>(
+        d_pts, d_R, d_grid, d_out, B, T, C, H, W, h);
+    QC_CHECK_LAUNCH("kpt_fwd_generic_kernel launch");
+    return 0;
+}
+
+template <int NT>
+int backward(const char *who, const float *d_pts, const float *d_R, const float *d_grid,
+             const float *d_gout, float *d_ggrid, float *d_gR, float *d_gpts, long B, int T,
+             int C, int H, int W, int t_begin, int t_end, float h, cudaStream_t stream) {
+    if (int st = check_shapes(who, B, T, C, H, W)) return st;
+    QC_RETURN_IF(t_begin < 0 || t_end > T || t_begin > t_end, QC_ERR_INVALID_ARGUMENT,
+                 "%s: rotations [%d, %d) outside [0, %d)", who, t_begin, t_end, T);
+    if (B == 0 || t_begin == t_end || C == 0) return 0;
+    QC_RETURN_IF(H == 0 || W == 0, QC_ERR_INVALID_ARGUMENT, "%s: empty plane", who);
+    QC_RETURN_IF(!d_pts || !d_R || !d_grid || !d_gout || !d_ggrid || !d_gR || !d_gpts,
+                 QC_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+    const bool vec = (C % 4 == 0) && C <= 128 && aligned16(d_grid) && aligned16(d_gout) &&
+                     aligned16(d_ggrid);
+    const int t0 = t_begin, t1 = t_end;
+    if (vec) {
+        switch (C / 4) {
+            case 1: return bwd_v4<1, NT>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, h, stream);
+            case 2: return bwd_v4<2, NT>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, h, stream);
+            case 4: return bwd_v4<4, NT>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, h, stream);
+            case 8: return bwd_v4<8, NT>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, h, stream);
+            case 16: return bwd_v4<16, NT>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, h, stream);
+            case 32: return bwd_v4<32, NT>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, h, stream);
+            default: break;
+        }
+    }
+    int blocks = 0;
+    if (int st = grid_size(B, &blocks)) return st;
+    kpt_bwd_generic_kernel<NT><<<blocks, kThreads, 18 * T * sizeof(float), stream>>>(
+        d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, C, H, W, t0, t1, h);
+    QC_CHECK_LAUNCH("kpt_bwd_generic_kernel launch");
     return 0;
 }
 
@@ -614,30 +757,15 @@ extern "C" {
 int kplanes_tilted_fuse_cuda(const float *d_pts, const float *d_R, const float *d_grid,
                              float *d_out, long B, int T, int C, int H, int W,
                              cudaStream_t stream) {
-    using namespace qc::kp;
-    if (int st = check_shapes("kplanes_tilted_fuse_cuda", B, T, C, H, W)) return st;
-    if (B == 0 || T == 0 || C == 0) return 0;
-    QC_RETURN_IF(H == 0 || W == 0, QC_ERR_INVALID_ARGUMENT, "kplanes_tilted_fuse_cuda: empty plane");
-    QC_RETURN_IF(!d_pts || !d_R || !d_grid || !d_out, QC_ERR_INVALID_ARGUMENT,
-                 "kplanes_tilted_fuse_cuda: null pointer");
-    const bool vec = (C % 4 == 0) && C <= 128 && aligned16(d_grid) && aligned16(d_out);
-    if (vec) {
-        switch (C / 4) {
-            case 1: return fwd_v4<1>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
-            case 2: return fwd_v4<2>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
-            case 4: return fwd_v4<4>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
-            case 8: return fwd_v4<8>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
-            case 16: return fwd_v4<16>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
-            case 32: return fwd_v4<32>(d_pts, d_R, d_grid, d_out, B, T, H, W, stream);
-            default: break;
-        }
-    }
-    int blocks = 0;
-    if (int st = grid_size(B, &blocks)) return st;
-    kpt_fwd_generic_kernel<<<blocks, kThreads, 9 * T * sizeof(float), stream>>>(d_pts, d_R, d_grid,
-                                                                              d_out, B, T, C, H, W);
-    QC_CHECK_LAUNCH("kpt_fwd_generic_kernel launch");
-    return 0;
+    return qc::kp::forward<1>("kplanes_tilted_fuse_cuda", d_pts, d_R, d_grid, d_out, B, T, C, H,
+                              W, 0.f, stream);
+}
+
+int kplanes_tilted_tv_fuse_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                                float *d_out, long B, int T, int C, int H, int W, float h,
+                                cudaStream_t stream) {
+    return qc::kp::forward<4>("kplanes_tilted_tv_fuse_cuda", d_pts, d_R, d_grid, d_out, B, T, C,
+                              H, W, h, stream);
 }
 
 int kplanes_tilted_fuse_grad_rotations_cuda(const float *d_pts, const float *d_R,
@@ -645,36 +773,17 @@ int kplanes_tilted_fuse_grad_rotations_cuda(const float *d_pts, const float *d_R
                                             float *d_ggrid, float *d_gR, float *d_gpts, long B,
                                             int T, int C, int H, int W, int t_begin, int t_end,
                                             cudaStream_t stream) {
-    using namespace qc::kp;
-    if (int st = check_shapes("kplanes_tilted_fuse_grad_cuda", B, T, C, H, W)) return st;
-    QC_RETURN_IF(t_begin < 0 || t_end > T || t_begin > t_end, QC_ERR_INVALID_ARGUMENT,
-                 "kplanes_tilted_fuse_grad_cuda: rotations [%d, %d) outside [0, %d)", t_begin,
-                 t_end, T);
-    if (B == 0 || t_begin == t_end || C == 0) return 0;
-    QC_RETURN_IF(H == 0 || W == 0, QC_ERR_INVALID_ARGUMENT,
-                 "kplanes_tilted_fuse_grad_cuda: empty plane");
-    QC_RETURN_IF(!d_pts || !d_R || !d_grid || !d_gout || !d_ggrid || !d_gR || !d_gpts,
-                 QC_ERR_INVALID_ARGUMENT, "kplanes_tilted_fuse_grad_cuda: null pointer");
-    const bool vec = (C % 4 == 0) && C <= 128 && aligned16(d_grid) && aligned16(d_gout) &&
-                     aligned16(d_ggrid);
-    const int t0 = t_begin, t1 = t_end;
-    if (vec) {
-        switch (C / 4) {
-            case 1: return bwd_v4<1>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
-            case 2: return bwd_v4<2>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
-            case 4: return bwd_v4<4>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
-            case 8: return bwd_v4<8>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
-            case 16: return bwd_v4<16>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
-            case 32: return bwd_v4<32>(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, H, W, t0, t1, stream);
-            default: break;
-        }
-    }
-    int blocks = 0;
-    if (int st = grid_size(B, &blocks)) return st;
-    kpt_bwd_generic_kernel<<<blocks, kThreads, 18 * T * sizeof(float), stream>>>(
-        d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR, d_gpts, B, T, C, H, W, t0, t1);
-    QC_CHECK_LAUNCH("kpt_bwd_generic_kernel launch");
-    return 0;
+    return qc::kp::backward<1>("kplanes_tilted_fuse_grad_cuda", d_pts, d_R, d_grid, d_gout,
+                               d_ggrid, d_gR, d_gpts, B, T, C, H, W, t_begin, t_end, 0.f, stream);
+}
+
+int kplanes_tilted_tv_fuse_grad_cuda(const float *d_pts, const float *d_R, const float *d_grid,
+                                     const float *d_gout, float *d_ggrid, float *d_gR,
+                                     float *d_gpts, long B, int T, int C, int H, int W, float h,
+                                     cudaStream_t stream) {
+    return qc::kp::backward<4>("kplanes_tilted_tv_fuse_grad_cuda", d_pts, d_R, d_grid, d_gout,
+                               d_ggrid, d_gR, d_gpts, B, T, C, H, W, 0, T < 0 ? 0 : T, h,
+                               stream);
 }
 
 int kplanes_tilted_fuse_grad_cuda(const float *d_pts, const float *d_R, const float *d_grid,

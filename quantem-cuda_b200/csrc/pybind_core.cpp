@@ -174,6 +174,34 @@ PYBIND11_MODULE(_core, m) {
         py::arg("C"), py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
 
     m.def(
+        "kplanes_tilted_tv_fuse_cuda",
+        [](uintptr_t pts, uintptr_t r, uintptr_t grid, uintptr_t out, long B, int T, int C, int H,
+           int W, float h, uintptr_t stream) {
+            check(kplanes_tilted_tv_fuse_cuda(ptr<const float>(pts), ptr<const float>(r),
+                                              ptr<const float>(grid), ptr<float>(out), B, T, C, H,
+                                              W, h, stream_of(stream)));
+        },
+        "Four-tap tilted K-Planes: out [4, B, T*C] at R.x and R.x + h*R[:, k-1].",
+        py::arg("pts_ptr"), py::arg("r_ptr"), py::arg("grid_ptr"), py::arg("out_ptr"), py::arg("B"),
+        py::arg("T"), py::arg("C"), py::arg("H"), py::arg("W"), py::arg("h"),
+        py::arg("stream_ptr"));
+
+    m.def(
+        "kplanes_tilted_tv_fuse_grad_cuda",
+        [](uintptr_t pts, uintptr_t r, uintptr_t grid, uintptr_t gout, uintptr_t ggrid,
+           uintptr_t gr, uintptr_t gpts, long B, int T, int C, int H, int W, float h,
+           uintptr_t stream) {
+            check(kplanes_tilted_tv_fuse_grad_cuda(
+                ptr<const float>(pts), ptr<const float>(r), ptr<const float>(grid),
+                ptr<const float>(gout), ptr<float>(ggrid), ptr<float>(gr), ptr<float>(gpts), B, T,
+                C, H, W, h, stream_of(stream)));
+        },
+        "Backward of kplanes_tilted_tv_fuse. gout [4, B, T*C]; ggrid, gr, gpts accumulated into.",
+        py::arg("pts_ptr"), py::arg("r_ptr"), py::arg("grid_ptr"), py::arg("gout_ptr"),
+        py::arg("ggrid_ptr"), py::arg("gr_ptr"), py::arg("gpts_ptr"), py::arg("B"), py::arg("T"),
+        py::arg("C"), py::arg("H"), py::arg("W"), py::arg("h"), py::arg("stream_ptr"));
+
+    m.def(
         "kplanes_tilted_fuse_grad_rotations_cuda",
         [](uintptr_t pts, uintptr_t r, uintptr_t grid, uintptr_t gout, uintptr_t ggrid,
            uintptr_t gr, uintptr_t gpts, long B, int T, int C, int H, int W, int t_begin,
@@ -274,16 +302,18 @@ PYBIND11_MODULE(_core, m) {
 
     m.def(
         "tv_loss_3d_slab_peer_cuda",
-        [](const qc_tv_peers &peers, unsigned long long seq, int variant, int flags,
-           uintptr_t vol, uintptr_t g, uintptr_t acc, uintptr_t grad, int B, int Dp, int H, int W,
-           int d_lo, int d_hi, int has_prev, int has_next, float eps, float scale, uintptr_t ws,
-           size_t ws_bytes, uintptr_t stream) {
-            check(tv_loss_3d_slab_peer_cuda(&peers, seq, variant, flags, ptr<const float>(vol),
-                                            ptr<const float>(g), ptr<float>(acc), ptr<float>(grad),
-                                            B, Dp, H, W, d_lo, d_hi, has_prev, has_next, eps,
-                                            scale, ptr<void>(ws), ws_bytes, stream_of(stream)));
+        [](const qc_tv_peers &peers, unsigned long long halo_seq, unsigned long long seq,
+           int variant, int flags, uintptr_t vol, uintptr_t g, uintptr_t acc, uintptr_t grad,
+           int B, int Dp, int H, int W, int d_lo, int d_hi, int has_prev, int has_next, float eps,
+           float scale, uintptr_t ws, size_t ws_bytes, uintptr_t stream) {
+            check(tv_loss_3d_slab_peer_cuda(&peers, halo_seq, seq, variant, flags,
+                                            ptr<const float>(vol), ptr<const float>(g),
+                                            ptr<float>(acc), ptr<float>(grad), B, Dp, H, W, d_lo,
+                                            d_hi, has_prev, has_next, eps, scale, ptr<void>(ws),
+                                            ws_bytes, stream_of(stream)));
         },
-        py::arg("peers"), py::arg("seq"), py::arg("variant"), py::arg("flags"), py::arg("vol_ptr"),
+        py::arg("peers"), py::arg("halo_seq"), py::arg("seq"), py::arg("variant"), py::arg("flags"),
+        py::arg("vol_ptr"),
         py::arg("g_ptr"), py::arg("acc_ptr"), py::arg("grad_ptr"), py::arg("B"), py::arg("Dp"),
         py::arg("H"), py::arg("W"), py::arg("d_lo"), py::arg("d_hi"), py::arg("has_prev"),
         py::arg("has_next"), py::arg("eps"), py::arg("acc_scale"), py::arg("ws_ptr"),

@@ -48,6 +48,7 @@
 #include <stdio.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "qc_common.cuh"
 
@@ -233,6 +234,117 @@ __device__ __forceinline__ Unit decode_unit(const Plan &pl, long long u, int til
     return U;
 }
 
+// ── cross-rank flags over peer memory ─────────────────────────────────────
+//
+// One communication block per rank, in memory its peers have mapped. Flags
+// hold the sequence number of the last call that set them; a waiter compares
+// with >= so a flag that has moved on to a later call still releases it.
+// Data goes into a peer's block with plain stores, then (one thread per CTA,
+// after a CTA barrier and a system-scope fence) the flag is stored with
+// release semantics; the waiter loads it with acquire semantics.
+
+struct PeerComm {
+    unsigned long long ready[2];   // [s]: neighbour on side s (0 = rank-1, 1 = rank+1) lets
+                                   // this rank store into that neighbour's halo for the call
+    unsigned long long filled[2];  // [s]: neighbour on side s has filled this rank's halo s
+    unsigned int arrive;           // CTAs of this rank's exchange launch done storing
+    unsigned int pad0[7];
+    unsigned long long red_flag[QC_MAX_PEER_RANKS];   // [q]: rank q's total is in the slot
+    double partials[2][QC_MAX_PEER_RANKS][4];         // [call & 1][q][accumulator]
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ double ld_relaxed_sys_f64(const double *p) {
+    double v;
+    asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until *flag >= seq, for at most limit_ns. Returns false if it gave up.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned long long *flag, unsigned long long seq,
+                                              uint64_t limit_ns) {
+    if (ld_acquire_sys(flag) >= seq) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        __nanosleep(64);
+        if (ld_acquire_sys(flag) >= seq) return true;
+        if (global_timer_ns() - t0 > limit_ns) return false;
+    }
+}
+
+__device__ __forceinline__ uint64_t peer_limit(const qc_tv_peers &p) {
+    return p.timeout_ns ? p.timeout_ns : kPeerWaitLimitNs;
+}
+
+// Halo exchange done by the sweep kernel itself (D-slabs over peer memory):
+// every CTA stores its share of this rank's two boundary planes into the
+// neighbours' halo planes at the start of the kernel, and the producer of a
+// unit that reads a halo plane waits for the neighbour's `filled` flag just
+// before issuing that plane's copy. seq == 0 disables it.
+struct HaloXchg {
+    PeerComm *self, *prev, *next;  // communication blocks (prev / next null at the ends)
+    float *prev_slab, *next_slab;  // the neighbours' slabs, mapped here
+    const float *vol;              // this rank's slab (the planes to send)
+    int prev_dp, next_dp;
+    unsigned long long seq;
+    uint64_t limit_ns;
+};
+
+// The exchange's first half, run by every thread of every CTA of the sweep:
+// tell the neighbours this rank's halos may be overwritten (all earlier work
+// on the stream has completed), wait until they say the same, store this
+// CTA's share of the boundary planes into their halos, and let the last CTA
+// raise their `filled` flags. `go` is a shared-memory int of the caller.
+__device__ __forceinline__ void halo_push_prologue(const HaloXchg &xc, int B, int Dp,
+                                                   long long plane, int *go) {
+    if (threadIdx.x == 0) {
+        if (xc.prev) st_release_sys(&xc.prev->ready[1], xc.seq);
+        if (xc.next) st_release_sys(&xc.next->ready[0], xc.seq);
+        bool ok = true;
+        if (xc.prev) ok = wait_flag_geq(&xc.self->ready[0], xc.seq, xc.limit_ns) && ok;
+        if (xc.next) ok = wait_flag_geq(&xc.self->ready[1], xc.seq, xc.limit_ns) && ok;
+        if (!ok) atomicOr(&g_tv_fault_word, QC_FAULT_PEER_WAIT);
+        *go = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (*go) {
+        // float4 items: side (to rank-1, to rank+1) × batch slice × plane / 4
+        const long long per = plane / 4, per_side = (long long)B * per;
+        const long long stride = (long long)gridDim.x * blockDim.x;
+        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < 2 * per_side;
+             i += stride) {
+            const int side = i >= per_side;
+            if (side == 0 ? xc.prev == nullptr : xc.next == nullptr) continue;
+            const long long j = i - side * per_side;
+            const long long b = j / per, e = j - b * per;
+            const long long src = (long long)b * Dp + (side == 0 ? 1 : Dp - 2);
+            const long long dst = side == 0 ? (long long)b * xc.prev_dp + xc.prev_dp - 1
+                                            : (long long)b * xc.next_dp;
+            float *d = side == 0 ? xc.prev_slab : xc.next_slab;
+            *reinterpret_cast<float4 *>(d + dst * plane + e * 4) = ldg4(xc.vol + src * plane + e * 4);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(&xc.self->arrive, 1u) == gridDim.x - 1) {
+            xc.self->arrive = 0;  // the next exchange on this stream starts after this grid
+            __threadfence_system();
+            if (xc.prev) st_release_sys(&xc.prev->filled[1], xc.seq);
+            if (xc.next) st_release_sys(&xc.next->filled[0], xc.seq);
+        }
+    }
+}
+
 // ── fast path: TMA ring + warp-specialised D-march ───────────────────────
 
 constexpr int kTileW = 128;                 // owned columns per tile
@@ -259,6 +371,7 @@ struct SweepSmem {
     uint64_t empty[G::S];
     double red[G::NW][kAccSlots];
     int abort;
+    int xgo;
 };
 
 template <class G>
@@ -456,7 +569,7 @@ __device__ __forceinline__ void row_flux4(const float4 &c, const float4 &n, cons
 template <int V, bool LOSS, bool GRAD, class G>
 __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
     const __grid_constant__ CUtensorMap map, const float *__restrict__ g,
-    float *__restrict__ grad, double *__restrict__ partials, const Plan pl) {
+    float *__restrict__ grad, double *__restrict__ partials, const Plan pl, const HaloXchg xc) {
     constexpr int R = G::R, NW = G::NW, S = G::S;
     // TMA destinations must be 128-byte aligned: align the ring explicitly
     // (the launch requests sizeof(SweepSmem) + 128 bytes).
@@ -475,6 +588,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
         fence_mbar_init();
     }
     __syncthreads();
+    if (xc.seq != 0) halo_push_prologue(xc, pl.B, pl.Dp, (long long)pl.H * pl.W, &sm.xgo);
 
     double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0;
 
@@ -491,6 +605,12 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                 const int zbase = U.n * pl.Dp;
                 for (int p = U.first; p <= U.last; ++p, ++seq) {
                     const int s = seq % S;
+                    if (xc.seq != 0 && ((p == pl.d_lo - 1 && pl.has_prev) || (p == pl.d_hi && pl.has_next))) {
+                        // a halo plane: wait until the neighbour has stored it here
+                        if (!wait_flag_geq(&xc.self->filled[p == pl.d_hi ? 1 : 0], xc.seq, xc.limit_ns))
+                            atomicOr(&g_tv_fault_word, QC_FAULT_PEER_WAIT);
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                    }
                     if (seq >= S) {
                         const uint32_t par = (uint32_t)(((seq / S) - 1) & 1);
                         if (!mbar_wait_bounded(&sm.empty[s], par, kWaitLimitNs)) {
@@ -642,58 +762,75 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                     float *gp = gbase + (size_t)p * plane_elems;
                     f2 la01 = 0ull, la23 = 0ull;  // paired loss sums of this plane (+0.0f pairs)
                     f2 up01 = pk2(Fh_up[0], Fh_up[1]), up23 = pk2(Fh_up[2], Fh_up[3]);
-                    ulonglong2 curp = lds_pairs(Sc, r0 + 1, scol);
+                    // The strip's rows, specialised on whether every row has its
+                    // +H neighbour (all strips but the one holding row H-1): then
+                    // no per-row validity selects are needed. Without a next plane
+                    // (has_nxt false) Sn is Sc, so `nxt` reads the voxel itself.
+                    auto rows = [&](auto full_tag) {
+                        constexpr bool FULL = decltype(full_tag)::value;
+                        ulonglong2 curp = lds_pairs(Sc, r0 + 1, scol);
+                        const f2 e01_full = pk2(eps_step, eps_step);
+                        const f2 e23_full = pk2(eps_step, last_quad ? kInf : eps_step);
+                        const bool loss_lane = has_nxt && lane_in;
 #pragma unroll
-                    for (int i = 0; i < R; ++i) {
-                        const int h = hbase + i;
-                        const bool row_ok = h + 1 < pl.H;  // row has a +H neighbour
-                        const ulonglong2 down = lds_pairs(Sc, r0 + i + 2, scol);
-                        const ulonglong2 nxt = has_nxt ? lds_pairs(Sn, r0 + i + 1, scol) : curp;
-                        float right = __shfl_down_sync(0xffffffffu, lo2(curp.x), 1);
-                        if (lane == 31) right = lds1(Sc, r0 + i + 1, scol + 4);
-                        if (last_quad) right = hi2(curp.y);
-                        const ulonglong2 dn = row_ok ? down : curp;
-                        const float eps_row = row_ok ? eps_step : kInf;
-                        const f2 e01 = pk2(eps_row, eps_row);
-                        const f2 e23 = pk2(eps_row, last_quad ? kInf : eps_row);
-                        ulonglong2 Fd, Fh, Fw;
-                        f2 q01 = 0ull, q23 = 0ull;
-                        float q1l = 0.f, q2l = 0.f;
-                        row_flux_pairs<V, LOSS, GRAD>(curp, nxt, dn, right, e01, e23, !last_quad, gn,
-                                                      Fd, Fh, Fw, q01, q23, q1l, q2l);
-                        if (LOSS) {
-                            if constexpr (V == QC_TV_ISO) {
-                                if (row_ok && has_nxt && lane_in) {
+                        for (int i = 0; i < R; ++i) {
+                            const int h = hbase + i;
+                            const bool row_ok = FULL || h + 1 < pl.H;  // row has a +H neighbour
+                            const ulonglong2 down = lds_pairs(Sc, r0 + i + 2, scol);
+                            const ulonglong2 nxt = lds_pairs(Sn, r0 + i + 1, scol);
+                            float right = __shfl_down_sync(0xffffffffu, lo2(curp.x), 1);
+                            if (lane == 31) right = lds1(Sc, r0 + i + 1, scol + 4);
+                            // iso: the missing +W neighbour of the volume's last column
+                            // is irrelevant (its corner carries eps = inf)
+                            if (V != QC_TV_ISO && last_quad) right = hi2(curp.y);
+                            // iso: a row without +H neighbour carries eps = inf, so the
+                            // zero-filled row below can stand in for the replicated one
+                            const ulonglong2 dn = (V == QC_TV_ISO || row_ok) ? down : curp;
+                            f2 e01 = e01_full, e23 = e23_full;
+                            if (!FULL && !row_ok) e01 = e23 = pk2(kInf, kInf);
+                            ulonglong2 Fd, Fh, Fw;
+                            f2 q01 = 0ull, q23 = 0ull;
+                            float q1l = 0.f, q2l = 0.f;
+                            row_flux_pairs<V, LOSS, GRAD>(curp, nxt, dn, right, e01, e23, !last_quad, gn,
+                                                          Fd, Fh, Fw, q01, q23, q1l, q2l);
+                            if (LOSS) {
+                                if constexpr (V == QC_TV_ISO) {
+                                    if (loss_lane && row_ok) {
+                                        la01 = add2(la01, q01);
+                                        la23 = add2(la23, q23);
+                                    }
+                                } else {
                                     la01 = add2(la01, q01);
                                     la23 = add2(la23, q23);
+                                    l1 += q1l;
+                                    l2 += q2l;
                                 }
-                            } else {
-                                la01 = add2(la01, q01);
-                                la23 = add2(la23, q23);
-                                l1 += q1l;
-                                l2 += q2l;
                             }
+                            if (GRAD) {
+                                const float fw_from_lane = __shfl_up_sync(0xffffffffu, hi2(Fw.y), 1);
+                                const float fw_from_halo = __shfl_sync(0xffffffffu, fw_halo, i);
+                                const float Fw_left0 = lane == 0 ? fw_from_halo : fw_from_lane;
+                                const f2 wl01 = pk2(Fw_left0, lo2(Fw.x));
+                                const f2 wl23 = pk2(hi2(Fw.x), lo2(Fw.y));
+                                const f2 gm = pk2(gn.gmul, gn.gmul);
+                                // gmul · ((Fd_prev − Fd) + (Fh_up − Fh) + (Fw_left − Fw))
+                                const f2 g01 = mul2(gm, add2(add2(sub2(Fd_prev[i][0], Fd.x), sub2(up01, Fh.x)),
+                                                             sub2(wl01, Fw.x)));
+                                const f2 g23 = mul2(gm, add2(add2(sub2(Fd_prev[i][1], Fd.y), sub2(up23, Fh.y)),
+                                                             sub2(wl23, Fw.y)));
+                                if (lane_in && (FULL || h < pl.H)) stcs_pairs(gp + (size_t)i * pl.W, g01, g23);
+                                Fd_prev[i][0] = Fd.x;
+                                Fd_prev[i][1] = Fd.y;
+                                up01 = Fh.x;
+                                up23 = Fh.y;
+                            }
+                            curp = down;
                         }
-                        if (GRAD) {
-                            const float fw_from_lane = __shfl_up_sync(0xffffffffu, hi2(Fw.y), 1);
-                            const float fw_from_halo = __shfl_sync(0xffffffffu, fw_halo, i);
-                            const float Fw_left0 = lane == 0 ? fw_from_halo : fw_from_lane;
-                            const f2 wl01 = pk2(Fw_left0, lo2(Fw.x));
-                            const f2 wl23 = pk2(hi2(Fw.x), lo2(Fw.y));
-                            const f2 gm = pk2(gn.gmul, gn.gmul);
-                            // gmul · ((Fd_prev − Fd) + (Fh_up − Fh) + (Fw_left − Fw))
-                            const f2 g01 = mul2(gm, add2(add2(sub2(Fd_prev[i][0], Fd.x), sub2(up01, Fh.x)),
-                                                         sub2(wl01, Fw.x)));
-                            const f2 g23 = mul2(gm, add2(add2(sub2(Fd_prev[i][1], Fd.y), sub2(up23, Fh.y)),
-                                                         sub2(wl23, Fw.y)));
-                            if (lane_in && h < pl.H) stcs_pairs(gp + (size_t)i * pl.W, g01, g23);
-                            Fd_prev[i][0] = Fd.x;
-                            Fd_prev[i][1] = Fd.y;
-                            up01 = Fh.x;
-                            up23 = Fh.y;
-                        }
-                        curp = down;
-                    }
+                    };
+                    if (hbase + R < pl.H)
+                        rows(std::true_type{});
+                    else
+                        rows(std::false_type{});
                     if (LOSS) l0 += (lo2(la01) + hi2(la01)) + (lo2(la23) + hi2(la23));
                 }
                 if (LOSS) {
@@ -860,57 +997,6 @@ __global__ void __launch_bounds__(kFinThreads) tv_finalize_kernel(const double *
     }
 }
 
-// ── cross-rank flags over peer memory ─────────────────────────────────────
-//
-// One communication block per rank, in memory its peers have mapped. Flags
-// hold the sequence number of the last call that set them; a waiter compares
-// with >= so a flag that has moved on to a later call still releases it.
-// Data goes into a peer's block with plain stores, then (one thread per CTA,
-// after a CTA barrier and a system-scope fence) the flag is stored with
-// release semantics; the waiter loads it with acquire semantics.
-
-struct PeerComm {
-    unsigned long long ready[2];   // [s]: neighbour on side s (0 = rank-1, 1 = rank+1) lets
-                                   // this rank store into that neighbour's halo for the call
-    unsigned long long filled[2];  // [s]: neighbour on side s has filled this rank's halo s
-    unsigned int arrive;           // CTAs of this rank's exchange launch done storing
-    unsigned int pad0[7];
-    unsigned long long red_flag[QC_MAX_PEER_RANKS];   // [q]: rank q's total is in the slot
-    double partials[2][QC_MAX_PEER_RANKS][4];         // [call & 1][q][accumulator]
-};
-
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ double ld_relaxed_sys_f64(const double *p) {
-    double v;
-    asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Waits until *flag >= seq, for at most limit_ns. Returns false if it gave up.
-__device__ __forceinline__ bool wait_flag_geq(const unsigned long long *flag, unsigned long long seq,
-                                              uint64_t limit_ns) {
-    if (ld_acquire_sys(flag) >= seq) return true;
-    const uint64_t t0 = global_timer_ns();
-    while (true) {
-        __nanosleep(64);
-        if (ld_acquire_sys(flag) >= seq) return true;
-        if (global_timer_ns() - t0 > limit_ns) return false;
-    }
-}
-
-__device__ __forceinline__ uint64_t peer_limit(const qc_tv_peers &p) {
-    return p.timeout_ns ? p.timeout_ns : kPeerWaitLimitNs;
-}
-
 // The finalize of a D-sharded loss: the fixed-order total of this rank's CTA
 // partials goes into slot [seq & 1][rank] of every rank's block; after all
 // ranks' flags show `seq`, every rank adds the slots in rank order. A slot is
@@ -1026,7 +1112,7 @@ using FastGeom = Geom<8, 4, 3, 3>;
 
 template <int V, bool LOSS, bool GRAD>
 int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, double *partials,
-                   Plan pl, int *grid_out, cudaStream_t stream) {
+                   Plan pl, const HaloXchg &xc, int *grid_out, cudaStream_t stream) {
     int sms = 0;
     if (int st = device_sm_count(&sms)) return st;
     if (use_tma) {
@@ -1072,7 +1158,7 @@ int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, 
         choose_chunking(pl, max_ctas, 1 + (GRAD ? 1 : 0));
         const long long rounds = (pl.n_units + max_ctas - 1) / max_ctas;
         const int grid = (int)((pl.n_units + rounds - 1) / rounds);
-        kern<<<grid, G::Threads, smem, stream>>>(map, g, grad, partials, pl);
+        kern<<<grid, G::Threads, smem, stream>>>(map, g, grad, partials, pl, xc);
         QC_CHECK_LAUNCH("tv_sweep_tma_kernel launch");
         *grid_out = grid;
     } else {
@@ -1098,19 +1184,24 @@ int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, 
 
 template <int V>
 int dispatch_mode(int flags, bool use_tma, const float *vol, const float *g, float *grad,
-                  double *partials, const Plan &pl, int *grid, cudaStream_t stream) {
+                  double *partials, const Plan &pl, const HaloXchg &xc, int *grid,
+                  cudaStream_t stream) {
     const bool L = flags & QC_TV_LOSS, G = flags & QC_TV_GRAD;
-    if (L && G) return launch_variant<V, true, true>(use_tma, vol, g, grad, partials, pl, grid, stream);
-    if (L) return launch_variant<V, true, false>(use_tma, vol, g, grad, partials, pl, grid, stream);
-    return launch_variant<V, false, true>(use_tma, vol, g, grad, partials, pl, grid, stream);
+    if (L && G) return launch_variant<V, true, true>(use_tma, vol, g, grad, partials, pl, xc, grid, stream);
+    if (L) return launch_variant<V, true, false>(use_tma, vol, g, grad, partials, pl, xc, grid, stream);
+    return launch_variant<V, false, true>(use_tma, vol, g, grad, partials, pl, xc, grid, stream);
 }
+
+int launch_halo_exchange(const qc_tv_peers *peers, unsigned long long seq, float *d_slab, int B,
+                         int Dp, int H, int W, cudaStream_t stream);
 
 size_t workspace_bytes() { return (size_t)kMaxPartials * kAccSlots * sizeof(double); }
 
 int run(int variant, int flags, const float *vol, const float *g, float *acc, float *grad, int B,
         int Dp, int H, int W, int d_lo, int d_hi, int has_prev, int has_next, float eps,
         float acc_scale, void *ws, size_t ws_bytes, cudaStream_t stream,
-        const qc_tv_peers *peers = nullptr, unsigned long long seq = 0) {
+        const qc_tv_peers *peers = nullptr, unsigned long long seq = 0,
+        unsigned long long halo_seq = 0) {
     const bool want_loss = flags & QC_TV_LOSS, want_grad = flags & QC_TV_GRAD;
     QC_RETURN_IF(variant < QC_TV_SQ || variant > QC_TV_L1, QC_ERR_INVALID_ARGUMENT,
                  "tv: unknown variant %d", variant);
@@ -1165,12 +1256,32 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     double *partials = reinterpret_cast<double *>(ws);
     int grid = 0;
     int st = 0;
+    HaloXchg xc{};
+    if (halo_seq != 0 && peers != nullptr && peers->world > 1) {
+        if (use_tma && !empty) {
+            // the sweep kernel stores the boundary planes and waits for the halos itself
+            const int r = peers->rank;
+            xc.self = static_cast<PeerComm *>(peers->comm[r]);
+            xc.prev = r > 0 ? static_cast<PeerComm *>(peers->comm[r - 1]) : nullptr;
+            xc.next = r < peers->world - 1 ? static_cast<PeerComm *>(peers->comm[r + 1]) : nullptr;
+            xc.prev_slab = peers->prev_slab;
+            xc.next_slab = peers->next_slab;
+            xc.prev_dp = peers->prev_dp;
+            xc.next_dp = peers->next_dp;
+            xc.vol = vol;
+            xc.seq = halo_seq;
+            xc.limit_ns = peers->timeout_ns ? peers->timeout_ns : kPeerWaitLimitNs;
+        } else {
+            st = launch_halo_exchange(peers, halo_seq, const_cast<float *>(vol), B, Dp, H, W, stream);
+            if (st) return st;
+        }
+    }
     if (empty) {
         // a rank that owns no planes still takes part in the cross-rank sum
     } else switch (variant) {
-        case QC_TV_SQ: st = dispatch_mode<QC_TV_SQ>(flags, use_tma, vol, g, grad, partials, pl, &grid, stream); break;
-        case QC_TV_ISO: st = dispatch_mode<QC_TV_ISO>(flags, use_tma, vol, g, grad, partials, pl, &grid, stream); break;
-        default: st = dispatch_mode<QC_TV_L1>(flags, use_tma, vol, g, grad, partials, pl, &grid, stream); break;
+        case QC_TV_SQ: st = dispatch_mode<QC_TV_SQ>(flags, use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
+        case QC_TV_ISO: st = dispatch_mode<QC_TV_ISO>(flags, use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
+        default: st = dispatch_mode<QC_TV_L1>(flags, use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
     }
     if (st) return st;
 
@@ -1439,16 +1550,8 @@ int check_peers(const qc_tv_peers *p, unsigned long long seq) {
     return 0;
 }
 
-}  // namespace tv
-}  // namespace qc
-
-extern "C" {
-
-size_t tv_peer_comm_bytes(void) { return sizeof(qc::tv::PeerComm); }
-
-int tv_slab_halo_exchange_cuda(const qc_tv_peers *peers, unsigned long long seq, float *d_slab,
-                               int B, int Dp, int H, int W, cudaStream_t stream) {
-    using namespace qc::tv;
+int launch_halo_exchange(const qc_tv_peers *peers, unsigned long long seq, float *d_slab, int B,
+                         int Dp, int H, int W, cudaStream_t stream) {
     if (int st = check_peers(peers, seq)) return st;
     const bool has_prev = peers->rank > 0, has_next = peers->rank < peers->world - 1;
     QC_RETURN_IF(B < 0 || H < 0 || W < 0, QC_ERR_INVALID_ARGUMENT,
@@ -1478,18 +1581,44 @@ int tv_slab_halo_exchange_cuda(const qc_tv_peers *peers, unsigned long long seq,
     return 0;
 }
 
-int tv_loss_3d_slab_peer_cuda(const qc_tv_peers *peers, unsigned long long seq, int variant,
-                              int flags, const float *d_vol, const float *d_g, float *d_acc,
-                              float *d_grad_vol, int B, int Dp, int H, int W, int d_lo, int d_hi,
-                              int has_prev, int has_next, float eps, float acc_scale,
-                              void *d_workspace, size_t workspace_bytes, cudaStream_t stream) {
+}  // namespace tv
+}  // namespace qc
+
+extern "C" {
+
+size_t tv_peer_comm_bytes(void) { return sizeof(qc::tv::PeerComm); }
+
+int tv_slab_halo_exchange_cuda(const qc_tv_peers *peers, unsigned long long seq, float *d_slab,
+                               int B, int Dp, int H, int W, cudaStream_t stream) {
+    return qc::tv::launch_halo_exchange(peers, seq, d_slab, B, Dp, H, W, stream);
+}
+
+int tv_loss_3d_slab_peer_cuda(const qc_tv_peers *peers, unsigned long long halo_seq,
+                              unsigned long long seq, int variant, int flags, const float *d_vol,
+                              const float *d_g, float *d_acc, float *d_grad_vol, int B, int Dp,
+                              int H, int W, int d_lo, int d_hi, int has_prev, int has_next,
+                              float eps, float acc_scale, void *d_workspace,
+                              size_t workspace_bytes, cudaStream_t stream) {
     using namespace qc::tv;
     if (int st = check_peers(peers, seq)) return st;
+    if (halo_seq != 0) {
+        const bool prev = peers->rank > 0, next = peers->rank < peers->world - 1;
+        QC_RETURN_IF(d_lo != 1 || d_hi != Dp - 1 || (int)prev != (has_prev ? 1 : 0) ||
+                         (int)next != (has_next ? 1 : 0),
+                     QC_ERR_INVALID_ARGUMENT,
+                     "tv_loss_3d_slab_peer_cuda: exchanging halos needs the slab layout (owned "
+                     "planes [1, Dp-1), neighbours exactly where the ranks have them)");
+        QC_RETURN_IF(Dp < 3, QC_ERR_INVALID_ARGUMENT,
+                     "tv_loss_3d_slab_peer_cuda: a slab needs a halo on each side and an owned plane");
+        QC_RETURN_IF((prev && (peers->prev_slab == nullptr || peers->prev_dp < 3)) ||
+                         (next && (peers->next_slab == nullptr || peers->next_dp < 3)),
+                     QC_ERR_INVALID_ARGUMENT, "tv_loss_3d_slab_peer_cuda: a neighbour's slab is missing");
+    }
     QC_RETURN_IF(!(flags & QC_TV_LOSS), QC_ERR_INVALID_ARGUMENT,
                  "tv_loss_3d_slab_peer_cuda: flags must include QC_TV_LOSS (use "
                  "tv_loss_3d_slab_cuda for the gradient alone)");
     return run(variant, flags, d_vol, d_g, d_acc, d_grad_vol, B, Dp, H, W, d_lo, d_hi, has_prev,
-               has_next, eps, acc_scale, d_workspace, workspace_bytes, stream, peers, seq);
+               has_next, eps, acc_scale, d_workspace, workspace_bytes, stream, peers, seq, halo_seq);
 }
 
 }  // extern "C"

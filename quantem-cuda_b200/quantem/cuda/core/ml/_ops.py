@@ -130,6 +130,79 @@ def _kpt_backward(ctx, grad_out):
 _kplanes_tilted_fuse.register_autograd(_kpt_backward, setup_context=_kpt_setup_context)
 
 
+# ── four-tap variant for finite-difference TV regularisation ──────────────
+#
+# The reference's kplanes_tilted_tv_fuse (core/ml/_ops.py:103-204): tap 0 at
+# R·x (the base op's values, bit for bit), taps 1..3 at R·x + h·R[:, k-1];
+# output [4, B, T*C] with the tap outermost; h carries no gradient.
+
+
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_tv_fuse", mutates_args=())
+def _kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
+    p = pts.contiguous()
+    r = rotations.contiguous()
+    c, hh, w = plane.shape[1:]
+    b = p.shape[0]
+    t = r.shape[0]
+    stream = _stream(p.device)
+    with torch.cuda.device(p.device):
+        g = _channels_last(plane, stream)
+        out = torch.empty((4, b, t * c), dtype=torch.float32, device=p.device)
+        _core.kplanes_tilted_tv_fuse_cuda(
+            p.data_ptr(), r.data_ptr(), g.data_ptr(), out.data_ptr(), b, t, c, hh, w, float(h), stream
+        )
+    return out
+
+
+@_kplanes_tilted_tv_fuse.register_fake
+def _(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
+    return pts.new_empty((4, pts.shape[0], rotations.shape[0] * plane.shape[1]))
+
+
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_tv_fuse_bwd", mutates_args=())
+def _kplanes_tilted_tv_fuse_bwd(
+    pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor, h: float
+) -> list[Tensor]:
+    p = pts.contiguous()
+    r = rotations.contiguous()
+    c, hh, w = plane.shape[1:]
+    b = p.shape[0]
+    t = r.shape[0]
+    stream = _stream(p.device)
+    with torch.cuda.device(p.device):
+        g = _channels_last(plane, stream)
+        gout = grad_out.detach().to(dtype=torch.float32, device=p.device).contiguous()
+        grad_pts = torch.zeros_like(p)
+        grad_r = torch.zeros_like(r)
+        grad_plane_cl = torch.zeros(g.shape, dtype=torch.float32, device=p.device)
+        _core.kplanes_tilted_tv_fuse_grad_cuda(
+            p.data_ptr(), r.data_ptr(), g.data_ptr(), gout.data_ptr(), grad_plane_cl.data_ptr(),
+            grad_r.data_ptr(), grad_pts.data_ptr(), b, t, c, hh, w, float(h), stream,
+        )
+        grad_plane = _from_channels_last(grad_plane_cl, plane, stream)
+    return [grad_pts, grad_r, grad_plane]
+
+
+@_kplanes_tilted_tv_fuse_bwd.register_fake
+def _(pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor, h: float) -> list[Tensor]:
+    return [torch.empty_like(pts), torch.empty_like(rotations), torch.empty_like(plane)]
+
+
+def _kpt_tv_setup_context(ctx, inputs, output) -> None:
+    pts, rotations, plane, h = inputs
+    ctx.save_for_backward(pts, rotations, plane)
+    ctx.h = h
+
+
+def _kpt_tv_backward(ctx, grad_out):
+    pts, rotations, plane = ctx.saved_tensors
+    grad_pts, grad_r, grad_plane = _kplanes_tilted_tv_fuse_bwd(pts, rotations, plane, grad_out, ctx.h)
+    return grad_pts, grad_r, grad_plane, None
+
+
+_kplanes_tilted_tv_fuse.register_autograd(_kpt_tv_backward, setup_context=_kpt_tv_setup_context)
+
+
 # ── public wrapper ────────────────────────────────────────────────────────
 
 
@@ -182,3 +255,31 @@ def kplanes_tilted_fuse(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor
     """
     _validate("kplanes_tilted_fuse", pts, rotations, plane)
     return _kplanes_tilted_fuse(pts, rotations, plane)
+
+
+def kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
+    """Four-tap tilted K-Planes interpolation for finite-difference TV.
+
+    For each point ``p`` and rotation ``R_t`` the ``kplanes_tilted_fuse``
+    features at four locations:
+
+        tap 0: R_t · p                 (bit-identical to kplanes_tilted_fuse)
+        tap 1: R_t · p + h · R_t[:, 0]  (= R_t · (p + h·e_x))
+        tap 2: R_t · p + h · R_t[:, 1]
+        tap 3: R_t · p + h · R_t[:, 2]
+
+    The rotation is evaluated once per (point, rotation) and the column
+    offsets once per rotation.
+
+    Args:
+        pts:       fp32 CUDA tensor ``[B, 3]``.
+        rotations: fp32 CUDA tensor ``[T, 3, 3]``.
+        plane:     fp32 CUDA tensor ``[3*T, C, H, W]``.
+        h:         finite-difference step in the ``[-1, 1]`` coordinates (no gradient).
+
+    Returns:
+        fp32 tensor ``[4, B, T*C]``, tap outermost, differentiable w.r.t.
+        pts, rotations and plane.
+    """
+    _validate("kplanes_tilted_tv_fuse", pts, rotations, plane)
+    return _kplanes_tilted_tv_fuse(pts, rotations, plane, float(h))

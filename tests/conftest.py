@@ -33,5 +33,11 @@ def kp_golden():
         return {k: z[k] for k in z.files}
 
 
+@pytest.fixture(scope="session")
+def kp_tv_golden():
+    with np.load(GOLDEN / "kplanes_tv_golden.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
 def golden_cases(data: dict) -> list[str]:
     return sorted({k.split("/")[0] for k in data})

@@ -6,6 +6,7 @@ live in its test files:
     tests/core/test_tv_loss.py:13-27      tv_iso_ref, tv_sq_ref
     tests/core/test_tv_loss.py:144-167    tv_l1_ref, ptycho_tv_ref
     tests/core/ml/test_kplanes_tilted.py:26-40  reference (einsum + grid_sample)
+    tests/core/ml/test_kplanes_tilted.py:200-220 reference_tv (four taps)
 This script imports those modules from a checkout of the reference (default
 /root/reference, or $QUANTEM_CUDA_REFERENCE), runs them on CPU with seeded
 CPU-generated inputs, and stores inputs, outputs and autograd gradients as
@@ -152,12 +153,61 @@ def make_kplanes(kpmod) -> dict:
     return out
 
 
+# four-tap K-Planes (N, T, C, H, W, h): the reference's tv test configs
+# (test_kplanes_tilted.py:191-197) scaled down, the fast path at C=8 and C=32,
+# and a border case whose taps cross the edge (:289-322).
+KP_TV_CASES = [
+    ("tv_37_1_1_5_5", (37, 1, 1, 5, 5), 0.05, 0),
+    ("tv_257_3_5_7_9", (257, 3, 5, 7, 9), 0.02, 1),
+    ("tv_c8_200_4_8_12_12", (200, 4, 8, 12, 12), 0.05, 2),
+    ("tv_c32_300_2_32_17_13", (300, 2, 32, 17, 13), 0.02, 3),
+]
+
+
+def make_kplanes_tv(kpmod) -> dict:
+    out = {}
+    for name, (N, T, C, H, W), h, seed in KP_TV_CASES:
+        gen = torch.Generator().manual_seed(3000 + seed)
+        pts = torch.empty((N, 3)).uniform_(-1.1, 1.1, generator=gen)
+        rot = torch.empty((T, 3, 3)).uniform_(-1.0, 1.0, generator=gen)
+        plane = torch.empty((3 * T, C, H, W)).uniform_(0.1, 0.5, generator=gen)
+        upstream = torch.randn((4, N, T * C), generator=gen)
+        out[f"{name}/h"] = np.float32(h)
+        for k, t in (("pts", pts), ("rotations", rot), ("plane", plane), ("upstream", upstream)):
+            out[f"{name}/{k}"] = t.numpy()
+        for dtype, tag in ((torch.float32, "f32"), (torch.float64, "f64")):
+            inp = tuple(t.to(dtype).requires_grad_(True) for t in (pts, rot, plane))
+            res = kpmod.reference_tv(*inp, h=h)
+            gp, gr, gg = torch.autograd.grad((res * upstream.to(dtype)).sum(), inp)
+            out[f"{name}/out_{tag}"] = res.detach().numpy()
+            out[f"{name}/grad_pts_{tag}"] = gp.numpy()
+            out[f"{name}/grad_rotations_{tag}"] = gr.numpy()
+            out[f"{name}/grad_plane_{tag}"] = gg.numpy()
+    T, C, H, W, h = 2, 4, 11, 11, 0.05
+    gen = torch.Generator().manual_seed(13)
+    rot = torch.stack([torch.eye(3), torch.eye(3).roll(1, 0)]).float()
+    plane = torch.empty((3 * T, C, H, W)).uniform_(0.1, 0.5, generator=gen)
+    pts = torch.tensor([[-1.0, -1.0, -1.0], [1.0, 1.0, 1.0], [0.98, 0.0, 0.0], [0.0, 0.98, 0.0],
+                        [0.0, 0.0, 0.98], [2.0, -3.0, 0.5]])
+    p = pts.clone().requires_grad_(True)
+    res = kpmod.reference_tv(p, rot, plane, h=h)
+    (gp,) = torch.autograd.grad(res.sum(), p)
+    out["tv_border/h"] = np.float32(h)
+    out["tv_border/pts"] = pts.numpy()
+    out["tv_border/rotations"] = rot.numpy()
+    out["tv_border/plane"] = plane.numpy()
+    out["tv_border/out_f32"] = res.detach().numpy()
+    out["tv_border/grad_pts_f32"] = gp.numpy()
+    return out
+
+
 def main() -> None:
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     tvmod, kpmod = _import_reference_tests()
     np.savez_compressed(HERE / "tv_golden.npz", **make_tv(tvmod))
     np.savez_compressed(HERE / "kplanes_golden.npz", **make_kplanes(kpmod))
-    for f in ("tv_golden.npz", "kplanes_golden.npz"):
+    np.savez_compressed(HERE / "kplanes_tv_golden.npz", **make_kplanes_tv(kpmod))
+    for f in ("tv_golden.npz", "kplanes_golden.npz", "kplanes_tv_golden.npz"):
         print(f, (HERE / f).stat().st_size, "bytes")
 
 

@@ -114,6 +114,9 @@ def test_peer_entries_reject_bad_arguments_without_a_device():
     with pytest.raises(RuntimeError, match="rank\\+1's slab missing"):
         _core.tv_slab_halo_exchange_cuda(_core.TvPeers(0, 2, 0, [16, 32], 0, 0, 0, 0), 1, 128, 1, 5, 4, 4, 0)
     with pytest.raises(RuntimeError, match="must include QC_TV_LOSS"):
-        _core.tv_loss_3d_slab_peer_cuda(good, 1, _core.TV_SQ, _core.TV_GRAD, 128, 0, 0, 256, 1, 5, 4, 4, 1, 4,
+        _core.tv_loss_3d_slab_peer_cuda(good, 0, 1, _core.TV_SQ, _core.TV_GRAD, 128, 0, 0, 256, 1, 5, 4, 4, 1, 4,
+                                        0, 1, 0.0, 1.0, 0, 0, 0)
+    with pytest.raises(RuntimeError, match="needs the slab layout"):
+        _core.tv_loss_3d_slab_peer_cuda(good, 1, 1, _core.TV_SQ, _core.TV_LOSS, 128, 0, 0, 256, 1, 5, 4, 4, 0, 4,
                                         0, 1, 0.0, 1.0, 0, 0, 0)
     assert _core.tv_peer_comm_bytes() >= 8 * 2 * 4 * 8

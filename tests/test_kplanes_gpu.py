@@ -275,7 +275,8 @@ def test_plane_layout_transposes(shape):
 
 @pytest.mark.parametrize("cfg", [(2000, 4, 32, 50, 33), (500, 3, 5, 9, 7), (300, 2, 16, 16, 16)])
 @pytest.mark.parametrize("channels_last", [False, True])
-def test_per_rotation_backward_matches_whole_backward(cfg, channels_last):
+@pytest.mark.parametrize("buckets", [1, 2, 4])
+def test_per_rotation_backward_matches_whole_backward(cfg, channels_last, buckets):
     """The multi-GPU path's per-rotation backward (one launch per rotation of
     kplanes_tilted_fuse_grad_rotations_cuda, each rotation's plane gradient put
     back in the parameter's layout at once) against the op on all rotations."""
@@ -287,7 +288,7 @@ def test_per_rotation_backward_matches_whole_backward(cfg, channels_last):
     g = plane.cuda()
     if channels_last:
         g = g.contiguous(memory_format=torch.channels_last)
-    out, g_pts, g_rot, g_plane, works = sharded._kplanes_fwd_bwd_bucketed(p, r, g, u, None, 1)
+    out, g_pts, g_rot, g_plane, works = sharded._kplanes_fwd_bwd_bucketed(p, r, g, u, None, 1, buckets)
     assert works == []
     ref_out = torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, g)
     ref_pts, ref_rot, ref_plane = torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, g, u)
@@ -305,3 +306,170 @@ def test_rotation_range_validation():
     with pytest.raises(RuntimeError, match="rotations \\[2, 5\\) outside \\[0, 4\\)"):
         _core.kplanes_tilted_fuse_grad_rotations_cuda(*(z.data_ptr(),) * 7, 1, 4, 4, 2, 2, 2, 5,
                                                      torch.cuda.current_stream().cuda_stream)
+
+
+# ── four-tap variant (kplanes_tilted_tv_fuse) ────────────────────────────────
+
+# the reference's tv configs (test_kplanes_tilted.py:191-197) and the fast path
+# at C = 4, 16, 64, 128
+TV_CONFIGS = [
+    (37, 1, 1, 5, 5),
+    (257, 3, 5, 7, 9),
+    (1024, 4, 8, 50, 50),
+    (2000, 4, 32, 33, 33),
+    (500, 2, 4, 20, 30),
+    (300, 3, 16, 16, 12),
+    (200, 2, 64, 9, 17),
+    (100, 2, 128, 8, 8),
+]
+
+
+def tv_grads(pts, rot, plane, up, h):
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    inp = [t.cuda().requires_grad_(True) for t in (pts, rot, plane)]
+    out = kplanes_tilted_tv_fuse(*inp, h=h)
+    (out * up.cuda()).sum().backward()
+    return out.detach(), [t.grad for t in inp]
+
+
+@pytest.mark.parametrize("cfg", TV_CONFIGS)
+def test_tv_forward_matches_oracle_and_base(cfg):
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    pts, rot, plane, _ = make_inputs(*cfg, seed=42)
+    p, r, g = pts.cuda(), rot.cuda(), plane.cuda()
+    out = kplanes_tilted_tv_fuse(p, r, g, h=0.05)
+    assert out.shape == (4, cfg[0], cfg[1] * cfg[2])
+    # tap 0 is the base op, bit for bit (test_kplanes_tilted.py:224-233)
+    torch.testing.assert_close(out[0], kplanes_tilted_fuse(p, r, g), rtol=0, atol=0)
+    ref = torch.from_numpy(oracle.kplanes_tv_fwd(pts.numpy(), rot.numpy(), plane.numpy(), 0.05))
+    torch.testing.assert_close(out.cpu(), ref, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("cfg", TV_CONFIGS)
+def test_tv_gradients_match_oracle(cfg):
+    N, T, C, H, W = cfg
+    pts, rot, plane, _ = make_inputs(*cfg, seed=43)
+    up = torch.randn((4, N, T * C), generator=torch.Generator().manual_seed(5))
+    _, (gp, gr, gg) = tv_grads(pts, rot, plane, up, 0.02)
+    o_gp, o_gr, o_gg = oracle.kplanes_tv_bwd(pts.numpy(), rot.numpy(), plane.numpy(), up.numpy(), 0.02)
+    assert_rel_max(gg, o_gg, 1e-4, "grad_plane")
+    assert_rel_max(gp, o_gp, 1e-4, "grad_pts")
+    assert_rel_max(gr, o_gr, 1e-4, "grad_rotations")
+
+
+def test_tv_golden_fixtures_fp64_anchored(kp_tv_golden):
+    """test_kplanes_tilted.py:249-286 on the committed fixtures (K = 4 for
+    rotations, 2 elsewhere)."""
+    names = sorted({k.split("/")[0] for k in kp_tv_golden if not k.startswith("tv_border")})
+    for name in names:
+        t = {k: torch.from_numpy(kp_tv_golden[f"{name}/{k}"]) for k in ("pts", "rotations", "plane", "upstream")}
+        h = float(kp_tv_golden[f"{name}/h"])
+        out, got = tv_grads(t["pts"], t["rotations"], t["plane"], t["upstream"], h)
+        torch.testing.assert_close(out.cpu(), torch.from_numpy(kp_tv_golden[f"{name}/out_f32"]), rtol=1e-4, atol=5e-6)
+        for label, mine in zip(("pts", "rotations", "plane"), got):
+            ref64 = kp_tv_golden[f"{name}/grad_{label}_f64"]
+            err_torch = np.abs(kp_tv_golden[f"{name}/grad_{label}_f32"].astype(np.float64) - ref64).max()
+            err_kernel = np.abs(mine.cpu().double().numpy() - ref64).max()
+            k = 4.0 if label == "rotations" else 2.0
+            assert err_kernel <= max(k * err_torch, 1e-6), (name, label, err_kernel, err_torch)
+
+
+def test_tv_border_points(kp_tv_golden):
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    pts, rot, plane = (torch.from_numpy(kp_tv_golden[f"tv_border/{k}"]).cuda() for k in ("pts", "rotations", "plane"))
+    h = float(kp_tv_golden["tv_border/h"])
+    p = pts.clone().requires_grad_(True)
+    out = kplanes_tilted_tv_fuse(p, rot, plane, h=h)
+    torch.testing.assert_close(out.cpu(), torch.from_numpy(kp_tv_golden["tv_border/out_f32"]), rtol=1e-4, atol=1e-6)
+    (g,) = torch.autograd.grad(out.sum(), p)
+    assert torch.isfinite(g).all()
+    torch.testing.assert_close(g.cpu(), torch.from_numpy(kp_tv_golden["tv_border/grad_pts_f32"]), rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("h_val", [2.0, 1e-4])
+def test_tv_edge_case_h(h_val):
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    pts, rot, plane, _ = make_inputs(256, 2, 8, 17, 17, seed=55)
+    inp = [t.cuda().requires_grad_(True) for t in (pts, rot, plane)]
+    out = kplanes_tilted_tv_fuse(*inp, h=h_val)
+    assert torch.isfinite(out).all()
+    out.sum().backward()
+    for t in inp:
+        assert torch.isfinite(t.grad).all()
+
+
+def test_tv_compile_fullgraph():
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    pts, rot, plane, _ = make_inputs(512, 2, 4, 17, 17, seed=56)
+    inp = [t.cuda().requires_grad_(True) for t in (pts, rot, plane)]
+
+    @torch.compile(fullgraph=True)
+    def f(p, r, g):
+        return kplanes_tilted_tv_fuse(p, r, g, h=0.01).square().mean()
+
+    f(*inp).backward()
+    assert all(t.grad is not None for t in inp)
+
+
+def test_tv_input_validation():
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    pts, rot, plane, _ = make_inputs(16, 2, 4, 9, 9, seed=57)
+    p, r, g = pts.cuda(), rot.cuda(), plane.cuda()
+    with pytest.raises(ValueError, match=r"pts \[B, 3\]"):
+        kplanes_tilted_tv_fuse(p[:, :2], r, g, h=0.01)
+    with pytest.raises(ValueError, match=r"rotations \[T, 3, 3\]"):
+        kplanes_tilted_tv_fuse(p, r[:, :2, :], g, h=0.01)
+    with pytest.raises(ValueError, match=r"3\*T"):
+        kplanes_tilted_tv_fuse(p, r, g[:3], h=0.01)
+    with pytest.raises(TypeError, match="fp32-only"):
+        kplanes_tilted_tv_fuse(p.double(), r, g, h=0.01)
+
+
+def test_tv_channels_last_plane_and_empty_points():
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    pts, rot, plane, up4 = make_inputs(300, 2, 8, 9, 11, seed=58)
+    up = torch.randn((4, 300, 16), generator=torch.Generator().manual_seed(6))
+    _, (gp, gr, gg) = tv_grads(pts, rot, plane, up, 0.03)
+    cl = plane.cuda().contiguous(memory_format=torch.channels_last).requires_grad_(True)
+    p, r = pts.cuda().requires_grad_(True), rot.cuda().requires_grad_(True)
+    (kplanes_tilted_tv_fuse(p, r, cl, h=0.03) * up.cuda()).sum().backward()
+    torch.testing.assert_close(cl.grad, gg, rtol=1e-5, atol=1e-6 * gg.abs().max().item())
+    assert cl.grad.stride() == cl.stride()
+    empty = kplanes_tilted_tv_fuse(pts[:0].cuda(), rot.cuda(), plane.cuda(), h=0.03)
+    assert empty.shape == (4, 0, 16)
+
+
+@pytest.mark.skipif(oracle.ref_core() is None, reason="reference _core not built into oracle/_ref")
+@pytest.mark.parametrize("cfg", [(2000, 4, 32, 33, 33), (257, 3, 5, 7, 9)])
+def test_tv_matches_reference_cuda_kernels(cfg):
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    ref = oracle.ref_core()
+    N, T, C, H, W = cfg
+    h = 0.05
+    pts, rot, plane, _ = make_inputs(*cfg, seed=59)
+    up = torch.randn((4, N, T * C), generator=torch.Generator().manual_seed(7)).cuda()
+    p, r = pts.cuda(), rot.cuda()
+    grid_cl = plane.cuda().permute(0, 2, 3, 1).contiguous()
+    st = torch.cuda.current_stream().cuda_stream
+    ref_out = torch.empty((4, N, T * C), device="cuda")
+    ref.kplanes_tilted_tv_fuse_cuda(p.data_ptr(), r.data_ptr(), grid_cl.data_ptr(), ref_out.data_ptr(), N, T, C, H, W,
+                                    h, st)
+    out = kplanes_tilted_tv_fuse(p, r, plane.cuda(), h=h)
+    torch.testing.assert_close(out, ref_out, rtol=0, atol=0)  # bit-exact with the reference kernel
+    gg = torch.zeros_like(grid_cl)
+    gr = torch.zeros_like(r)
+    gp = torch.zeros_like(p)
+    ref.kplanes_tilted_tv_fuse_grad_cuda(p.data_ptr(), r.data_ptr(), grid_cl.data_ptr(), up.data_ptr(), gg.data_ptr(),
+                                         gr.data_ptr(), gp.data_ptr(), N, T, C, H, W, h, st)
+    _, (m_gp, m_gr, m_gg) = tv_grads(pts, rot, plane, up.cpu(), h)
+    for mine, theirs, what in ((m_gg, gg.permute(0, 3, 1, 2), "plane"), (m_gr, gr, "rotations"), (m_gp, gp, "pts")):
+        err = (mine - theirs).abs().max().item()
+        assert err <= 1e-4 * theirs.abs().max().item(), (what, err)

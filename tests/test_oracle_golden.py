@@ -98,3 +98,47 @@ def test_kplanes_border_points(kp_golden):
     np.testing.assert_allclose(out, kp_golden["border/out_f32"], rtol=1e-5, atol=1e-6)
     gp, _, _ = oracle.kplanes_bwd(pts, rot, plane, np.ones_like(out))
     np.testing.assert_allclose(gp, kp_golden["border/grad_pts_f32"], rtol=1e-4, atol=1e-6)
+
+
+# ── four-tap K-Planes (reference_tv, test_kplanes_tilted.py:200-220) ─────────
+
+
+def _kp_tv_names(kp_tv_golden):
+    return [c for c in golden_cases(kp_tv_golden) if c != "tv_border"]
+
+
+def test_kplanes_tv_forward_matches_reference_tv(kp_tv_golden):
+    for name in _kp_tv_names(kp_tv_golden):
+        g = {k: kp_tv_golden[f"{name}/{k}"] for k in ("pts", "rotations", "plane")}
+        h = float(kp_tv_golden[f"{name}/h"])
+        out = oracle.kplanes_tv_fwd(g["pts"], g["rotations"], g["plane"], h)
+        assert out.shape == kp_tv_golden[f"{name}/out_f32"].shape
+        # tap 0 is the base forward, bit for bit
+        np.testing.assert_array_equal(out[0], oracle.kplanes_fwd(g["pts"], g["rotations"], g["plane"]))
+        # the reference test's tolerance for all four taps (test_kplanes_tilted.py:246)
+        np.testing.assert_allclose(out, kp_tv_golden[f"{name}/out_f32"], rtol=1e-4, atol=5e-6)
+        np.testing.assert_allclose(out, kp_tv_golden[f"{name}/out_f64"], rtol=1e-4, atol=5e-6)
+
+
+def test_kplanes_tv_gradients_fp64_anchored(kp_tv_golden):
+    # test_kplanes_tilted.py:249-286: error against the fp64 torch gradients no
+    # worse than K x torch's own fp32 error (K = 4 for rotations, 2 elsewhere).
+    for name in _kp_tv_names(kp_tv_golden):
+        g = {k: kp_tv_golden[f"{name}/{k}"] for k in ("pts", "rotations", "plane", "upstream")}
+        h = float(kp_tv_golden[f"{name}/h"])
+        got = oracle.kplanes_tv_bwd(g["pts"], g["rotations"], g["plane"], g["upstream"], h)
+        for label, mine in zip(("pts", "rotations", "plane"), got):
+            ref64 = kp_tv_golden[f"{name}/grad_{label}_f64"]
+            err_torch = np.abs(kp_tv_golden[f"{name}/grad_{label}_f32"].astype(np.float64) - ref64).max()
+            err_oracle = np.abs(mine.astype(np.float64) - ref64).max()
+            k = 4.0 if label == "rotations" else 2.0
+            assert err_oracle <= max(k * err_torch, 1e-6), (name, label, err_oracle, err_torch)
+
+
+def test_kplanes_tv_border_points(kp_tv_golden):
+    pts, rot, plane = (kp_tv_golden[f"tv_border/{k}"] for k in ("pts", "rotations", "plane"))
+    h = float(kp_tv_golden["tv_border/h"])
+    out = oracle.kplanes_tv_fwd(pts, rot, plane, h)
+    np.testing.assert_allclose(out, kp_tv_golden["tv_border/out_f32"], rtol=1e-4, atol=1e-6)
+    gp, _, _ = oracle.kplanes_tv_bwd(pts, rot, plane, np.ones_like(out), h)
+    np.testing.assert_allclose(gp, kp_tv_golden["tv_border/grad_pts_f32"], rtol=1e-4, atol=1e-6)

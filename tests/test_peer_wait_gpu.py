@@ -38,7 +38,7 @@ def test_unanswered_peer_waits_return_with_fault_bit():
         st = torch.cuda.current_stream().cuda_stream
         t0 = time.perf_counter()
         _core.tv_slab_halo_exchange_cuda(peers, 1, slab.data_ptr(), B, Dp, H, W, st)
-        _core.tv_loss_3d_slab_peer_cuda(peers, 1, _core.TV_SQ, _core.TV_LOSS | _core.TV_GRAD | _core.TV_ACC_OVERWRITE,
+        _core.tv_loss_3d_slab_peer_cuda(peers, 0, 1, _core.TV_SQ, _core.TV_LOSS | _core.TV_GRAD | _core.TV_ACC_OVERWRITE,
                                         slab.data_ptr(), g.data_ptr(), acc.data_ptr(), grad.data_ptr(),
                                         B, Dp, H, W, 1, Dp - 1, 0, 1, 0.0, 1.0, ws.data_ptr(), ws.numel(), st)
         torch.cuda.synchronize()

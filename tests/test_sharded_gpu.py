@@ -86,17 +86,19 @@ def test_dslab_over_nccl_matches_single_gpu():
 
 # ── D-slabs over peer memory (CUDA IPC, stores over NVLink) ──────────────────
 
-PEER_SHAPE = (2, 45, 40, 132)  # D split 23 + 22: slabs of different depth
+# D split 23 + 22 (slabs of different depth) on the TMA path, and an odd width
+# on the generic path (which exchanges with a separate kernel)
+PEER_SHAPES = [(2, 45, 40, 132), (1, 9, 7, 10)]
 PEER_STEPS = 3
 PEER_CASES = ((0, [1.5], 0.0), (1, [0.75], 1e-6), (2, [0.3, 1.1, 0.6], 0.0))  # SQ, ISO, L1
 
 
-def _peer_volume(step: int):
+def _peer_volume(shape, step: int):
     gen = torch.Generator().manual_seed(100 + step)
-    return torch.rand(PEER_SHAPE, generator=gen)
+    return torch.rand(shape, generator=gen)
 
 
-def _peer_worker(rank, world, port, queue):
+def _peer_worker(rank, world, port, queue, shape):
     import datetime
 
     import torch.distributed as dist
@@ -109,16 +111,22 @@ def _peer_worker(rank, world, port, queue):
     try:
         from quantem.cuda import _core, sharded
 
-        B, D, H, W = PEER_SHAPE
+        B, D, H, W = shape
         ps = sharded.PeerSlab(B, D, H, W, timeout_s=20.0)
         lo, hi = ps.d_lo, ps.d_hi
         out = []
         for step in range(PEER_STEPS):
             # the volume changes between steps, so stale halos would show
-            ps.owned.copy_(_peer_volume(step)[:, lo:hi].cuda())
+            ps.owned.copy_(_peer_volume(shape, step)[:, lo:hi].cuda())
             per = {}
             for variant, g, eps in PEER_CASES:
-                loss, grad = ps.fwd_grad(variant, torch.tensor(g), eps)
+                if step == 1:
+                    # the exchange as its own kernel, then the sweep without one
+                    ps.exchange_halos()
+                    loss, grad = ps.fwd_grad(variant, torch.tensor(g), eps, exchange=False)
+                else:
+                    # the exchange inside the sweep kernel
+                    loss, grad = ps.fwd_grad(variant, torch.tensor(g), eps)
                 per[variant] = (loss.cpu().numpy(), grad[:, 1:-1].cpu().numpy())
             out.append(per)
         fault = _core.device_fault_word(rank)
@@ -130,14 +138,15 @@ def _peer_worker(rank, world, port, queue):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_peer_slab_matches_single_gpu_over_steps():
+@pytest.mark.parametrize("shape", PEER_SHAPES)
+def test_peer_slab_matches_single_gpu_over_steps(shape):
     from quantem.cuda.core import tv_loss_iso_3d_fwd_grad, tv_loss_l1_3d_fwd_grad, tv_loss_sq_3d_fwd_grad
 
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q, shape)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=240) for _ in range(world)], key=lambda t: t[0])
@@ -148,7 +157,7 @@ def test_peer_slab_matches_single_gpu_over_steps():
         assert fault == 0, f"rank {rank} gave up waiting (fault word {fault:#x})"
     fns = {0: tv_loss_sq_3d_fwd_grad, 1: tv_loss_iso_3d_fwd_grad, 2: tv_loss_l1_3d_fwd_grad}
     for step in range(PEER_STEPS):
-        v = _peer_volume(step).cuda()
+        v = _peer_volume(shape, step).cuda()
         for variant, g, eps in PEER_CASES:
             kw = {"eps": eps} if variant == 1 else {}
             loss, grad = fns[variant](v, g[0] if len(g) == 1 else tuple(g), **kw)

@@ -48,6 +48,36 @@ def test_kplanes_cpu_rejected():
         kplanes_tilted_fuse(pts, rotations, plane)
 
 
+def test_kplanes_tv_cpu_rejected_and_messages():
+    from quantem.cuda.core.ml import kplanes_tilted_tv_fuse
+
+    pts = torch.rand(8, 3)
+    rotations = torch.rand(2, 3, 3)
+    plane = torch.rand(6, 4, 9, 9)
+    with pytest.raises(ValueError, match="CUDA"):
+        kplanes_tilted_tv_fuse(pts, rotations, plane, h=0.01)
+    with pytest.raises(ValueError, match=r"kplanes_tilted_tv_fuse expects pts \[B, 3\]"):
+        kplanes_tilted_tv_fuse(pts[:, :2], rotations, plane, h=0.01)
+    with pytest.raises(ValueError, match=r"3\*T"):
+        kplanes_tilted_tv_fuse(pts, rotations, plane[:3], h=0.01)
+    with pytest.raises(TypeError, match="kplanes_tilted_tv_fuse is fp32-only"):
+        kplanes_tilted_tv_fuse(pts.double(), rotations, plane, h=0.01)
+
+
+def test_kplanes_tv_fake_shapes():
+    from quantem.cuda.core.ml import _ops  # noqa: F401  (registers the ops)
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        p = torch.empty(10, 3, device="cuda")
+        r = torch.empty(2, 3, 3, device="cuda")
+        g = torch.empty(6, 8, 5, 5, device="cuda")
+        out = torch.ops.quantem_cuda.kplanes_tilted_tv_fuse(p, r, g, 0.1)
+        assert tuple(out.shape) == (4, 10, 16)
+        gp, gr, gg = torch.ops.quantem_cuda.kplanes_tilted_tv_fuse_bwd(p, r, g, out, 0.1)
+        assert tuple(gp.shape) == (10, 3) and tuple(gr.shape) == (2, 3, 3) and tuple(gg.shape) == (6, 8, 5, 5)
+
+
 def test_kplanes_shape_validation_messages():
     pts = torch.rand(16, 3)
     rotations = torch.rand(2, 3, 3)
@@ -72,6 +102,8 @@ def test_ops_registered_with_reference_names():
         "tv_loss_l1_3d_bwd",
         "kplanes_tilted_fuse",
         "kplanes_tilted_fuse_bwd",
+        "kplanes_tilted_tv_fuse",
+        "kplanes_tilted_tv_fuse_bwd",
     ):
         assert hasattr(torch.ops.quantem_cuda, name)
 
