@@ -454,7 +454,8 @@ __device__ __forceinline__ void row_flux_pairs(const ulonglong2 &c, const ulongl
                                                const ulonglong2 &dn, float right, f2 eps01,
                                                f2 eps23, bool s3_ok, const Gains &gn,
                                                ulonglong2 &Fd, ulonglong2 &Fh, ulonglong2 &Fw,
-                                               f2 &acc01, f2 &acc23, float &r1, float &r2) {
+                                               f2 &acc01, f2 &acc23, float &r0, float &r1,
+                                               float &r2) {
     const f2 dd01 = sub2(n.x, c.x), dd23 = sub2(n.y, c.y);
     const f2 dh01 = sub2(dn.x, c.x), dh23 = sub2(dn.y, c.y);
     const f2 w01 = pk2(hi2(c.x), lo2(c.y)), w23 = pk2(hi2(c.y), right);
@@ -478,14 +479,12 @@ __device__ __forceinline__ void row_flux_pairs(const ulonglong2 &c, const ulongl
         const float dh[4] = {lo2(dh01), hi2(dh01), lo2(dh23), hi2(dh23)};
         const float dw[4] = {lo2(dw01), hi2(dw01), lo2(dw23), hi2(dw23)};
         if (LOSS) {
-            float a0 = 0.f;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                a0 += fabsf(dd[j]);
+                r0 += fabsf(dd[j]);
                 r1 += fabsf(dh[j]);
                 r2 += fabsf(dw[j]);
             }
-            acc01 = add2(acc01, pk2(a0, 0.f));
         }
         if (GRAD) {
             Fd = make_ulonglong2(pk2(gsign_fast(gn.gd, dd[0]), gsign_fast(gn.gd, dd[1])),
@@ -790,20 +789,17 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                             if (!FULL && !row_ok) e01 = e23 = pk2(kInf, kInf);
                             ulonglong2 Fd, Fh, Fw;
                             f2 q01 = 0ull, q23 = 0ull;
-                            float q1l = 0.f, q2l = 0.f;
                             row_flux_pairs<V, LOSS, GRAD>(curp, nxt, dn, right, e01, e23, !last_quad, gn,
-                                                          Fd, Fh, Fw, q01, q23, q1l, q2l);
+                                                          Fd, Fh, Fw, q01, q23, l0, l1, l2);
                             if (LOSS) {
                                 if constexpr (V == QC_TV_ISO) {
                                     if (loss_lane && row_ok) {
                                         la01 = add2(la01, q01);
                                         la23 = add2(la23, q23);
                                     }
-                                } else {
+                                } else if constexpr (V == QC_TV_SQ) {
                                     la01 = add2(la01, q01);
                                     la23 = add2(la23, q23);
-                                    l1 += q1l;
-                                    l2 += q2l;
                                 }
                             }
                             if (GRAD) {
@@ -1101,13 +1097,25 @@ void choose_chunking(Plan &pl, int max_ctas, int halo_planes) {
     pl.n_units = (long long)pl.n_chunks * pl.n_cols;
 }
 
-// Fast-path geometry: rows per consumer warp, consumer warps, ring stages and
-// the CTAs per SM that registers are budgeted for. QC_TV_R, QC_TV_NW, QC_TV_S
-// and QC_TV_MINB override it at build time.
+// Fast-path geometry per variant: rows per consumer warp, consumer warps, ring
+// stages and the CTAs per SM that registers are budgeted for, chosen by timing
+// geometries on a B200 ([4, 256^3]): the L1 sweep, whose sign transfers need
+// the most registers, runs 16-row tiles at 4 CTAs per SM (8% faster than
+// 32-row tiles at 3); iso and sq keep 32-row tiles. QC_TV_R, QC_TV_NW, QC_TV_S
+// and QC_TV_MINB override all three at build time.
+template <int V>
+struct FastGeomFor {
 #ifdef QC_TV_R
-using FastGeom = Geom<QC_TV_R, QC_TV_NW, QC_TV_S, QC_TV_MINB>;
+    using type = Geom<QC_TV_R, QC_TV_NW, QC_TV_S, QC_TV_MINB>;
 #else
-using FastGeom = Geom<8, 4, 3, 3>;
+    using type = Geom<8, 4, 3, 3>;
+#endif
+};
+#ifndef QC_TV_R
+template <>
+struct FastGeomFor<QC_TV_L1> {
+    using type = Geom<4, 4, 4, 4>;
+};
 #endif
 
 template <int V, bool LOSS, bool GRAD>
@@ -1116,7 +1124,7 @@ int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, 
     int sms = 0;
     if (int st = device_sm_count(&sms)) return st;
     if (use_tma) {
-        using G = FastGeom;
+        using G = typename FastGeomFor<V>::type;
         EncodeTiledFn encode = nullptr;
         if (int st = get_encode_fn(&encode)) return st;
         // The tensor map is encoded through the driver API, which needs a

@@ -137,12 +137,19 @@ def _peer_worker(rank, world, port, queue, shape):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def _gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+# 2 ranks (both at an end of the volume), and 4 ranks (two interior ranks with
+# a neighbour on each side) where the box has them
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("shape", PEER_SHAPES)
-def test_peer_slab_matches_single_gpu_over_steps(shape):
+def test_peer_slab_matches_single_gpu_over_steps(shape, world):
     from quantem.cuda.core import tv_loss_iso_3d_fwd_grad, tv_loss_l1_3d_fwd_grad, tv_loss_sq_3d_fwd_grad
 
-    world = 2
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
