@@ -171,6 +171,7 @@ int tv_loss_3d_slab_cuda(int variant, int flags, const float *d_vol, const float
  * QC_FAULT_PEER_WAIT in the device fault word and (for the reduction) store
  * NaN in the loss, so a rank that stops never hangs the others. */
 #define QC_MAX_PEER_RANKS 8
+#define QC_TV_MAX_PEER_SUMS 8 /* loss sums one cross-rank finalize carries (iso 1 + L1 3 + sq 1 fit) */
 #define QC_IPC_HANDLE_BYTES 64
 #define QC_FAULT_TMA_WAIT 0x1u  /* a kernel gave up waiting for its own TMA copies */
 #define QC_FAULT_PEER_WAIT 0x2u /* a kernel gave up waiting for another rank */
@@ -225,6 +226,31 @@ int tv_loss_3d_slab_peer_cuda(const qc_tv_peers *peers, unsigned long long halo_
                               int H, int W, int d_lo, int d_hi, int has_prev, int has_next,
                               float eps, float acc_scale, void *d_workspace,
                               size_t workspace_bytes, cudaStream_t stream);
+
+/* Two-phase form, for several losses of one step with a single cross-rank
+ * wait: tv_loss_3d_slab_sweep_cuda launches one loss's sweep (gradient written
+ * as usual; with QC_TV_LOSS its CTA partial sums stay in d_workspace, their
+ * count in *n_partials), and tv_loss_3d_peer_finalize_cuda then turns the
+ * partials of up to QC_TV_MAX_PEER_SUMS sums (each term's workspace must stay
+ * untouched until then) into the rank-ordered global sums, one wait for all
+ * terms. peers may be NULL in the sweep call when halo_seq is 0. */
+typedef struct qc_tv_term {
+    const void *workspace; /* the sweep's workspace */
+    int n_partials;        /* as returned by the sweep */
+    int n_acc;             /* 1 (sq, iso) or 3 (L1) */
+    float *acc;            /* device sums, n_acc floats */
+    float acc_scale;       /* multiplies the global sums */
+    int overwrite;         /* acc = scale·Σ (else acc += scale·Σ) */
+} qc_tv_term;
+
+int tv_loss_3d_slab_sweep_cuda(const qc_tv_peers *peers, unsigned long long halo_seq, int variant,
+                               int flags, const float *d_vol, const float *d_g,
+                               float *d_grad_vol, int B, int Dp, int H, int W, int d_lo, int d_hi,
+                               int has_prev, int has_next, float eps, float acc_scale,
+                               void *d_workspace, size_t workspace_bytes, int *n_partials,
+                               cudaStream_t stream);
+int tv_loss_3d_peer_finalize_cuda(const qc_tv_peers *peers, unsigned long long seq,
+                                  const qc_tv_term *terms, int n_terms, cudaStream_t stream);
 
 /* ── tilted K-Planes ────────────────────────────────────────────────────── */
 

@@ -301,6 +301,51 @@ PYBIND11_MODULE(_core, m) {
         py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
 
     m.def(
+        "tv_loss_3d_slab_sweep_cuda",
+        [](py::object peers, unsigned long long halo_seq, int variant, int flags, uintptr_t vol,
+           uintptr_t g, uintptr_t grad, int B, int Dp, int H, int W, int d_lo, int d_hi,
+           int has_prev, int has_next, float eps, float scale, uintptr_t ws, size_t ws_bytes,
+           uintptr_t stream) {
+            const qc_tv_peers *pp = peers.is_none() ? nullptr : peers.cast<const qc_tv_peers *>();
+            int n = 0;
+            check(tv_loss_3d_slab_sweep_cuda(pp, halo_seq, variant, flags, ptr<const float>(vol),
+                                             ptr<const float>(g), ptr<float>(grad), B, Dp, H, W,
+                                             d_lo, d_hi, has_prev, has_next, eps, scale,
+                                             ptr<void>(ws), ws_bytes, &n, stream_of(stream)));
+            return n;
+        },
+        "One loss's sweep without its finalize; returns the number of CTA partials in ws.",
+        py::arg("peers"), py::arg("halo_seq"), py::arg("variant"), py::arg("flags"),
+        py::arg("vol_ptr"), py::arg("g_ptr"), py::arg("grad_ptr"), py::arg("B"), py::arg("Dp"),
+        py::arg("H"), py::arg("W"), py::arg("d_lo"), py::arg("d_hi"), py::arg("has_prev"),
+        py::arg("has_next"), py::arg("eps"), py::arg("acc_scale"), py::arg("ws_ptr"),
+        py::arg("ws_bytes"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_3d_peer_finalize_cuda",
+        [](const qc_tv_peers &peers, unsigned long long seq, py::list terms, uintptr_t stream) {
+            std::vector<qc_tv_term> ts;
+            for (auto item : terms) {
+                auto t = item.cast<py::tuple>();
+                if (t.size() != 6)
+                    throw std::invalid_argument(
+                        "term = (ws_ptr, n_partials, n_acc, acc_ptr, acc_scale, overwrite)");
+                qc_tv_term q{};
+                q.workspace = ptr<const void>(t[0].cast<uintptr_t>());
+                q.n_partials = t[1].cast<int>();
+                q.n_acc = t[2].cast<int>();
+                q.acc = ptr<float>(t[3].cast<uintptr_t>());
+                q.acc_scale = t[4].cast<float>();
+                q.overwrite = t[5].cast<bool>() ? 1 : 0;
+                ts.push_back(q);
+            }
+            check(tv_loss_3d_peer_finalize_cuda(&peers, seq, ts.data(), (int)ts.size(),
+                                                stream_of(stream)));
+        },
+        "Rank-ordered global sums of several sweeps' partials with one cross-rank wait.",
+        py::arg("peers"), py::arg("seq"), py::arg("terms"), py::arg("stream_ptr"));
+
+    m.def(
         "tv_loss_3d_slab_peer_cuda",
         [](const qc_tv_peers &peers, unsigned long long halo_seq, unsigned long long seq,
            int variant, int flags, uintptr_t vol, uintptr_t g, uintptr_t acc, uintptr_t grad,

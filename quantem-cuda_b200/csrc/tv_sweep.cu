@@ -249,8 +249,8 @@ struct PeerComm {
     unsigned long long filled[2];  // [s]: neighbour on side s has filled this rank's halo s
     unsigned int arrive;           // CTAs of this rank's exchange launch done storing
     unsigned int pad0[7];
-    unsigned long long red_flag[QC_MAX_PEER_RANKS];   // [q]: rank q's total is in the slot
-    double partials[2][QC_MAX_PEER_RANKS][4];         // [call & 1][q][accumulator]
+    unsigned long long red_flag[QC_MAX_PEER_RANKS];   // [q]: rank q's totals are in the slot
+    double partials[2][QC_MAX_PEER_RANKS][QC_TV_MAX_PEER_SUMS];  // [call & 1][q][sum]
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
@@ -993,33 +993,53 @@ __global__ void __launch_bounds__(kFinThreads) tv_finalize_kernel(const double *
     }
 }
 
-// The finalize of a D-sharded loss: the fixed-order total of this rank's CTA
-// partials goes into slot [seq & 1][rank] of every rank's block; after all
-// ranks' flags show `seq`, every rank adds the slots in rank order. A slot is
-// rewritten two calls later at the earliest, and a rank gets there only after
-// every rank has finished reading it (its own call seq+1 waited for all).
-__global__ void __launch_bounds__(kFinThreads) tv_finalize_peer_kernel(
-    const double *__restrict__ partials, int n_partials, int n_acc, float *__restrict__ acc,
-    float scale, int overwrite, qc_tv_peers peers, unsigned long long seq) {
+// The finalize of D-sharded losses: for each term (one loss's CTA partials),
+// the fixed-order total of this rank's partials; all of this rank's totals go
+// into slot [seq & 1][rank] of every rank's block, and after all ranks' flags
+// show `seq`, every rank adds the slots in rank order. A slot is rewritten two
+// calls later at the earliest, and a rank gets there only after every rank
+// has finished reading it (its own call seq+1 waited for all). Several losses
+// of one step share a single finalize, i.e. a single wait for the other ranks.
+struct FinTerm {
+    const double *partials;
+    int n_partials, n_acc;
+    float *acc;
+    float scale;
+    int overwrite;
+};
+struct FinTerms {
+    FinTerm t[QC_TV_MAX_PEER_SUMS];
+    int n;
+};
+
+__global__ void __launch_bounds__(kFinThreads) tv_finalize_peer_kernel(const FinTerms terms,
+                                                                       qc_tv_peers peers,
+                                                                       unsigned long long seq) {
     griddep_wait();
-    __shared__ double red[kAccSlots][kFinThreads];
+    __shared__ double red[kFinThreads];
+    __shared__ double tot[QC_TV_MAX_PEER_SUMS];
     __shared__ int gave_up;
-    for (int a = 0; a < n_acc; ++a) {
-        double t = 0.0;
-        for (int i = threadIdx.x; i < n_partials; i += kFinThreads)
-            t += partials[(size_t)i * kAccSlots + a];
-        red[a][threadIdx.x] = t;
-    }
     if (threadIdx.x == 0) gave_up = 0;
-    __syncthreads();
-    for (int s = kFinThreads / 2; s > 0; s >>= 1) {
-        if (threadIdx.x < s)
-            for (int a = 0; a < n_acc; ++a) red[a][threadIdx.x] += red[a][threadIdx.x + s];
-        __syncthreads();
+    int n_sums = 0;
+    for (int k = 0; k < terms.n; ++k) {
+        const FinTerm &tm = terms.t[k];
+        for (int a = 0; a < tm.n_acc; ++a, ++n_sums) {
+            double t = 0.0;
+            for (int i = threadIdx.x; i < tm.n_partials; i += kFinThreads)
+                t += tm.partials[(size_t)i * kAccSlots + a];
+            red[threadIdx.x] = t;
+            __syncthreads();
+            for (int s = kFinThreads / 2; s > 0; s >>= 1) {
+                if (threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
+                __syncthreads();
+            }
+            if (threadIdx.x == 0) tot[n_sums] = red[0];
+            __syncthreads();
+        }
     }
     const int slot = (int)(seq & 1ull);
-    if (threadIdx.x < n_acc) {
-        const double v = red[threadIdx.x][0];
+    if (threadIdx.x < n_sums) {
+        const double v = tot[threadIdx.x];
         for (int q = 0; q < peers.world; ++q)
             static_cast<PeerComm *>(peers.comm[q])->partials[slot][peers.rank][threadIdx.x] = v;
     }
@@ -1037,12 +1057,22 @@ __global__ void __launch_bounds__(kFinThreads) tv_finalize_peer_kernel(
         }
     }
     __syncthreads();
-    if (threadIdx.x < n_acc) {
+    if (threadIdx.x < n_sums) {
         double t = 0.0;
         for (int q = 0; q < peers.world; ++q)
             t += ld_relaxed_sys_f64(&self->partials[slot][q][threadIdx.x]);
-        const float v = gave_up ? __int_as_float(0x7fc00000) : (float)(t * (double)scale);
-        acc[threadIdx.x] = overwrite ? v : acc[threadIdx.x] + v;
+        tot[threadIdx.x] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int j = 0;
+        for (int k = 0; k < terms.n; ++k) {
+            const FinTerm &tm = terms.t[k];
+            for (int a = 0; a < tm.n_acc; ++a, ++j) {
+                const float v = gave_up ? __int_as_float(0x7fc00000) : (float)(tot[j] * (double)tm.scale);
+                tm.acc[a] = tm.overwrite ? v : tm.acc[a] + v;
+            }
+        }
     }
 }
 
@@ -1209,7 +1239,11 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
         int Dp, int H, int W, int d_lo, int d_hi, int has_prev, int has_next, float eps,
         float acc_scale, void *ws, size_t ws_bytes, cudaStream_t stream,
         const qc_tv_peers *peers = nullptr, unsigned long long seq = 0,
-        unsigned long long halo_seq = 0) {
+        unsigned long long halo_seq = 0, int *n_partials_out = nullptr) {
+    // n_partials_out != nullptr: launch the sweep only (its CTA partials stay
+    // in ws, *n_partials_out of them) for a later tv_loss_3d_peer_finalize_cuda.
+    const bool sweep_only = n_partials_out != nullptr;
+    if (sweep_only) *n_partials_out = 0;
     const bool want_loss = flags & QC_TV_LOSS, want_grad = flags & QC_TV_GRAD;
     QC_RETURN_IF(variant < QC_TV_SQ || variant > QC_TV_L1, QC_ERR_INVALID_ARGUMENT,
                  "tv: unknown variant %d", variant);
@@ -1239,7 +1273,7 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     }
     QC_RETURN_IF(!empty && vol == nullptr, QC_ERR_INVALID_ARGUMENT, "tv: null volume");
 
-    if (empty && peers == nullptr) {
+    if (empty && peers == nullptr && !sweep_only) {
         if (want_loss && (flags & QC_TV_ACC_OVERWRITE))
             QC_CUDA_TRY(cudaMemsetAsync(acc, 0, n_acc * sizeof(float), stream), "cudaMemsetAsync(acc)");
         return 0;
@@ -1293,6 +1327,10 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     }
     if (st) return st;
 
+    if (sweep_only) {
+        *n_partials_out = want_loss ? grid : 0;
+        return 0;
+    }
     if (want_loss) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(1);
@@ -1305,9 +1343,11 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         if (peers != nullptr) {
-            QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_peer_kernel, (const double *)partials,
-                                           grid, n_acc, acc, acc_scale,
-                                           (flags & QC_TV_ACC_OVERWRITE) ? 1 : 0, *peers, seq),
+            FinTerms terms{};
+            terms.n = 1;
+            terms.t[0] = FinTerm{partials, grid, n_acc, acc, acc_scale,
+                                 (flags & QC_TV_ACC_OVERWRITE) ? 1 : 0};
+            QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_peer_kernel, terms, *peers, seq),
                         "tv_finalize_peer_kernel launch");
         } else {
             QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_kernel, (const double *)partials, grid,
@@ -1630,3 +1670,64 @@ int tv_loss_3d_slab_peer_cuda(const qc_tv_peers *peers, unsigned long long halo_
 }
 
 }  // extern "C"
+
+extern "C" int tv_loss_3d_slab_sweep_cuda(const qc_tv_peers *peers, unsigned long long halo_seq,
+                                          int variant, int flags, const float *d_vol,
+                                          const float *d_g, float *d_grad_vol, int B, int Dp,
+                                          int H, int W, int d_lo, int d_hi, int has_prev,
+                                          int has_next, float eps, float acc_scale,
+                                          void *d_workspace, size_t workspace_bytes,
+                                          int *n_partials, cudaStream_t stream) {
+    using namespace qc::tv;
+    QC_RETURN_IF(n_partials == nullptr, QC_ERR_INVALID_ARGUMENT,
+                 "tv_loss_3d_slab_sweep_cuda: null n_partials");
+    if (halo_seq != 0) {
+        if (int st = check_peers(peers, 1)) return st;
+        QC_RETURN_IF(d_lo != 1 || d_hi != Dp - 1, QC_ERR_INVALID_ARGUMENT,
+                     "tv_loss_3d_slab_sweep_cuda: exchanging halos needs the slab layout "
+                     "(owned planes [1, Dp-1))");
+        QC_RETURN_IF((peers->rank > 0 && peers->prev_slab == nullptr) ||
+                         (peers->rank < peers->world - 1 && peers->next_slab == nullptr),
+                     QC_ERR_INVALID_ARGUMENT, "tv_loss_3d_slab_sweep_cuda: a neighbour's slab is missing");
+    }
+    // a dummy acc satisfies run()'s argument checks; the sweep never writes it
+    static float unused_acc;
+    return run(variant, flags, d_vol, d_g, &unused_acc, d_grad_vol, B, Dp, H, W, d_lo, d_hi,
+               has_prev, has_next, eps, acc_scale, d_workspace, workspace_bytes, stream,
+               halo_seq != 0 ? peers : nullptr, 0, halo_seq, n_partials);
+}
+
+extern "C" int tv_loss_3d_peer_finalize_cuda(const qc_tv_peers *peers, unsigned long long seq,
+                                             const qc_tv_term *terms, int n_terms,
+                                             cudaStream_t stream) {
+    using namespace qc::tv;
+    if (int st = check_peers(peers, seq)) return st;
+    QC_RETURN_IF(terms == nullptr || n_terms < 1 || n_terms > QC_TV_MAX_PEER_SUMS,
+                 QC_ERR_INVALID_ARGUMENT, "tv_loss_3d_peer_finalize_cuda: %d terms", n_terms);
+    FinTerms ft{};
+    int sums = 0;
+    for (int k = 0; k < n_terms; ++k) {
+        const qc_tv_term &t = terms[k];
+        QC_RETURN_IF(t.acc == nullptr || t.n_acc < 1 || t.n_acc > kAccSlots || t.n_partials < 0 ||
+                         t.n_partials > kMaxPartials || (t.n_partials > 0 && t.workspace == nullptr),
+                     QC_ERR_INVALID_ARGUMENT, "tv_loss_3d_peer_finalize_cuda: bad term %d", k);
+        sums += t.n_acc;
+        ft.t[k] = FinTerm{static_cast<const double *>(t.workspace), t.n_partials, t.n_acc, t.acc,
+                          t.acc_scale, t.overwrite ? 1 : 0};
+    }
+    QC_RETURN_IF(sums > QC_TV_MAX_PEER_SUMS, QC_ERR_INVALID_ARGUMENT,
+                 "tv_loss_3d_peer_finalize_cuda: %d sums exceed %d", sums, QC_TV_MAX_PEER_SUMS);
+    ft.n = n_terms;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kFinThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_peer_kernel, ft, *peers, seq),
+                "tv_finalize_peer_kernel launch");
+    return 0;
+}

@@ -352,6 +352,7 @@ class PeerSlab:
         from quantem.cuda._common import _workspace
 
         self._ws = _workspace(self.device)
+        self._ws_many = []
         self._halo_seq = 0
         self._red_seq = 0
         dist.barrier(group=group)
@@ -404,6 +405,49 @@ class PeerSlab:
                 int(self.rank > 0), int(self.rank < self.world - 1), float(eps), float(scale),
                 self._ws.data_ptr(), self._ws.numel(), torch.cuda.current_stream(self.device).cuda_stream)
         return (acc.squeeze(0) if variant != L1 else acc), grad
+
+    def fwd_grad_many(self, terms, exchange: bool = True, grads=None):
+        """Several losses of one step over the same slab with a single
+        cross-rank wait: ``terms`` is a list of ``(variant, grad_out, eps)``;
+        each sweep writes its own gradient (``grads[k]`` if given), and one
+        finalize kernel adds every loss over the ranks in rank order. Returns
+        ``[(loss, grad), ...]`` in the order of ``terms``. The halos are
+        exchanged by the first sweep when ``exchange``."""
+        from quantem.cuda import _core
+        from quantem.cuda._common import _workspace
+
+        b, dp, h, w = self.shape
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if len(self._ws_many) < len(terms):
+            self._ws_many += [_workspace(self.device) for _ in range(len(terms) - len(self._ws_many))]
+        fin, out = [], []
+        with torch.cuda.device(self.device):
+            for k, (variant, grad_out, eps) in enumerate(terms):
+                halo_seq = 0
+                if exchange and k == 0:
+                    self._halo_seq += 1
+                    halo_seq = self._halo_seq
+                scale = 1.0
+                if variant == ISO:
+                    scale = 1.0 / max(1, b * (self.global_d - 1) * (h - 1) * (w - 1))
+                grad = None if grads is None else grads[k]
+                if grad is None:
+                    grad = torch.empty(self.shape, dtype=torch.float32, device=self.device)
+                g = grad_out.to(device=self.device, dtype=torch.float32).contiguous()
+                if g.numel() != _N_ACC[variant]:
+                    raise ValueError(f"grad_out needs {_N_ACC[variant]} element(s), got {g.numel()}")
+                acc = torch.empty(_N_ACC[variant], dtype=torch.float32, device=self.device)
+                ws = self._ws_many[k]
+                n = _core.tv_loss_3d_slab_sweep_cuda(
+                    self._peers, halo_seq, variant, _LOSS | _GRAD, self._slab_mem.ptr, g.data_ptr(),
+                    grad.data_ptr(), b, dp, h, w, 1, dp - 1, int(self.rank > 0),
+                    int(self.rank < self.world - 1), float(eps), float(scale), ws.data_ptr(), ws.numel(),
+                    stream)
+                fin.append((ws.data_ptr(), n, _N_ACC[variant], acc.data_ptr(), float(scale), True))
+                out.append(((acc.squeeze(0) if variant != L1 else acc), grad))
+            self._red_seq += 1
+            _core.tv_loss_3d_peer_finalize_cuda(self._peers, self._red_seq, fin, stream)
+        return out
 
     def close(self) -> None:
         """Unmaps the peers' memory after every rank has finished with it.

@@ -119,7 +119,12 @@ def _peer_worker(rank, world, port, queue, shape):
             # the volume changes between steps, so stale halos would show
             ps.owned.copy_(_peer_volume(shape, step)[:, lo:hi].cuda())
             per = {}
-            for variant, g, eps in PEER_CASES:
+            if step == 2:
+                # all three losses with one cross-rank finalize
+                res = ps.fwd_grad_many([(v, torch.tensor(g), eps) for v, g, eps in PEER_CASES])
+                for (variant, _, _), (loss, grad) in zip(PEER_CASES, res):
+                    per[variant] = (loss.cpu().numpy(), grad[:, 1:-1].cpu().numpy())
+            for variant, g, eps in PEER_CASES if step < 2 else ():
                 if step == 1:
                     # the exchange as its own kernel, then the sweep without one
                     ps.exchange_halos()
