@@ -600,9 +600,15 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
             bwd()
     else:
         # one channels-last copy of the planes for both passes, one backward
-        # launch, then the plane- and rotation-gradient all_reduce
-        # (--kp-buckets > 1 overlaps per-bucket all_reduces with the backward)
-        fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u, buckets=ctx.args.kp_buckets))
+        # launch, then the plane- and rotation-gradient sum over the ranks:
+        # by default one kernel over peer memory (deterministic, rank order);
+        # --kp-reduce nccl uses NCCL all_reduce (--kp-buckets > 1 overlaps
+        # per-bucket all_reduces with the backward)
+        if ctx.args.kp_reduce == "peer":
+            reducer = sharded.kplanes_gradient_reducer(g, r)
+            fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u, reducer=reducer))
+        else:
+            fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u, buckets=ctx.args.kp_buckets))
 
         def step():
             fb()
@@ -611,6 +617,8 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
     ms = time_steps(ctx, step, steps, warmup, sampler)
     ms_step = ms / steps
     f_ms, b_ms = t_f.mean_ms(steps), t_b.mean_ms(steps)
+    if ctx.world > 1 and ctx.args.kp_reduce == "peer":
+        reducer.close()
     if ctx.world > 1:
         f_ms = None  # b_ms covers the whole sharded forward + backward
     P = 3 * T * C * plane.shape[2] * plane.shape[3] * 4
@@ -646,10 +654,13 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         "value": N * ctx.world / (ms_step / 1e3),
         "unit": "points/s",
         "ms_per_step": ms_step,
-        "gpu_launches": (5 if ctx.world == 1 else 2 + 2 * min(max(ctx.args.kp_buckets, 1), T)) * steps,
+        "gpu_launches": (5 if ctx.world == 1 else
+                         (5 if ctx.args.kp_reduce == "peer" else 2 + 2 * min(max(ctx.args.kp_buckets, 1), T))) * steps,
         "config": {"workload": DESCRIPTIONS["kplanes"],
                    "points_per_gpu": N,
-                   "parallelism": f"points{ctx.world} (gradient buckets {ctx.args.kp_buckets})" if ctx.world > 1 else "single GPU",
+                   "parallelism": (f"points{ctx.world} (gradient sum: {ctx.args.kp_reduce}"
+                                   + (f", buckets {ctx.args.kp_buckets})" if ctx.args.kp_reduce == "nccl" else ")"))
+                   if ctx.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (512 MiB output + 512 MiB upstream gradient per step)",
                    "fwd_op_ms": f_ms, "bwd_op_ms": b_ms},
         "roofline": {"bound": "hbm",
@@ -729,6 +740,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tv_iso_l1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kp-reduce", choices=("peer", "nccl"), default="peer",
+                    help="multi-GPU K-Planes: gradient sum over peer memory or with NCCL all_reduce")
     ap.add_argument("--kp-buckets", type=int, default=1,
                     help="multi-GPU K-Planes: backward launches whose gradient all_reduce overlaps the next")
     ap.add_argument("--tv-transport", choices=("peer", "nccl"), default="peer",

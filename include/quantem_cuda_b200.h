@@ -252,6 +252,30 @@ int tv_loss_3d_slab_sweep_cuda(const qc_tv_peers *peers, unsigned long long halo
 int tv_loss_3d_peer_finalize_cuda(const qc_tv_peers *peers, unsigned long long seq,
                                   const qc_tv_term *terms, int n_terms, cudaStream_t stream);
 
+/* ── sum of one fp32 buffer over the GPUs of a node, over peer memory ──────
+ *
+ * No counterpart in the reference. Every rank's buffer (n floats, allocated
+ * with quantem_cuda_peer_alloc) and communication block
+ * (peer_allreduce_comm_bytes) are mapped into every process. One kernel:
+ * rank r adds chunk r of all buffers in rank order and stores the sum into
+ * chunk r of every buffer, so after the call every buffer holds the sum,
+ * bitwise identical on every rank and run to run. `seq` numbers the calls
+ * (1, 2, ...; the same on every rank). Waits on other ranks are bounded
+ * (timeout_ns, 0: 10 s) and set QC_FAULT_PEER_WAIT in the word that
+ * peer_allreduce_fault_word reads. */
+typedef struct qc_peer_group {
+    int rank;
+    int world;
+    unsigned long long timeout_ns;
+    void *comm[QC_MAX_PEER_RANKS];  /* every rank's communication block, mapped here */
+    float *buf[QC_MAX_PEER_RANKS];  /* every rank's buffer, mapped here (buf[rank] own) */
+} qc_peer_group;
+
+size_t peer_allreduce_comm_bytes(void);
+int peer_allreduce_sum_f32_cuda(const qc_peer_group *group, unsigned long long seq, long long n,
+                                cudaStream_t stream);
+int peer_allreduce_fault_word(int device, unsigned int *word, int clear);
+
 /* ── tilted K-Planes ────────────────────────────────────────────────────── */
 
 /* out[b, t*C + c] = Π_{p∈XY,ZX,YZ} bilinear(grid[t*3+p], (R_t·pts_b) pair p), with

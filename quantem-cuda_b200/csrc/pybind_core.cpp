@@ -32,6 +32,24 @@ T *ptr(uintptr_t v) {
 
 cudaStream_t stream_of(uintptr_t v) { return reinterpret_cast<cudaStream_t>(v); }
 
+qc_peer_group make_group(int rank, int world, unsigned long long timeout_ns,
+                         const std::vector<uintptr_t> &comm, const std::vector<uintptr_t> &buf) {
+    if (world < 1 || world > QC_MAX_PEER_RANKS || (int)comm.size() != world ||
+        (int)buf.size() != world)
+        throw std::invalid_argument("PeerGroup: need 1 <= world <= " +
+                                    std::to_string(QC_MAX_PEER_RANKS) +
+                                    " and one communication block and buffer per rank");
+    qc_peer_group g{};
+    g.rank = rank;
+    g.world = world;
+    g.timeout_ns = timeout_ns;
+    for (int q = 0; q < world; ++q) {
+        g.comm[q] = ptr<void>(comm[q]);
+        g.buf[q] = ptr<float>(buf[q]);
+    }
+    return g;
+}
+
 qc_tv_peers make_peers(int rank, int world, unsigned long long timeout_ns,
                        const std::vector<uintptr_t> &comm, uintptr_t prev_slab, int prev_dp,
                        uintptr_t next_slab, int next_dp) {
@@ -281,6 +299,27 @@ PYBIND11_MODULE(_core, m) {
         py::arg("handle"));
     m.def("ipc_close", [](uintptr_t p) { check(quantem_cuda_ipc_close(ptr<void>(p))); },
           py::arg("ptr"));
+
+    py::class_<qc_peer_group>(m, "PeerGroup")
+        .def(py::init(&make_group), py::arg("rank"), py::arg("world"), py::arg("timeout_ns"),
+             py::arg("comm"), py::arg("buf"))
+        .def_readonly("rank", &qc_peer_group::rank)
+        .def_readonly("world", &qc_peer_group::world);
+    m.def("peer_allreduce_comm_bytes", &peer_allreduce_comm_bytes);
+    m.def(
+        "peer_allreduce_sum_f32_cuda",
+        [](const qc_peer_group &g, unsigned long long seq, long long n, uintptr_t stream) {
+            check(peer_allreduce_sum_f32_cuda(&g, seq, n, stream_of(stream)));
+        },
+        py::arg("group"), py::arg("seq"), py::arg("n"), py::arg("stream_ptr"));
+    m.def(
+        "peer_allreduce_fault_word",
+        [](int device, bool clear) {
+            unsigned int w = 0;
+            check(peer_allreduce_fault_word(device, &w, clear ? 1 : 0));
+            return w;
+        },
+        py::arg("device"), py::arg("clear") = false);
 
     py::class_<qc_tv_peers>(m, "TvPeers")
         .def(py::init(&make_peers), py::arg("rank"), py::arg("world"), py::arg("timeout_ns"),

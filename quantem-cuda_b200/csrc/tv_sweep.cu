@@ -47,6 +47,7 @@
 // programmatic dependent launch, sums the slots in fixed order.
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -63,6 +64,7 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;       // 2 s per barrier wait
 constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;  // default bound of a wait for another rank
 
 constexpr int kMaxPartials = 2048;  // CTA partial-sum slots in the workspace
+constexpr int kMaxDevices = 64;     // per-device host-side caches
 constexpr int kAccSlots = 3;        // L1 keeps one sum per axis
 
 // ── per-variant arithmetic ───────────────────────────────────────────────
@@ -1180,13 +1182,18 @@ int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, 
                              (long long)pl.B * pl.Dp);
         auto kern = tv_sweep_tma_kernel<V, LOSS, GRAD, G>;
         const size_t smem = sizeof(SweepSmem<G>) + 128;
-        // Above 48 KB of dynamic shared memory needs an opt-in; it is a
-        // per-device function attribute, so set it on every launch (cheap).
-        QC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                    "cudaFuncSetAttribute(tv_sweep_tma_kernel)");
-        int occ = 0;
-        QC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, G::Threads, smem),
-                    "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        // Above 48 KB of dynamic shared memory needs an opt-in, a per-device
+        // function attribute; it and the occupancy it allows are looked up
+        // once per device (host-side cost off the per-call path).
+        static std::atomic<int> occ_cache[kMaxDevices];
+        int occ = (dev >= 0 && dev < kMaxDevices) ? occ_cache[dev].load(std::memory_order_relaxed) : 0;
+        if (occ <= 0) {
+            QC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                        "cudaFuncSetAttribute(tv_sweep_tma_kernel)");
+            QC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, G::Threads, smem),
+                        "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+            if (dev >= 0 && dev < kMaxDevices && occ > 0) occ_cache[dev].store(occ, std::memory_order_relaxed);
+        }
         int max_ctas = occ * sms;
         if (max_ctas > kMaxPartials) max_ctas = kMaxPartials;
         if (max_ctas < 1) max_ctas = 1;
@@ -1201,9 +1208,15 @@ int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, 
         *grid_out = grid;
     } else {
         auto kern = tv_sweep_generic_kernel<V, LOSS, GRAD>;
-        int occ = 0;
-        QC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kGenThreads, 0),
-                    "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        int dev = 0;
+        QC_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+        static std::atomic<int> occ_cache[kMaxDevices];
+        int occ = (dev >= 0 && dev < kMaxDevices) ? occ_cache[dev].load(std::memory_order_relaxed) : 0;
+        if (occ <= 0) {
+            QC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kGenThreads, 0),
+                        "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+            if (dev >= 0 && dev < kMaxDevices && occ > 0) occ_cache[dev].store(occ, std::memory_order_relaxed);
+        }
         int max_ctas = occ * sms;
         if (max_ctas > kMaxPartials) max_ctas = kMaxPartials;
         if (max_ctas < 1) max_ctas = 1;

@@ -168,6 +168,7 @@ def kplanes_fwd_bwd_sharded(
     async_op: bool = False,
     fwd_bwd: Callable | None = None,
     buckets: int = 1,
+    reducer: "PeerAllReduce | None" = None,
 ):
     """Forward and backward of one K-Planes level over point-sharded ranks.
 
@@ -187,6 +188,11 @@ def kplanes_fwd_bwd_sharded(
     hides (the collective's SMs and L2 traffic slow the L2-bound backward:
     2.61 ms per step with 4 buckets against 2.16 ms with one), so the default
     is a single backward launch followed by the all_reduce.
+
+    ``reducer`` (a :func:`kplanes_gradient_reducer` built once per level)
+    replaces the NCCL all_reduce: the backward accumulates straight into the
+    reducer's peer-memory buffer and one kernel sums it over the ranks in rank
+    order (deterministic, identical on every rank); ``work`` is then None.
     """
     _, world = _rank_world(group)
     if fwd_bwd is not None:
@@ -197,6 +203,9 @@ def kplanes_fwd_bwd_sharded(
                 dist.all_reduce(g_plane, group=group, async_op=True),
                 dist.all_reduce(g_rot, group=group, async_op=True),
             ]
+    elif reducer is not None:
+        out, g_pts, g_rot, g_plane = _kplanes_fwd_bwd_peer(pts_local, rotations, plane, grad_out_local, reducer)
+        works = []
     else:
         out, g_pts, g_rot, g_plane, works = _kplanes_fwd_bwd_bucketed(
             pts_local, rotations, plane, grad_out_local, group, world, buckets)
@@ -213,6 +222,43 @@ def kplanes_fwd_bwd_sharded(
             work.wait()
             work = None
     return out, g_pts, g_rot, g_plane, work
+
+
+def _kplanes_fwd_bwd_peer(pts, rotations, plane, grad_out, reducer):
+    from quantem.cuda import _core
+    from quantem.cuda.core.ml._ops import _channels_last, _from_channels_last
+
+    dev = pts.device
+    p = pts.contiguous()
+    r = rotations.contiguous()
+    t_count = r.shape[0]
+    c, h, w = plane.shape[1:]
+    n = p.shape[0]
+    P = plane.numel()
+    if reducer.numel < P + r.numel():
+        raise ValueError(f"reducer holds {reducer.numel} floats; the gradients need {P + r.numel()}")
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        g = _channels_last(plane, stream)
+        out = torch.empty((n, t_count * c), dtype=torch.float32, device=dev)
+        _core.kplanes_tilted_fuse_cuda(p.data_ptr(), r.data_ptr(), g.data_ptr(), out.data_ptr(),
+                                       n, t_count, c, h, w, stream)
+        gout = grad_out.detach().to(dtype=torch.float32, device=dev).contiguous()
+        g_pts = torch.zeros_like(p)
+        buf = reducer.buffer
+        buf[: P + r.numel()].zero_()
+        g_cl = buf[:P].view(3 * t_count, h, w, c)
+        g_rot = buf[P : P + r.numel()].view(t_count, 3, 3)
+        _core.kplanes_tilted_fuse_grad_cuda(p.data_ptr(), r.data_ptr(), g.data_ptr(), gout.data_ptr(),
+                                            g_cl.data_ptr(), g_rot.data_ptr(), g_pts.data_ptr(),
+                                            n, t_count, c, h, w, stream)
+        reducer.all_reduce()
+        # the reducer's buffer is reused by the next call: hand out copies
+        g_plane = _from_channels_last(g_cl, plane, stream)
+        if g_plane.data_ptr() == g_cl.data_ptr():
+            g_plane = g_plane.clone(memory_format=torch.channels_last)
+        g_rot = g_rot.clone()
+    return out, g_pts, g_rot, g_plane
 
 
 def _kplanes_fwd_bwd_bucketed(pts, rotations, plane, grad_out, group, world, buckets=1):
@@ -463,3 +509,77 @@ class PeerSlab:
                 _core.ipc_close(p)
         self._mapped = None
         dist.barrier(group=self.group)
+
+
+class PeerAllReduce:
+    """A float32 buffer of ``numel`` elements on every rank, summed over the
+    ranks in place by one kernel over peer memory (CUDA IPC on the GPUs of one
+    node): rank r adds chunk r of all buffers in rank order and stores it into
+    every buffer, so the result is bitwise identical on every rank and from
+    run to run. Every rank constructs it together and calls :meth:`all_reduce`
+    in the same order (one stream per rank)."""
+
+    def __init__(self, numel: int, group=None, device: torch.device | None = None, timeout_s: float = 10.0):
+        from quantem.cuda import _core
+
+        rank, world = _rank_world(group)
+        if world > _core.MAX_PEER_RANKS:
+            raise ValueError(f"PeerAllReduce supports at most {_core.MAX_PEER_RANKS} ranks, got {world}")
+        self.group, self.rank, self.world, self.numel = group, rank, world, int(numel)
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self._buf_mem = _PeerAllocation((self.numel,), "<f4", 4, self.device)
+        self._comm_mem = _PeerAllocation((int(_core.peer_allreduce_comm_bytes()),), "|u1", 1, self.device)
+        self.buffer = torch.as_tensor(self._buf_mem, device=self.device)
+        with torch.cuda.device(self.device):
+            mine = (_core.ipc_handle(self._buf_mem.ptr), _core.ipc_handle(self._comm_mem.ptr))
+        infos = [None] * world
+        dist.all_gather_object(infos, mine, group=group)
+        self._mapped: list[int] = []
+        bufs, comms = [], []
+        with torch.cuda.device(self.device):
+            for q, (buf_h, comm_h) in enumerate(infos):
+                if q == rank:
+                    bufs.append(self._buf_mem.ptr)
+                    comms.append(self._comm_mem.ptr)
+                    continue
+                b = int(_core.ipc_open(buf_h))
+                c = int(_core.ipc_open(comm_h))
+                self._mapped += [b, c]
+                bufs.append(b)
+                comms.append(c)
+        self._group = _core.PeerGroup(rank, world, int(timeout_s * 1e9), comms, bufs)
+        self._seq = 0
+        dist.barrier(group=group)
+
+    def all_reduce(self) -> Tensor:
+        """Sums ``buffer`` over the ranks in place (kernel on the current
+        stream) and returns it."""
+        from quantem.cuda import _core
+
+        self._seq += 1
+        with torch.cuda.device(self.device):
+            _core.peer_allreduce_sum_f32_cuda(self._group, self._seq, self.numel,
+                                              torch.cuda.current_stream(self.device).cuda_stream)
+        return self.buffer
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (collective)."""
+        from quantem.cuda import _core
+
+        if self._mapped is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._mapped:
+                _core.ipc_close(p)
+        self._mapped = None
+        dist.barrier(group=self.group)
+
+
+def kplanes_gradient_reducer(plane: Tensor, rotations: Tensor, group=None) -> PeerAllReduce:
+    """A :class:`PeerAllReduce` sized for one K-Planes level's plane and
+    rotation gradients (``3T·H·W·C + 9T`` floats), for
+    :func:`kplanes_fwd_bwd_sharded`'s ``reducer``."""
+    n = plane.numel() + rotations.numel()
+    return PeerAllReduce(n, group=group, device=plane.device)

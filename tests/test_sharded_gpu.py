@@ -213,10 +213,21 @@ def _kp_worker(rank, world, port, queue):
 
         pts, rot, plane, up = _kp_inputs()
         lo, hi = sharded.slab_bounds(pts.shape[0], rank, world)
-        out, g_pts, g_rot, g_plane, work = sharded.kplanes_fwd_bwd_sharded(
-            pts[lo:hi].cuda(), rot.cuda(), plane.cuda(), up[lo:hi].cuda(), async_op=True)
+        p, r, g, u = pts[lo:hi].cuda(), rot.cuda(), plane.cuda(), up[lo:hi].cuda()
+        out, g_pts, g_rot, g_plane, work = sharded.kplanes_fwd_bwd_sharded(p, r, g, u, async_op=True)
         work.wait()
-        queue.put((rank, lo, hi, out.cpu(), g_pts.cpu(), g_rot.cpu(), g_plane.cpu()))
+        # the same step with the gradients summed over peer memory, twice
+        reducer = sharded.kplanes_gradient_reducer(g, r)
+        for _ in range(2):
+            _, pg_pts, pg_rot, pg_plane, pwork = sharded.kplanes_fwd_bwd_sharded(p, r, g, u, reducer=reducer)
+        assert pwork is None
+        torch.cuda.synchronize()
+        from quantem.cuda import _core
+
+        fault = _core.peer_allreduce_fault_word(rank)
+        reducer.close()
+        queue.put((rank, lo, hi, out.cpu(), g_pts.cpu(), g_rot.cpu(), g_plane.cpu(),
+                   pg_pts.cpu(), pg_rot.cpu(), pg_plane.cpu(), fault))
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
@@ -238,10 +249,69 @@ def test_kplanes_point_sharding_matches_single_gpu():
     pts, rot, plane, up = (t.cuda() for t in _kp_inputs())
     out = torch.ops.quantem_cuda.kplanes_tilted_fuse(pts, rot, plane).cpu()
     ref_pts, ref_rot, ref_plane = (t.cpu() for t in torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(pts, rot, plane, up))
-    for rank, lo, hi, r_out, r_pts, r_rot, r_plane in res:
+    for rank, lo, hi, r_out, r_pts, r_rot, r_plane, p_pts, p_rot, p_plane, fault in res:
+        assert fault == 0
         assert torch.equal(r_out, out[lo:hi])
-        torch.testing.assert_close(r_pts, ref_pts[lo:hi], rtol=1e-4, atol=1e-5 * ref_pts.abs().max().item())
-        torch.testing.assert_close(r_rot, ref_rot, rtol=1e-4, atol=1e-4 * ref_rot.abs().max().item())
-        torch.testing.assert_close(r_plane, ref_plane, rtol=1e-4, atol=1e-5 * ref_plane.abs().max().item())
-    # the all_reduce gives every rank the same gradients
+        for gp, gr, gg in ((r_pts, r_rot, r_plane), (p_pts, p_rot, p_plane)):
+            torch.testing.assert_close(gp, ref_pts[lo:hi], rtol=1e-4, atol=1e-5 * ref_pts.abs().max().item())
+            torch.testing.assert_close(gr, ref_rot, rtol=1e-4, atol=1e-4 * ref_rot.abs().max().item())
+            torch.testing.assert_close(gg, ref_plane, rtol=1e-4, atol=1e-5 * ref_plane.abs().max().item())
+    # both reductions give every rank the same gradients
     assert torch.equal(res[0][5], res[1][5]) and torch.equal(res[0][6], res[1][6])
+    assert torch.equal(res[0][8], res[1][8]) and torch.equal(res[0][9], res[1][9])
+
+
+
+# ── the peer-memory all-reduce on its own ────────────────────────────────────
+
+
+def _allreduce_worker(rank, world, port, queue):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from quantem.cuda import _core, sharded
+
+        n = 1_000_003  # not a multiple of 4 x world: exercises the tail
+        red = sharded.PeerAllReduce(n, timeout_s=20.0)
+        outs = []
+        for call in range(3):
+            gen = torch.Generator().manual_seed(1000 * call + rank)
+            red.buffer.copy_(torch.randn(n, generator=gen).cuda())
+            outs.append(red.all_reduce().cpu().clone())
+        torch.cuda.synchronize()
+        queue.put((rank, outs, _core.peer_allreduce_fault_word(rank)))
+        red.close()
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_allreduce_is_the_rank_ordered_sum(world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_allreduce_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=240) for _ in range(world)], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    n = 1_000_003
+    for call in range(3):
+        parts = [torch.randn(n, generator=torch.Generator().manual_seed(1000 * call + r)) for r in range(world)]
+        expect = parts[0].clone()
+        for x in parts[1:]:
+            expect += x  # fp32, rank order: what the kernel computes
+        for rank, outs, fault in res:
+            assert fault == 0
+            assert torch.equal(outs[call], expect), (rank, call)
