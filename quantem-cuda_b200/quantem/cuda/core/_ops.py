@@ -380,3 +380,12 @@ def ptycho_tv_loss(array: Tensor, weight: tuple[float, float]) -> Tensor:
     wt = sums.new_tensor([wz, wxy, wxy])
     active = max(1, int(wz > 0) + 2 * int(wxy > 0))
     return (wt * sums / counts).sum() / active
+
+
+def tv_vol_loss(volume: Tensor, weight: float) -> Tensor:
+    """quantem's ``tv_vol`` volume regulariser: ``weight`` times the squared
+    anisotropic TV sum of :func:`tv_loss_sq_3d` divided by the number of
+    voxels (the scaling the reference's docstring names, core/_ops.py:170-172).
+    A zero weight returns an exact zero that still carries a (zero) gradient."""
+    loss = tv_loss_sq_3d(volume)
+    return loss * (float(weight) / max(1, volume.numel()))

@@ -146,9 +146,9 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-# 2 ranks (both at an end of the volume), and 4 ranks (two interior ranks with
-# a neighbour on each side) where the box has them
-@pytest.mark.parametrize("world", [2, 4])
+# 2 ranks (both at an end of the volume), and 4 and 8 ranks (interior ranks
+# with a neighbour on each side) where the box has them
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("shape", PEER_SHAPES)
 def test_peer_slab_matches_single_gpu_over_steps(shape, world):
     from quantem.cuda.core import tv_loss_iso_3d_fwd_grad, tv_loss_l1_3d_fwd_grad, tv_loss_sq_3d_fwd_grad
@@ -292,7 +292,7 @@ def _allreduce_worker(rank, world, port, queue):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_peer_allreduce_is_the_rank_ordered_sum(world):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")

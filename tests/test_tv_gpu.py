@@ -153,6 +153,20 @@ def test_ptycho_recipe(tv_golden, key):
     torch.testing.assert_close(a.grad.cpu(), torch.from_numpy(tv_golden[f"{key}/grad"]), rtol=1e-4, atol=1e-7)
 
 
+@pytest.mark.parametrize("weight", [0.5, 0.0])
+def test_tv_vol_scaling(weight):
+    from quantem.cuda.core import tv_vol_loss
+
+    x = rand_vol((12, 20, 33), 15)
+    v = x.cuda().requires_grad_(True)
+    loss = tv_vol_loss(v, weight)
+    expect = weight * oracle.tv_sq_loss(x.numpy()) / x.numel()
+    np.testing.assert_allclose(loss.item(), expect, rtol=FWD_RTOL, atol=1e-12)
+    loss.backward()
+    ref = oracle.tv_sq_grad(x.numpy(), weight / x.numel())
+    assert_grad_close(v.grad, ref)
+
+
 def test_deterministic_losses():
     v = rand_vol((2, 40, 70, 260), 14).cuda()
     for fn in (lambda x: tv_loss_iso_3d(x), tv_loss_sq_3d, tv_loss_l1_3d):
