@@ -180,16 +180,18 @@ def tv_iso_l1_volume(seed: int, d: int = 256) -> torch.Tensor:
     return vol
 
 
-def blob_volume(n: int, seed: int, device) -> torch.Tensor:
-    """Sum of 64 Gaussian blobs (centres U[0, n)^3, sigma U[8, 64], amplitude 1)
-    + N(0, 0.01) noise, built on the device plane by plane."""
+def blob_volume(n: int, seed: int, device, z0: int = 0, z1: int | None = None) -> torch.Tensor:
+    """Planes [z0, z1) of an [n, n, n] volume: sum of 64 Gaussian blobs
+    (centres U[0, n)^3, sigma U[8, 64], amplitude 1) + N(0, 0.01) noise, built
+    on the device plane by plane (each plane's noise seeded by its index, so a
+    D-slab of the volume does not depend on how the volume is split)."""
+    z1 = n if z1 is None else z1
     gen = torch.Generator().manual_seed(seed)
     centres = torch.rand((64, 3), generator=gen) * n
     sigmas = 8 + torch.rand(64, generator=gen) * 56
-    vol = torch.empty((n, n, n), device=device)
+    vol = torch.empty((z1 - z0, n, n), device=device)
     ax = torch.arange(n, device=device, dtype=torch.float32)
-    gd = torch.Generator(device=device).manual_seed(seed)
-    for z in range(n):
+    for z in range(z0, z1):
         plane = torch.zeros((n, n), device=device)
         for (cz, cy, cx), s in zip(centres.tolist(), sigmas.tolist()):
             wz = math.exp(-((z - cz) ** 2) / (2 * s * s))
@@ -198,7 +200,8 @@ def blob_volume(n: int, seed: int, device) -> torch.Tensor:
             gy = torch.exp(-((ax - cy) ** 2) / (2 * s * s))
             gx = torch.exp(-((ax - cx) ** 2) / (2 * s * s))
             plane += wz * gy[:, None] * gx[None, :]
-        vol[z] = plane + 0.01 * torch.randn((n, n), device=device, generator=gd)
+        gd = torch.Generator(device=device).manual_seed(seed * 1_000_003 + z)
+        vol[z - z0] = plane + 0.01 * torch.randn((n, n), device=device, generator=gd)
     return vol
 
 
@@ -365,6 +368,81 @@ def cpu_kplanes(sample_n: int = 1 << 14, min_seconds: float = 10.0, reps: int | 
         "sample": f"first {sample_n} of the 2^20 points, forward + backward with the C oracle "
         f"(OpenMP), {k} reps, {el:.3f} s",
     }, per_step
+
+
+def cpu_tv_1024(sample_d: int = 4, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
+    oracle, threads = cpu_oracle()
+    x = blob_volume(1024, 4, "cpu", 510, 510 + sample_d).numpy()
+    voxels = x.size
+
+    def step():
+        oracle.tv_sq_loss(x)
+        oracle.tv_sq_grad(x, 1.0)
+        oracle.tv_iso_sum(x, 1e-8)
+        oracle.tv_iso_grad(x, 1.0, 1e-8)
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    k = 0
+    while True:
+        step()
+        k += 1
+        el = time.perf_counter() - t0
+        if (reps is not None and k >= reps) or (reps is None and el >= min_seconds):
+            break
+    per_step = el / k
+    return {
+        "value": voxels / per_step,
+        "unit": "voxels/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"[{sample_d}, 1024, 1024] slab (planes 510..) of the volume: sq loss + grad and iso "
+        f"loss + grad with the C oracle (OpenMP), {k} reps, {el:.3f} s",
+    }, per_step
+
+
+def cpu_kplanes_ms(sample_n: int = 2048, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
+    oracle, threads = cpu_oracle()
+    gen = torch.Generator().manual_seed(3)
+    pts = torch.empty((sample_n, 3)).uniform_(-1.0, 1.0, generator=gen).numpy()
+    rot = quaternion_rotations(8, gen).numpy()
+    planes = [torch.empty((24, 32, r, r)).uniform_(0.1, 0.5, generator=gen).numpy() for r in (64, 128, 256, 512)]
+    up = torch.randn((sample_n, 256), generator=gen).numpy()
+
+    def step():
+        for g in planes:
+            oracle.kplanes_fwd(pts, rot, g)
+            oracle.kplanes_bwd(pts, rot, g, up)
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    k = 0
+    while True:
+        step()
+        k += 1
+        el = time.perf_counter() - t0
+        if (reps is not None and k >= reps) or (reps is None and el >= min_seconds):
+            break
+    per_step = el / k
+    return {
+        "value": sample_n / per_step,
+        "unit": "points/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{sample_n} points through all four levels (T=8, C=32), forward + backward with the "
+        f"C oracle (OpenMP), {k} reps, {el:.3f} s",
+    }, per_step
+
+
+CPU_BASELINES = {
+    "tv_iso_l1": lambda **k: cpu_tv_iso_l1(**k),
+    "tv_sq_128": lambda **k: cpu_tv_iso_l1(**k),
+    "tv_1024": lambda **k: cpu_tv_1024(**k),
+    "kplanes": lambda **k: cpu_kplanes(**k),
+    "kplanes_ms": lambda **k: cpu_kplanes_ms(**k),
+}
 
 
 # ── workloads (ours) ────────────────────────────────────────────────────────
@@ -546,36 +624,150 @@ def run_tv_sq_128(ctx: Ctx, steps: int, warmup: int) -> dict:
 
 
 def run_tv_1024(ctx: Ctx, steps: int, warmup: int) -> dict:
+    """The tomography-scale volume [1024, 1024, 1024]: sq + iso single-sweep
+    fwd+grad. On N GPUs the volume is split along D into N slabs (strong
+    scaling: the job's volume is fixed), halos and the two loss sums over
+    peer memory."""
+    from quantem.cuda import sharded
     from quantem.cuda.core import tv_loss_iso_3d_fwd_grad, tv_loss_sq_3d_fwd_grad
 
-    vol = blob_volume(1024, 4, ctx.device)
-    g1 = torch.ones(1, device=ctx.device)
+    n = 1024
+    dev = ctx.device
+    g1 = torch.ones(1, device=dev)
     t_sq, t_iso = KernelTimer(), KernelTimer()
-    sq = t_sq.wrap(lambda: tv_loss_sq_3d_fwd_grad(vol, g1))
-    iso = t_iso.wrap(lambda: tv_loss_iso_3d_fwd_grad(vol, g1, eps=1e-8))
+    if ctx.world == 1:
+        vol = blob_volume(n, 4, dev)
+        sq = t_sq.wrap(lambda: tv_loss_sq_3d_fwd_grad(vol, g1))
+        iso = t_iso.wrap(lambda: tv_loss_iso_3d_fwd_grad(vol, g1, eps=1e-8))
 
-    def step():
-        sq()
-        iso()
+        def step():
+            sq()
+            iso()
 
+        local_voxels = vol.numel()
+        launches = 4
+    else:
+        ps = sharded.PeerSlab(1, n, n, n, device=dev)
+        ps.owned.copy_(blob_volume(n, 4, dev, ps.d_lo, ps.d_hi).unsqueeze(0))
+        grads = [torch.empty_like(ps.slab), torch.empty_like(ps.slab)]
+        terms = [(sharded.SQ, g1, 0.0), (sharded.ISO, g1, 1e-8)]
+        both = t_sq.wrap(lambda: ps.fwd_grad_many(terms, exchange=True, grads=grads))
+
+        def step():
+            both()
+
+        local_voxels = (ps.d_hi - ps.d_lo) * n * n
+        launches = 3
     sampler = ClockSampler(ctx.local_rank)
     ms = time_steps(ctx, step, steps, warmup, sampler)
     ms_step = ms / steps
     peak, peak_kind = measured_hbm_peak()
-    dom_ms = max(t_sq.mean_ms(steps), t_iso.mean_ms(steps))
-    algo = 8.0 * vol.numel()
+    if ctx.world == 1:
+        per_loss = {"sq": t_sq.mean_ms(steps), "iso": t_iso.mean_ms(steps)}
+        dom_ms = max(per_loss.values())
+        kernel = "tv single sweep (the slower of sq and iso)"
+    else:
+        per_loss = {"sq_plus_iso": t_sq.mean_ms(steps)}
+        dom_ms = per_loss["sq_plus_iso"] / 2
+        kernel = "tv sq + iso sweeps with one cross-rank finalize (per sweep, per rank)"
+        ps.close()
+    algo = 8.0 * local_voxels
     return {
         "metric": "TV fwd+grad voxels/sec",
-        "value": vol.numel() * ctx.world / (ms_step / 1e3),
+        "value": n ** 3 / (ms_step / 1e3),
         "unit": "voxels/s",
         "ms_per_step": ms_step,
-        "gpu_launches": 4 * steps,
+        "scaling": "strong" if ctx.world > 1 else "weak",
+        "gpu_launches": launches * steps,
         "config": {"workload": DESCRIPTIONS["tv_1024"],
-                   "l2": "inputs larger than L2 (4 GiB)",
-                   "per_loss_ms": {"sq": t_sq.mean_ms(steps), "iso": t_iso.mean_ms(steps)}},
-        "roofline": {"bound": "hbm", "kernel": "tv single sweep", "achieved": algo / (dom_ms / 1e3) / 1e9,
+                   "global_shape": [n, n, n],
+                   "parallelism": f"d-slab{ctx.world} (peer)" if ctx.world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (4 GiB volume)",
+                   "per_loss_ms": per_loss},
+        "roofline": {"bound": "hbm", "kernel": kernel, "achieved": algo / (dom_ms / 1e3) / 1e9,
                      "peak": peak, "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
                      "frac": algo / (dom_ms / 1e3) / 1e9 / peak, "traffic": None, "algorithmic_bytes": algo},
+        "clocks": sampler.summary(),
+        "e2e": None,
+        "dtype": "f32",
+    }
+
+
+def kplanes_ms_inputs(world: int, rank: int, device):
+    """The multiscale configuration: 4 levels at 64/128/256/512, N = 2^24
+    points U[-1, 1]^3 (this rank's contiguous share), R = 8 rotations from
+    normalised N(0,1) quaternions, C = 32, planes U[0.1, 0.5], upstream
+    gradient N(0, 1) per level (drawn on the device from a seeded generator:
+    17 GB per level at one GPU)."""
+    from quantem.cuda import sharded
+
+    n_total, T, C = 1 << 24, 8, 32
+    gen = torch.Generator().manual_seed(3)
+    pts = torch.empty((n_total, 3)).uniform_(-1.0, 1.0, generator=gen)
+    rot = quaternion_rotations(T, gen)
+    planes = [torch.empty((3 * T, C, r, r)).uniform_(0.1, 0.5, generator=gen) for r in (64, 128, 256, 512)]
+    lo, hi = sharded.slab_bounds(n_total, rank, world)
+    p = pts[lo:hi].to(device)
+    gd = torch.Generator(device=device).manual_seed(3 + rank)
+    ups = [torch.randn((hi - lo, T * C), device=device, generator=gd) for _ in planes]
+    return p, rot.to(device), [g.to(device) for g in planes], ups, n_total
+
+
+def run_kplanes_ms(ctx: Ctx, steps: int, warmup: int) -> dict:
+    """Multiscale K-Planes fwd+bwd over 4 levels, N = 2^24 points split over
+    the ranks (strong scaling), plane and rotation gradients of each level
+    summed over the ranks over peer memory right after its backward."""
+    from quantem.cuda import sharded
+
+    dev = ctx.device
+    p, r, planes, ups, n_total = kplanes_ms_inputs(ctx.world, ctx.rank, dev)
+    T, C = r.shape[0], planes[0].shape[1]
+    reducers = [sharded.kplanes_gradient_reducer(g, r) for g in planes] if ctx.world > 1 else None
+    timers = [KernelTimer() for _ in planes]
+
+    def level(k):
+        if ctx.world > 1:
+            return sharded.kplanes_fwd_bwd_sharded(p, r, planes[k], ups[k], reducer=reducers[k])
+        out = torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, planes[k])
+        grads = torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, planes[k], ups[k])
+        return out, grads
+
+    runs = [t.wrap(lambda k=k: level(k)) for k, t in enumerate(timers)]
+
+    def step():
+        for run in runs:
+            run()  # each level's output and gradients are released before the next
+
+    sampler = ClockSampler(ctx.local_rank)
+    ms = time_steps(ctx, step, steps, warmup, sampler)
+    ms_step = ms / steps
+    if reducers is not None:
+        for red in reducers:
+            red.close()
+    n_local = p.shape[0]
+    P = [g.numel() * 4 for g in planes]
+    # per rank: out + upstream (2·4·N·R·C) + points (12 N fwd, 12 N bwd, 12 N gpts)
+    # per level, plus plane, plane gradient read-modify-write (3 P) per level
+    algo = sum(2 * 4 * n_local * T * C + 36 * n_local + 3 * pl for pl in P)
+    peak, peak_kind = measured_hbm_peak()
+    lvl_ms = [t.mean_ms(steps) for t in timers]
+    return {
+        "metric": "K-Planes fwd+bwd points/sec",
+        "value": n_total / (ms_step / 1e3),
+        "unit": "points/s",
+        "ms_per_step": ms_step,
+        "scaling": "strong" if ctx.world > 1 else "weak",
+        "gpu_launches": (5 if ctx.world == 1 else 6) * len(planes) * steps,
+        "config": {"workload": DESCRIPTIONS["kplanes_ms"],
+                   "points_per_gpu": n_local,
+                   "parallelism": f"points{ctx.world} (gradient sum: peer)" if ctx.world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (17 GB output + 17 GB upstream gradient per level at 1 GPU)",
+                   "level_ms": dict(zip(("64", "128", "256", "512"), lvl_ms))},
+        "roofline": {"bound": "hbm", "kernel": "all four levels' fwd+bwd (per rank, step)",
+                     "achieved": algo / (ms_step / 1e3) / 1e9, "peak": peak,
+                     "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
+                     "frac": algo / (ms_step / 1e3) / 1e9 / peak, "traffic": None,
+                     "algorithmic_bytes": algo},
         "clocks": sampler.summary(),
         "e2e": None,
         "dtype": "f32",
@@ -617,8 +809,6 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
     ms = time_steps(ctx, step, steps, warmup, sampler)
     ms_step = ms / steps
     f_ms, b_ms = t_f.mean_ms(steps), t_b.mean_ms(steps)
-    if ctx.world > 1 and ctx.args.kp_reduce == "peer":
-        reducer.close()
     if ctx.world > 1:
         f_ms = None  # b_ms covers the whole sharded forward + backward
     P = 3 * T * C * plane.shape[2] * plane.shape[3] * 4
@@ -648,6 +838,29 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
         e2e = {"value": N / (e2e_ms / steps / 1e3), "unit": "points/s",
                "h2d_bytes_per_step": sum(t.numel() * 4 for t in (hp, hr, hg, hu)), "d2h_bytes_per_step": 4}
+    else:
+        # each rank brings its points and upstream gradient in from pinned host
+        # memory (planes and rotations are parameters resident on the device)
+        # and reads the summed rotation gradient back
+        hp, hu = pts.pin_memory(), up.pin_memory()
+        res_host = torch.empty(T * 9, pin_memory=True)
+
+        def e2e_step():
+            pp = hp.to(dev, non_blocking=True)
+            uu = hu.to(dev, non_blocking=True)
+            if ctx.args.kp_reduce == "peer":
+                _, _, g_rot, _, _ = sharded.kplanes_fwd_bwd_sharded(pp, r, g, uu, reducer=reducer)
+            else:
+                _, _, g_rot, _, _ = sharded.kplanes_fwd_bwd_sharded(pp, r, g, uu, buckets=ctx.args.kp_buckets)
+            res_host.copy_(g_rot.reshape(-1), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
+        e2e = {"value": N * ctx.world / (e2e_ms / steps / 1e3), "unit": "points/s",
+               "h2d_bytes_per_step": (hp.numel() + hu.numel()) * 4 * ctx.world,
+               "d2h_bytes_per_step": T * 9 * 4 * ctx.world}
+    if ctx.world > 1 and ctx.args.kp_reduce == "peer":
+        reducer.close()
 
     return {
         "metric": "K-Planes fwd+bwd points/sec",
@@ -682,6 +895,7 @@ DESCRIPTIONS = {
     "tv_sq_128": "tv_sq_128: tv_loss_sq_3d single-sweep fwd+grad on [128,128,128]",
     "tv_1024": "tv_1024: tv_loss_sq_3d + tv_loss_iso_3d single-sweep fwd+grad on [1024]^3 blobs",
     "kplanes": "kplanes: kplanes_tilted_fuse fwd + bwd ops, N=2^20, T=4, C=32, 256^2",
+    "kplanes_ms": "kplanes_ms: multiscale kplanes_tilted_fuse fwd + bwd, 4 levels 64/128/256/512, N=2^24, T=8, C=32",
 }
 
 WORKLOADS = {
@@ -689,6 +903,7 @@ WORKLOADS = {
     "tv_sq_128": run_tv_sq_128,
     "tv_1024": run_tv_1024,
     "kplanes": run_kplanes,
+    "kplanes_ms": run_kplanes_ms,
 }
 
 
@@ -699,12 +914,8 @@ def run_reference(ctx: Ctx, args) -> dict | None:
     if ctx.rank != 0:
         return None
     warmup = max(args.warmup, 3)
-    if args.workload in ("kplanes",):
-        cb, per_step = cpu_kplanes(reps=args.steps, warmup=warmup)
-        metric = "K-Planes fwd+bwd points/sec"
-    else:
-        cb, per_step = cpu_tv_iso_l1(reps=args.steps, warmup=warmup)
-        metric = "TV fwd+grad voxels/sec"
+    cb, per_step = CPU_BASELINES[args.workload](reps=args.steps, warmup=warmup)
+    metric = "K-Planes fwd+bwd points/sec" if args.workload.startswith("kplanes") else "TV fwd+grad voxels/sec"
     return {
         "metric": metric,
         "value": cb["value"],
@@ -769,10 +980,7 @@ def main() -> None:
     res = WORKLOADS[args.workload](ctx, args.steps, warmup)
 
     if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
-        if args.workload == "kplanes":
-            res["cpu_baseline"], _ = cpu_kplanes()
-        else:
-            res["cpu_baseline"], _ = cpu_tv_iso_l1()
+        res["cpu_baseline"], _ = CPU_BASELINES[args.workload]()
 
     if ctx.world > 1:
         dist.barrier(device_ids=[ctx.local_rank])
@@ -787,7 +995,7 @@ def main() -> None:
             "warmup": warmup,
             "ms_per_step": res.pop("ms_per_step"),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": res.pop("scaling", "weak"),
             "vs_baseline": None,
             "dtype": res.pop("dtype"),
             "data": "synthetic",

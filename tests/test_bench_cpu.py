@@ -1,0 +1,44 @@
+"""Host-side pieces of bench.py: synthetic inputs that do not depend on how
+the job is split over ranks, the committed ncu traffic lines, and the
+reference arm's single JSON line on stdout."""
+
+from __future__ import annotations
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(REPO))
+
+import bench  # noqa: E402
+
+
+def test_blob_volume_slabs_match_the_whole_volume():
+    whole = bench.blob_volume(24, 4, "cpu")
+    for z0, z1 in ((0, 7), (7, 16), (16, 24)):
+        torch.testing.assert_close(bench.blob_volume(24, 4, "cpu", z0, z1), whole[z0:z1], rtol=0, atol=0)
+
+
+def test_committed_traffic_lines_parse():
+    tv = bench.ncu_traffic("tv_iso_l1")
+    kp = bench.ncu_traffic("kplanes")
+    assert tv is not None and tv["unit"] == "voxel" and 7.0 < tv["bytes_per_unit"] < 9.0
+    assert kp is not None and kp["unit"] == "point" and kp["bytes_per_unit"] > 100
+
+
+def test_reference_arm_prints_one_json_line():
+    out = subprocess.run(
+        [sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--workload", "tv_iso_l1",
+         "--steps", "1", "--warmup", "1"],
+        capture_output=True, text=True, timeout=600, cwd=REPO,
+    )
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1
+    res = json.loads(lines[0])
+    assert res["impl"] == "reference" and res["unit"] == "voxels/s" and res["value"] > 0
+    assert res["cpu_baseline"]["kind"] == "port" and res["e2e"]["h2d_bytes_per_step"] == 0
