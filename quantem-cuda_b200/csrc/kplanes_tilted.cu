@@ -709,6 +709,7 @@ int bwd_v4(const float *pts, const float *R, const float *grid, const float *gou
 template <int NT>
 int forward(const char *who, const float *d_pts, const float *d_R, const float *d_grid,
             float *d_out, long B, int T, int C, int H, int W, float h, cudaStream_t stream) {
+    QC_NVTX(NT == 1 ? "quantem::kplanes_fwd" : "quantem::kplanes_tv_fwd");
     if (int st = check_shapes(who, B, T, C, H, W)) return st;
     if (B == 0 || T == 0 || C == 0) return 0;
     QC_RETURN_IF(H == 0 || W == 0, QC_ERR_INVALID_ARGUMENT, "%s: empty plane", who);
@@ -738,6 +739,7 @@ template <int NT>
 int backward(const char *who, const float *d_pts, const float *d_R, const float *d_grid,
              const float *d_gout, float *d_ggrid, float *d_gR, float *d_gpts, long B, int T,
              int C, int H, int W, int t_begin, int t_end, float h, cudaStream_t stream) {
+    QC_NVTX(NT == 1 ? "quantem::kplanes_bwd" : "quantem::kplanes_tv_bwd");
     if (int st = check_shapes(who, B, T, C, H, W)) return st;
     QC_RETURN_IF(t_begin < 0 || t_end > T || t_begin > t_end, QC_ERR_INVALID_ARGUMENT,
                  "%s: rotations [%d, %d) outside [0, %d)", who, t_begin, t_end, T);

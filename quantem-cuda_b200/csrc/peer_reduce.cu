@@ -127,6 +127,7 @@ size_t peer_allreduce_comm_bytes(void) { return sizeof(qc::pr::Comm); }
 
 int peer_allreduce_sum_f32_cuda(const qc_peer_group *g, unsigned long long seq, long long n,
                                 cudaStream_t stream) {
+    QC_NVTX("quantem::peer_allreduce");
     QC_RETURN_IF(g == nullptr, QC_ERR_INVALID_ARGUMENT, "peer_allreduce: null group");
     QC_RETURN_IF(g->world < 1 || g->world > QC_MAX_PEER_RANKS || g->rank < 0 ||
                      g->rank >= g->world,

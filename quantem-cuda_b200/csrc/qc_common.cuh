@@ -6,6 +6,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include "quantem_cuda_b200.h"
@@ -35,6 +36,16 @@ int check_cuda(cudaError_t err, const char *what);
 
 // Number of SMs of the current device (cached per device).
 int device_sm_count(int *sms);
+
+// NVTX range over a C-ABI entry point, so that a profiler timeline shows each
+// call by name next to its kernels (NVTX costs nothing without a tool).
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
+#define QC_NVTX(name) ::qc::NvtxRange qc_nvtx_range_(name)
 
 // ── device-side PTX wrappers ──────────────────────────────────────────────
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {

@@ -1253,6 +1253,7 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
         float acc_scale, void *ws, size_t ws_bytes, cudaStream_t stream,
         const qc_tv_peers *peers = nullptr, unsigned long long seq = 0,
         unsigned long long halo_seq = 0, int *n_partials_out = nullptr) {
+    QC_NVTX(variant == QC_TV_SQ ? "quantem::tv_sq" : variant == QC_TV_ISO ? "quantem::tv_iso" : "quantem::tv_l1");
     // n_partials_out != nullptr: launch the sweep only (its CTA partials stay
     // in ws, *n_partials_out of them) for a later tv_loss_3d_peer_finalize_cuda.
     const bool sweep_only = n_partials_out != nullptr;
@@ -1613,6 +1614,7 @@ int check_peers(const qc_tv_peers *p, unsigned long long seq) {
 
 int launch_halo_exchange(const qc_tv_peers *peers, unsigned long long seq, float *d_slab, int B,
                          int Dp, int H, int W, cudaStream_t stream) {
+    QC_NVTX("quantem::tv_halo_exchange");
     if (int st = check_peers(peers, seq)) return st;
     const bool has_prev = peers->rank > 0, has_next = peers->rank < peers->world - 1;
     QC_RETURN_IF(B < 0 || H < 0 || W < 0, QC_ERR_INVALID_ARGUMENT,
@@ -1714,6 +1716,7 @@ extern "C" int tv_loss_3d_peer_finalize_cuda(const qc_tv_peers *peers, unsigned 
                                              const qc_tv_term *terms, int n_terms,
                                              cudaStream_t stream) {
     using namespace qc::tv;
+    QC_NVTX("quantem::tv_peer_finalize");
     if (int st = check_peers(peers, seq)) return st;
     QC_RETURN_IF(terms == nullptr || n_terms < 1 || n_terms > QC_TV_MAX_PEER_SUMS,
                  QC_ERR_INVALID_ARGUMENT, "tv_loss_3d_peer_finalize_cuda: %d terms", n_terms);
