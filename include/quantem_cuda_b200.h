@@ -54,10 +54,12 @@ const char *quantem_cuda_status_string(int status);
  * Replaces the reference's `_core.__cudart_version__` (csrc/bindings.cpp:24). */
 int quantem_cuda_cudart_version(void);
 
-/* Reads (and, if `clear` != 0, resets) the device-side fault word of `device`.
- * Kernels that wait on a TMA barrier give up after a bounded time and set a bit
- * here instead of hanging; 0 means no kernel has given up. Synchronises the
- * device. */
+/* Reads (and, if `clear` != 0, resets) the device-side fault word of `device`:
+ * the OR of every kernel family's bits. Kernels that wait (on a TMA barrier, on
+ * another rank) give up after a bounded time and set a bit here instead of
+ * hanging; the library built with QC_DEBUG_BOUNDS (libquantem_cuda_b200_debug.so)
+ * also sets QC_FAULT_BOUNDS when a computed index falls outside its buffer and
+ * skips that access. 0 means nothing happened. Synchronises the device. */
 int quantem_cuda_device_fault_word(int device, unsigned int *word, int clear);
 
 /* ── 3-D total variation ────────────────────────────────────────────────── */
@@ -175,6 +177,7 @@ int tv_loss_3d_slab_cuda(int variant, int flags, const float *d_vol, const float
 #define QC_IPC_HANDLE_BYTES 64
 #define QC_FAULT_TMA_WAIT 0x1u  /* a kernel gave up waiting for its own TMA copies */
 #define QC_FAULT_PEER_WAIT 0x2u /* a kernel gave up waiting for another rank */
+#define QC_FAULT_BOUNDS 0x4u    /* debug builds (QC_DEBUG_BOUNDS): an index out of range was skipped */
 
 typedef struct qc_tv_peers {
     int rank;                          /* this rank, 0 <= rank < world */

@@ -47,6 +47,12 @@ CU_SOURCES = ["status.cu", "tv_sweep.cu", "kplanes_tilted.cu", "peer_mem.cu", "p
 HEADERS = [INCLUDE / "quantem_cuda_b200.h", CSRC / "qc_common.cuh"]
 
 LIB = PKG / "libquantem_cuda_b200.so"
+# The same library with every computed global index checked against its buffer
+# (QC_DEBUG_BOUNDS): out-of-range accesses are skipped and reported in the
+# device fault word. A sanitizer substitute for debugging, never loaded by the
+# torch ops.
+DEBUG_LIB = PKG / "libquantem_cuda_b200_debug.so"
+OBJ_DEBUG = HERE / "_build_debug"
 CORE = PKG / ("_core" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 
@@ -66,12 +72,26 @@ def _run(cmd: list[str], log: Path | None = None) -> None:
         raise RuntimeError(f"build step failed: {' '.join(cmd[:3])} ... (exit {res.returncode})")
 
 
-def _compile_cu(name: str) -> Path:
+def _compile_cu(name: str, debug: bool = False) -> Path:
     src = CSRC / name
-    obj = OBJ / (Path(name).stem + ".o")
+    out_dir = OBJ_DEBUG if debug else OBJ
+    obj = out_dir / (Path(name).stem + ".o")
     if _stale(obj, [src, *HEADERS]):
-        _run([NVCC, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)], OBJ / (Path(name).stem + ".ptxas.txt"))
+        flags = [*NVCC_FLAGS, "-DQC_DEBUG_BOUNDS"] if debug else NVCC_FLAGS
+        _run([NVCC, *flags, "-c", str(src), "-o", str(obj)], out_dir / (Path(name).stem + ".ptxas.txt"))
     return obj
+
+
+def build_debug(verbose: bool = False) -> Path:
+    """Builds the bounds-checked library (libquantem_cuda_b200_debug.so)."""
+    OBJ_DEBUG.mkdir(exist_ok=True)
+    with ThreadPoolExecutor(max_workers=len(CU_SOURCES)) as ex:
+        objs = list(ex.map(lambda n: _compile_cu(n, debug=True), CU_SOURCES))
+    if _stale(DEBUG_LIB, objs):
+        _run([NVCC, *ARCH, "-shared", "-o", str(DEBUG_LIB), *map(str, objs)])
+    if verbose:
+        print(f"built {DEBUG_LIB.name} in {PKG}")
+    return DEBUG_LIB
 
 
 def build(verbose: bool = False) -> tuple[Path, Path]:
@@ -112,3 +132,5 @@ def build(verbose: bool = False) -> tuple[Path, Path]:
 
 if __name__ == "__main__":
     build(verbose=True)
+    if "--debug-bounds" in sys.argv:
+        build_debug(verbose=True)

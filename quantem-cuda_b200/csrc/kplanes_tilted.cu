@@ -35,6 +35,9 @@
 namespace qc {
 namespace kp {
 
+// QC_FAULT_BOUNDS from the debug build's checks (see check_tap).
+__device__ unsigned int g_kp_fault_word = 0;
+
 struct Tap {
     int cell[4];     // y*W + x of the (nw, ne, sw, se) corners, +1 sides clamped
     float w[4];      // bilinear weights; 0 exactly where a +1 side was clamped
@@ -65,6 +68,20 @@ __device__ __forceinline__ Tap make_tap(float gx, float gy, int H, int W) {
     t.cell[2] = y1 * W + x0;
     t.cell[3] = y1 * W + x1;
     return t;
+}
+
+// Debug build: every corner index must lie in the plane; one that does not is
+// recorded and redirected to cell 0 so that no access leaves the buffers.
+__device__ __forceinline__ void check_tap(Tap &t, int H, int W) {
+#ifdef QC_DEBUG_BOUNDS
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        if (!QC_IN_BOUNDS(t.cell[k], (long long)H * W, g_kp_fault_word)) t.cell[k] = 0;
+#else
+    (void)t;
+    (void)H;
+    (void)W;
+#endif
 }
 
 // r = R_t·p as a0*x0 + a1*x1 + a2*x2 evaluated the way nvcc contracts that
@@ -190,7 +207,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kFwdMinBlocks : 4) kpt_fwd
             for (int p = 0; p < 3; ++p) {
                 float gx, gy;
                 plane_coords(ax, ay, az, p, gx, gy);
-                const Tap tp = make_tap(gx, gy, H, W);
+                Tap tp = make_tap(gx, gy, H, W);
+                check_tap(tp, H, W);
                 const float *pc = g0 + p * planeHWC;
                 const float4 v0 = ldg4(pc + tp.cell[0] * C), v1 = ldg4(pc + tp.cell[1] * C);
                 const float4 v2 = ldg4(pc + tp.cell[2] * C), v3 = ldg4(pc + tp.cell[3] * C);
@@ -296,6 +314,7 @@ __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
             float gx, gy;
             plane_coords(ax, ay, az, p, gx, gy);
             tap[p] = make_tap(gx, gy, H, W);
+            check_tap(tap[p], H, W);
             sample_with_slopes<C>(g0 + p * planeHWC, tap[p], s[p], dx[p], dy[p]);
         }
 
@@ -405,6 +424,7 @@ __global__ void __launch_bounds__(kThreads) kpt_fwd_generic_kernel(
                     float gx, gy;
                     plane_coords(ax, ay, az, p, gx, gy);
                     tp[p] = make_tap(gx, gy, H, W);
+                    check_tap(tp[p], H, W);
                 }
                 for (int c = lane; c < C; c += 32) {
                     float s[3];
@@ -459,6 +479,7 @@ __global__ void __launch_bounds__(kThreads) kpt_bwd_generic_kernel(
                 float gx, gy;
                 plane_coords(ax, ay, az, p, gx, gy);
                 tp[p] = make_tap(gx, gy, H, W);
+                    check_tap(tp[p], H, W);
             }
             float dgx[3] = {0.f, 0.f, 0.f}, dgy[3] = {0.f, 0.f, 0.f};
             for (int c = lane; c < C; c += 32) {
@@ -770,6 +791,19 @@ int backward(const char *who, const float *d_pts, const float *d_R, const float 
 }
 
 }  // namespace kp
+
+int kp_fault_word(unsigned int *word, int clear) {
+    unsigned int w = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&w, kp::g_kp_fault_word, sizeof(w));
+    if (e == cudaSuccess && clear) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(kp::g_kp_fault_word, &zero, sizeof(zero));
+    }
+    QC_CUDA_TRY(e, "cudaMemcpyFromSymbol(K-Planes fault word)");
+    *word = w;
+    return 0;
+}
+
 }  // namespace qc
 
 extern "C" {

@@ -85,6 +85,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(qc_peer_group g,
         const long long stride = (long long)gridDim.x * blockDim.x;
         for (long long i = b4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < e4;
              i += stride) {
+            if (!QC_IN_BOUNDS(4 * i + 3, n, g_pr_fault_word)) continue;
             float4 s = ld_cg4(g.buf[0] + 4 * i);
             for (int q = 1; q < g.world; ++q) {
                 const float4 v = ld_cg4(g.buf[q] + 4 * i);
@@ -119,6 +120,19 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(qc_peer_group g,
 }
 
 }  // namespace pr
+
+int pr_fault_word(unsigned int *word, int clear) {
+    unsigned int w = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&w, pr::g_pr_fault_word, sizeof(w));
+    if (e == cudaSuccess && clear) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(pr::g_pr_fault_word, &zero, sizeof(zero));
+    }
+    QC_CUDA_TRY(e, "cudaMemcpyFromSymbol(all-reduce fault word)");
+    *word = w;
+    return 0;
+}
+
 }  // namespace qc
 
 extern "C" {

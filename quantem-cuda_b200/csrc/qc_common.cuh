@@ -136,4 +136,24 @@ __device__ __forceinline__ float4 ldg4(const float *p) {
     return __ldg(reinterpret_cast<const float4 *>(p));
 }
 
+// Bounds checks of the debug build (-DQC_DEBUG_BOUNDS): true when
+// 0 <= i < n; otherwise sets QC_FAULT_BOUNDS in `word` and returns false, and
+// the caller skips (or redirects) the access. The release build compiles them
+// out.
+__device__ __forceinline__ bool in_bounds_checked(long long i, long long n, unsigned int *word) {
+    if (i >= 0 && i < n) return true;
+    atomicOr(word, QC_FAULT_BOUNDS);
+    return false;
+}
+#ifdef QC_DEBUG_BOUNDS
+#define QC_IN_BOUNDS(i, n, word) (::qc::in_bounds_checked((long long)(i), (long long)(n), &(word)))
+#else
+#define QC_IN_BOUNDS(i, n, word) true
+#endif
+
+// Fault words of the kernel families compiled in other translation units
+// (each reads the current device's word, clearing it if `clear`).
+int kp_fault_word(unsigned int *word, int clear);
+int pr_fault_word(unsigned int *word, int clear);
+
 }  // namespace qc

@@ -332,7 +332,10 @@ __device__ __forceinline__ void halo_push_prologue(const HaloXchg &xc, int B, in
             const long long dst = side == 0 ? (long long)b * xc.prev_dp + xc.prev_dp - 1
                                             : (long long)b * xc.next_dp;
             float *d = side == 0 ? xc.prev_slab : xc.next_slab;
-            *reinterpret_cast<float4 *>(d + dst * plane + e * 4) = ldg4(xc.vol + src * plane + e * 4);
+            const int ddp = side == 0 ? xc.prev_dp : xc.next_dp;
+            if (QC_IN_BOUNDS(src * plane + e * 4 + 3, (long long)B * Dp * plane, g_tv_fault_word) &&
+                QC_IN_BOUNDS(dst * plane + e * 4 + 3, (long long)B * ddp * plane, g_tv_fault_word))
+                *reinterpret_cast<float4 *>(d + dst * plane + e * 4) = ldg4(xc.vol + src * plane + e * 4);
         }
     }
     __syncthreads();
@@ -816,7 +819,12 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                                                              sub2(wl01, Fw.x)));
                                 const f2 g23 = mul2(gm, add2(add2(sub2(Fd_prev[i][1], Fd.y), sub2(up23, Fh.y)),
                                                              sub2(wl23, Fw.y)));
-                                if (lane_in && (FULL || h < pl.H)) stcs_pairs(gp + (size_t)i * pl.W, g01, g23);
+                                float *dst = gp + (size_t)i * pl.W;
+                                if (lane_in && (FULL || h < pl.H) &&
+                                    QC_IN_BOUNDS((dst - grad) + 3,
+                                                 (long long)pl.B * pl.Dp * pl.H * (long long)pl.W,
+                                                 g_tv_fault_word))
+                                    stcs_pairs(dst, g01, g23);
                                 Fd_prev[i][0] = Fd.x;
                                 Fd_prev[i][1] = Fd.y;
                                 up01 = Fh.x;
@@ -897,8 +905,11 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
         const int h = U.h0 + ty, w = U.w0 + tx;
         const bool in = h < pl.H && w < pl.W;
         const float *vb = vol + (size_t)U.n * pl.Dp * plane;
+        const long long total = (long long)pl.B * pl.Dp * (long long)plane;
         auto at = [&](int p, int hh, int ww) -> float {
-            return __ldg(vb + (size_t)p * plane + (size_t)hh * pl.W + ww);
+            const long long i = (long long)U.n * pl.Dp * (long long)plane + (long long)p * plane +
+                                (long long)hh * pl.W + ww;
+            return QC_IN_BOUNDS(i, total, g_tv_fault_word) ? __ldg(vol + i) : 0.f;
         };
         const bool vh = h + 1 < pl.H, vw = w + 1 < pl.W;
         float Fd_prev = 0.f;
@@ -930,7 +941,9 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
                     }
                     const float gv =
                         gn.gmul * ((Fd_prev - Fd) + (Fh_up - Fh) + (Fw_left - Fw));
-                    grad[(size_t)U.n * pl.Dp * plane + (size_t)p * plane + (size_t)h * pl.W + w] = gv;
+                    const long long gi = (long long)U.n * pl.Dp * (long long)plane +
+                                         (long long)p * plane + (long long)h * pl.W + w;
+                    if (QC_IN_BOUNDS(gi, total, g_tv_fault_word)) grad[gi] = gv;
                 }
             }
             Fd_prev = Fd;
@@ -1451,15 +1464,18 @@ int quantem_cuda_device_fault_word(int device, unsigned int *word, int clear) {
     int prev = 0;
     QC_CUDA_TRY(cudaGetDevice(&prev), "cudaGetDevice");
     QC_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
-    unsigned int w = 0;
+    unsigned int w = 0, wk = 0, wp = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&w, qc::tv::g_tv_fault_word, sizeof(w));
     if (e == cudaSuccess && clear) {
         const unsigned int zero = 0;
         e = cudaMemcpyToSymbol(qc::tv::g_tv_fault_word, &zero, sizeof(zero));
     }
+    int st = e == cudaSuccess ? qc::kp_fault_word(&wk, clear) : 0;
+    if (e == cudaSuccess && st == 0) st = qc::pr_fault_word(&wp, clear);
     cudaSetDevice(prev);
     QC_CUDA_TRY(e, "cudaMemcpyFromSymbol(fault word)");
-    if (word) *word = w;
+    if (st) return st;
+    if (word) *word = w | wk | wp;
     return 0;
 }
 
@@ -1572,6 +1588,11 @@ __global__ void __launch_bounds__(kHaloThreads) tv_halo_exchange_kernel(
             const long long dst_plane = side == 0 ? (long long)b * peers.prev_dp + peers.prev_dp - 1
                                                   : (long long)b * peers.next_dp;
             float *dst = side == 0 ? peers.prev_slab : peers.next_slab;
+            const int ddp = side == 0 ? peers.prev_dp : peers.next_dp;
+            const long long last = vec4 ? e * 4 + 3 : e;
+            if (!QC_IN_BOUNDS(src_plane * plane + last, (long long)B * Dp * plane, g_tv_fault_word) ||
+                !QC_IN_BOUNDS(dst_plane * plane + last, (long long)B * ddp * plane, g_tv_fault_word))
+                continue;
             if (vec4) {
                 const float4 v = ldg4(slab + src_plane * plane + e * 4);
                 *reinterpret_cast<float4 *>(dst + dst_plane * plane + e * 4) = v;

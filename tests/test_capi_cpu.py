@@ -41,8 +41,14 @@ def test_header_declares_the_hot_path():
         assert required in names
 
 
-def test_library_exports_every_declared_symbol():
-    lib = ctypes.CDLL(str(LIB))
+DEBUG_LIB = LIB.with_name("libquantem_cuda_b200_debug.so")
+
+
+@pytest.mark.parametrize("path", [LIB, DEBUG_LIB], ids=["release", "bounds-checked"])
+def test_library_exports_every_declared_symbol(path):
+    if not path.exists():
+        pytest.skip(f"{path.name} not built")
+    lib = ctypes.CDLL(str(path))
     missing = [n for n in declared_functions() if not hasattr(lib, n)]
     assert not missing, f"declared but not exported: {missing}"
 
