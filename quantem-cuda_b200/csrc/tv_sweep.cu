@@ -332,10 +332,13 @@ __device__ __forceinline__ void halo_push_prologue(const HaloXchg &xc, int B, in
             const long long dst = side == 0 ? (long long)b * xc.prev_dp + xc.prev_dp - 1
                                             : (long long)b * xc.next_dp;
             float *d = side == 0 ? xc.prev_slab : xc.next_slab;
+#ifdef QC_DEBUG_BOUNDS
             const int ddp = side == 0 ? xc.prev_dp : xc.next_dp;
-            if (QC_IN_BOUNDS(src * plane + e * 4 + 3, (long long)B * Dp * plane, g_tv_fault_word) &&
-                QC_IN_BOUNDS(dst * plane + e * 4 + 3, (long long)B * ddp * plane, g_tv_fault_word))
-                *reinterpret_cast<float4 *>(d + dst * plane + e * 4) = ldg4(xc.vol + src * plane + e * 4);
+            if (!QC_IN_BOUNDS(src * plane + e * 4 + 3, (long long)B * Dp * plane, g_tv_fault_word) ||
+                !QC_IN_BOUNDS(dst * plane + e * 4 + 3, (long long)B * ddp * plane, g_tv_fault_word))
+                continue;
+#endif
+            *reinterpret_cast<float4 *>(d + dst * plane + e * 4) = ldg4(xc.vol + src * plane + e * 4);
         }
     }
     __syncthreads();
@@ -819,12 +822,16 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                                                              sub2(wl01, Fw.x)));
                                 const f2 g23 = mul2(gm, add2(add2(sub2(Fd_prev[i][1], Fd.y), sub2(up23, Fh.y)),
                                                              sub2(wl23, Fw.y)));
+#ifdef QC_DEBUG_BOUNDS
                                 float *dst = gp + (size_t)i * pl.W;
                                 if (lane_in && (FULL || h < pl.H) &&
                                     QC_IN_BOUNDS((dst - grad) + 3,
                                                  (long long)pl.B * pl.Dp * pl.H * (long long)pl.W,
                                                  g_tv_fault_word))
                                     stcs_pairs(dst, g01, g23);
+#else
+                                if (lane_in && (FULL || h < pl.H)) stcs_pairs(gp + (size_t)i * pl.W, g01, g23);
+#endif
                                 Fd_prev[i][0] = Fd.x;
                                 Fd_prev[i][1] = Fd.y;
                                 up01 = Fh.x;
