@@ -14,8 +14,9 @@ import ctypes
 from pathlib import Path
 
 import pytest
+import multiprocessing as mp
+
 import torch
-import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
@@ -84,7 +85,10 @@ def _run_all(name):
 
 def _child(name, queue):
     try:
-        queue.put(("ok",) + _run_all(name))
+        res, fault = _run_all(name)
+        # numpy arrays travel by value (tensors would be shared through file
+        # descriptors that close when this process exits)
+        queue.put(("ok", {k: tuple(t.numpy() for t in v) for k, v in res.items()}, fault))
     except BaseException as e:  # report, do not hang the parent
         queue.put(("error", repr(e), 0))
 
@@ -103,7 +107,7 @@ def test_checked_build_is_clean_and_matches_release():
     release, rel_fault = _run_all("libquantem_cuda_b200.so")
     assert rel_fault == 0
     for key, ref in release.items():
-        got = checked[key]
+        got = tuple(torch.from_numpy(a) for a in checked[key])
         if key[0] == "tv":
             assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1]), key
         else:
