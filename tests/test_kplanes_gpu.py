@@ -473,3 +473,20 @@ def test_tv_matches_reference_cuda_kernels(cfg):
     for mine, theirs, what in ((m_gg, gg.permute(0, 3, 1, 2), "plane"), (m_gr, gr, "rotations"), (m_gp, gp, "pts")):
         err = (mine - theirs).abs().max().item()
         assert err <= 1e-4 * theirs.abs().max().item(), (what, err)
+
+
+def test_ops_replay_from_a_cuda_graph():
+    pts, rot, plane, up = make_inputs(1000, 2, 32, 24, 20, seed=61)
+    p, r, g, u = pts.cuda(), rot.cuda(), plane.cuda(), up.cuda()
+    eager_out = torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, g)
+    eager_grads = torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, g, u)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, g)
+        grads = torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, g, u)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager_out)
+    for a, b in zip(grads, eager_grads):
+        torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5 * b.abs().max().item())

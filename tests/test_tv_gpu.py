@@ -356,3 +356,20 @@ def test_first_cuda_work_on_a_fresh_host_thread():
     assert "err" not in box, box.get("err")
     np.testing.assert_allclose(box["res"][0], oracle.tv_iso_loss(x, 1e-8), rtol=FWD_RTOL)
     assert_grad_close(box["res"][1], oracle.tv_iso_grad(x, 1.0 / n_corners(x.shape), 1e-8))
+
+
+def test_ops_replay_from_a_cuda_graph():
+    """The single-sweep ops and the autograd pair are capturable: a CUDA graph
+    replays them with the eager results (workspaces come from torch's
+    allocator; per-device setup happens on the first, eager call)."""
+    v = rand_vol((2, 24, 40, 132), 16).cuda()
+    g = torch.tensor([0.3], device="cuda")
+    eager = (tv_loss_iso_3d_fwd_grad(v, g, eps=1e-8), tv_loss_l1_3d(v))
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        (loss, grad), sums = tv_loss_iso_3d_fwd_grad(v, g, eps=1e-8), tv_loss_l1_3d(v)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(loss, eager[0][0]) and torch.equal(grad, eager[0][1]) and torch.equal(sums, eager[1])
