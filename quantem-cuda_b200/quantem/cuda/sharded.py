@@ -23,7 +23,14 @@ natural sharding of the work:
 
 * K-Planes over points. Each rank evaluates its own points against the
   replicated planes and rotations; point gradients stay local, and the plane
-  and rotation gradients are summed with all_reduce.
+  and rotation gradients are summed over the ranks: by one kernel over peer
+  memory (:class:`PeerAllReduce`, deterministic rank-ordered sums) or with a
+  torch.distributed all_reduce.
+
+Objects holding peer memory (:class:`PeerSlab`, :class:`PeerAllReduce`) are
+collective: every rank creates them together, calls their methods in the
+same order on one stream, and calls ``close()`` together before the process
+group goes away (a rank must not free memory another rank still maps).
 
 The per-rank compute defaults to the CUDA kernels. ``slab_kernel`` exists so
 that the host logic (halo exchange, ownership flags, reductions) can be tested
@@ -463,6 +470,8 @@ class PeerSlab:
         from quantem.cuda._common import _workspace
 
         b, dp, h, w = self.shape
+        if not 1 <= len(terms) <= 8 or sum(_N_ACC[t[0]] for t in terms) > 8:
+            raise ValueError("fwd_grad_many takes 1..8 terms with at most 8 loss sums in total")
         stream = torch.cuda.current_stream(self.device).cuda_stream
         if len(self._ws_many) < len(terms):
             self._ws_many += [_workspace(self.device) for _ in range(len(terms) - len(self._ws_many))]
@@ -479,6 +488,8 @@ class PeerSlab:
                 grad = None if grads is None else grads[k]
                 if grad is None:
                     grad = torch.empty(self.shape, dtype=torch.float32, device=self.device)
+                elif tuple(grad.shape) != self.shape or not grad.is_contiguous() or grad.dtype != torch.float32:
+                    raise ValueError(f"grads[{k}] must be a contiguous fp32 tensor of shape {self.shape}")
                 g = grad_out.to(device=self.device, dtype=torch.float32).contiguous()
                 if g.numel() != _N_ACC[variant]:
                     raise ValueError(f"grad_out needs {_N_ACC[variant]} element(s), got {g.numel()}")
