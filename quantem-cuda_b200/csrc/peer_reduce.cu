@@ -31,8 +31,10 @@ struct Comm {
     unsigned int pad[31];
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// Flags are raised as one system-scope fence followed by relaxed stores (one
+// fence for all ranks' flags instead of one per flag).
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
     unsigned long long v;
@@ -68,8 +70,9 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(qc_peer_group g,
     const uint64_t limit = g.timeout_ns ? g.timeout_ns : kDefaultLimitNs;
     __shared__ int go;
     if (threadIdx.x == 0) {
+        __threadfence_system();
         for (int q = 0; q < g.world; ++q)
-            st_release_sys(&static_cast<Comm *>(g.comm[q])->arrive[g.rank], seq);
+            st_relaxed_sys(&static_cast<Comm *>(g.comm[q])->arrive[g.rank], seq);
         bool ok = true;
         for (int q = 0; q < g.world; ++q) ok = wait_geq(&self->arrive[q], seq, limit) && ok;
         if (!ok) atomicOr(&g_pr_fault_word, QC_FAULT_PEER_WAIT);
@@ -111,7 +114,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(qc_peer_group g,
             self->count = 0;  // the next call on this stream starts after this grid
             __threadfence_system();
             for (int q = 0; q < g.world; ++q)
-                st_release_sys(&static_cast<Comm *>(g.comm[q])->done[g.rank], seq);
+                st_relaxed_sys(&static_cast<Comm *>(g.comm[q])->done[g.rank], seq);
             bool ok = true;
             for (int q = 0; q < g.world; ++q) ok = wait_geq(&self->done[q], seq, limit) && ok;
             if (!ok) atomicOr(&g_pr_fault_word, QC_FAULT_PEER_WAIT);

@@ -242,8 +242,8 @@ __device__ __forceinline__ Unit decode_unit(const Plan &pl, long long u, int til
 // hold the sequence number of the last call that set them; a waiter compares
 // with >= so a flag that has moved on to a later call still releases it.
 // Data goes into a peer's block with plain stores, then (one thread per CTA,
-// after a CTA barrier and a system-scope fence) the flag is stored with
-// release semantics; the waiter loads it with acquire semantics.
+// after a CTA barrier) one system-scope fence and the flags as relaxed stores;
+// the waiter loads a flag with acquire semantics.
 
 struct PeerComm {
     unsigned long long ready[2];   // [s]: neighbour on side s (0 = rank-1, 1 = rank+1) lets
@@ -255,8 +255,11 @@ struct PeerComm {
     double partials[2][QC_MAX_PEER_RANKS][QC_TV_MAX_PEER_SUMS];  // [call & 1][q][sum]
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// Flag stores. A group of flags that publishes earlier stores is written as
+// one system-scope fence followed by relaxed stores, so that raising k flags
+// costs one fence (st.release would fence again before every flag).
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
@@ -309,8 +312,10 @@ struct HaloXchg {
 __device__ __forceinline__ void halo_push_prologue(const HaloXchg &xc, int B, int Dp,
                                                    long long plane, int *go) {
     if (threadIdx.x == 0) {
-        if (xc.prev) st_release_sys(&xc.prev->ready[1], xc.seq);
-        if (xc.next) st_release_sys(&xc.next->ready[0], xc.seq);
+        // nothing of this grid precedes these flags: the work they announce
+        // (earlier kernels on the stream) completed before the grid started
+        if (xc.prev) st_relaxed_sys(&xc.prev->ready[1], xc.seq);
+        if (xc.next) st_relaxed_sys(&xc.next->ready[0], xc.seq);
         bool ok = true;
         if (xc.prev) ok = wait_flag_geq(&xc.self->ready[0], xc.seq, xc.limit_ns) && ok;
         if (xc.next) ok = wait_flag_geq(&xc.self->ready[1], xc.seq, xc.limit_ns) && ok;
@@ -347,8 +352,8 @@ __device__ __forceinline__ void halo_push_prologue(const HaloXchg &xc, int B, in
         if (atomicAdd(&xc.self->arrive, 1u) == gridDim.x - 1) {
             xc.self->arrive = 0;  // the next exchange on this stream starts after this grid
             __threadfence_system();
-            if (xc.prev) st_release_sys(&xc.prev->filled[1], xc.seq);
-            if (xc.next) st_release_sys(&xc.next->filled[0], xc.seq);
+            if (xc.prev) st_relaxed_sys(&xc.prev->filled[1], xc.seq);
+            if (xc.next) st_relaxed_sys(&xc.next->filled[0], xc.seq);
         }
     }
 }
@@ -1069,7 +1074,7 @@ __global__ void __launch_bounds__(kFinThreads) tv_finalize_peer_kernel(const Fin
     if (threadIdx.x == 0) {
         __threadfence_system();
         for (int q = 0; q < peers.world; ++q)
-            st_release_sys(&static_cast<PeerComm *>(peers.comm[q])->red_flag[peers.rank], seq);
+            st_relaxed_sys(&static_cast<PeerComm *>(peers.comm[q])->red_flag[peers.rank], seq);
     }
     PeerComm *self = static_cast<PeerComm *>(peers.comm[peers.rank]);
     if (threadIdx.x < peers.world) {
@@ -1571,8 +1576,8 @@ __global__ void __launch_bounds__(kHaloThreads) tv_halo_exchange_kernel(
     const uint64_t limit = peer_limit(peers);
     __shared__ int go;
     if (threadIdx.x == 0) {
-        if (has_prev) st_release_sys(&prevc->ready[1], seq);
-        if (has_next) st_release_sys(&nextc->ready[0], seq);
+        if (has_prev) st_relaxed_sys(&prevc->ready[1], seq);
+        if (has_next) st_relaxed_sys(&nextc->ready[0], seq);
         bool ok = true;
         if (has_prev) ok = wait_flag_geq(&self->ready[0], seq, limit) && ok;
         if (has_next) ok = wait_flag_geq(&self->ready[1], seq, limit) && ok;
@@ -1615,8 +1620,8 @@ __global__ void __launch_bounds__(kHaloThreads) tv_halo_exchange_kernel(
         if (before == gridDim.x - 1) {
             self->arrive = 0;  // the next exchange on this stream starts after this grid
             __threadfence_system();
-            if (has_prev) st_release_sys(&prevc->filled[1], seq);
-            if (has_next) st_release_sys(&nextc->filled[0], seq);
+            if (has_prev) st_relaxed_sys(&prevc->filled[1], seq);
+            if (has_next) st_relaxed_sys(&nextc->filled[0], seq);
             bool ok = true;
             if (has_prev) ok = wait_flag_geq(&self->filled[0], seq, limit) && ok;
             if (has_next) ok = wait_flag_geq(&self->filled[1], seq, limit) && ok;
