@@ -67,14 +67,45 @@ def slab_bounds(global_d: int, rank: int, world: int) -> tuple[int, int]:
     return lo, lo + base + (1 if rank < extra else 0)
 
 
-def exchange_halos(slab: Tensor, group=None) -> None:
+def _check_neighbour_planes(slab: Tensor, rank: int, world: int, group) -> None:
+    """Compares this rank's plane shape (B, H, W) with its neighbours' before
+    any plane moves; a mismatch raises ValueError on both sides of it."""
+    mine = torch.tensor([slab.shape[0], slab.shape[2], slab.shape[3]], dtype=torch.int64, device=slab.device)
+    theirs = {}
+    ops = []
+    for q in (rank - 1, rank + 1):
+        if 0 <= q < world:
+            theirs[q] = torch.empty_like(mine)
+            ops.append(dist.P2POp(dist.isend, mine, _peer(group, q), group))
+            ops.append(dist.P2POp(dist.irecv, theirs[q], _peer(group, q), group))
+    for req in dist.batch_isend_irecv(ops):
+        req.wait()
+    b_h_w = mine.tolist()
+    for q, t in theirs.items():
+        if t.tolist() != b_h_w:
+            raise ValueError(
+                f"halo exchange: rank {rank} has planes (B, H, W) = {tuple(b_h_w)} but neighbour "
+                f"rank {q} has {tuple(t.tolist())}")
+
+
+def exchange_halos(slab: Tensor, group=None, check_shapes: bool = True) -> None:
     """Fills the halo planes 0 and -1 of ``slab [B, D_local + 2, H, W]`` with
     the neighbouring ranks' boundary planes (rank r-1's last owned plane and
     rank r+1's first). Ranks at the ends of the global volume leave that halo
-    as it is (the kernel is told it is not a neighbour)."""
+    as it is (the kernel is told it is not a neighbour).
+
+    With ``check_shapes`` the neighbours first compare their (B, H, W) and
+    raise ValueError on a mismatch (one extra small message each way and a
+    host synchronisation); a loop whose shapes are fixed can check once and
+    pass False afterwards. A neighbour that never takes part makes the
+    exchange fail after the process group's timeout."""
     rank, world = _rank_world(group)
     if world == 1:
         return
+    if slab.dim() != 4 or slab.shape[1] < 3:
+        raise ValueError(f"slab must be [B, D_local + 2, H, W] with D_local >= 1, got {tuple(slab.shape)}")
+    if check_shapes:
+        _check_neighbour_planes(slab, rank, world, group)
     d_local = slab.shape[1] - 2
     send_lo = slab[:, 1].contiguous()
     send_hi = slab[:, d_local].contiguous()
@@ -133,6 +164,7 @@ def tv_loss_slab_fwd_grad(
     group=None,
     exchange: bool = True,
     slab_kernel: Callable | None = None,
+    check_shapes: bool = True,
 ) -> tuple[Tensor, Tensor]:
     """Loss and gradient of one TV variant over a D-sharded volume.
 
@@ -143,6 +175,7 @@ def tv_loss_slab_fwd_grad(
         grad_out: upstream gradient, shape (1,) (SQ, ISO) or (3,) (L1).
         global_d: D of the whole volume (the isotropic mean divides by the
                   global corner count).
+        check_shapes: passed to :func:`exchange_halos`.
 
     Returns:
         ``(loss, grad)``: the global loss (identical on every rank; the mean
@@ -151,7 +184,7 @@ def tv_loss_slab_fwd_grad(
     """
     rank, world = _rank_world(group)
     if exchange:
-        exchange_halos(slab, group)
+        exchange_halos(slab, group, check_shapes)
     b, dp, h, w = slab.shape
     d_local = dp - 2
     scale = 1.0
@@ -316,6 +349,13 @@ def _kplanes_fwd_bwd_bucketed(pts, rotations, plane, grad_out, group, world, buc
 # ── D-slabs over peer memory ────────────────────────────────────────────────
 
 
+def _same_on_every_rank(values: list, what: str) -> None:
+    """Raises ValueError (on every rank, which all hold the same gathered
+    list) unless every rank passed the same value."""
+    if any(v != values[0] for v in values):
+        raise ValueError(f"{what} differs between ranks: " + ", ".join(f"rank {q}: {v}" for q, v in enumerate(values)))
+
+
 class _PeerAllocation:
     """One ``quantem_cuda_peer_alloc`` allocation (zero-filled, IPC-exportable),
     viewable as a torch tensor through ``__cuda_array_interface__``; freed when
@@ -380,9 +420,13 @@ class PeerSlab:
         self._comm_mem = _PeerAllocation((int(_core.tv_peer_comm_bytes()),), "|u1", 1, self.device)
         self.slab = torch.as_tensor(self._slab_mem, device=self.device)
         with torch.cuda.device(self.device):
-            mine = (rank, dp, _core.ipc_handle(self._slab_mem.ptr), _core.ipc_handle(self._comm_mem.ptr))
+            mine = ((batch, global_d, height, width), dp, _core.ipc_handle(self._slab_mem.ptr),
+                    _core.ipc_handle(self._comm_mem.ptr))
         infos = [None] * world
         dist.all_gather_object(infos, mine, group=group)
+        # the neighbours' halo stores are sized by this rank's (B, H, W): every
+        # rank must describe the same volume before any memory is mapped
+        _same_on_every_rank([i[0] for i in infos], "PeerSlab (batch, global_d, height, width)")
         self._mapped: list[int] = []
         comm, prev_ptr, prev_dp, next_ptr, next_dp = [], 0, 0, 0, 0
         with torch.cuda.device(self.device):
@@ -542,13 +586,15 @@ class PeerAllReduce:
         self._comm_mem = _PeerAllocation((int(_core.peer_allreduce_comm_bytes()),), "|u1", 1, self.device)
         self.buffer = torch.as_tensor(self._buf_mem, device=self.device)
         with torch.cuda.device(self.device):
-            mine = (_core.ipc_handle(self._buf_mem.ptr), _core.ipc_handle(self._comm_mem.ptr))
+            mine = (self.numel, _core.ipc_handle(self._buf_mem.ptr), _core.ipc_handle(self._comm_mem.ptr))
         infos = [None] * world
         dist.all_gather_object(infos, mine, group=group)
+        # each rank reads and writes every buffer over its whole length
+        _same_on_every_rank([i[0] for i in infos], "PeerAllReduce numel")
         self._mapped: list[int] = []
         bufs, comms = [], []
         with torch.cuda.device(self.device):
-            for q, (buf_h, comm_h) in enumerate(infos):
+            for q, (_, buf_h, comm_h) in enumerate(infos):
                 if q == rank:
                     bufs.append(self._buf_mem.ptr)
                     comms.append(self._comm_mem.ptr)

@@ -171,3 +171,94 @@ def test_kplanes_point_sharding_reduces_plane_gradients():
         np.testing.assert_allclose(gp, o_gp[lo:hi].numpy(), rtol=1e-6, atol=1e-7)
         np.testing.assert_allclose(gr, o_gr.numpy(), rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(gg, o_gg.numpy(), rtol=1e-5, atol=1e-7)
+
+
+# ── failures on the host: a rank that stops, a neighbour with another shape ──
+
+
+def _dead_rank_worker(rank, world, port, queue):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    from quantem.cuda import sharded
+
+    if rank == world - 1:
+        # this rank stops before the step: it never sends its halo
+        queue.put((rank, "left"))
+        queue.close()
+        queue.join_thread()
+        os._exit(0)
+    slab = torch.rand((1, 6, 4, 8))
+    try:
+        sharded.tv_loss_slab_fwd_grad(SQ, slab, torch.tensor([1.0]), 4 * world, slab_kernel=oracle_slab_kernel)
+        queue.put((rank, "no error"))
+    except Exception as e:  # the collective gives up after the group's timeout
+        queue.put((rank, f"detected: {type(e).__name__}"))
+    queue.close()
+    queue.join_thread()
+    os._exit(0)
+
+
+def test_a_rank_that_stops_is_detected_by_its_neighbours():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dead_rank_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        out = dict(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert out[world - 1] == "left"
+    assert out[0].startswith("detected"), out[0]
+
+
+def _shape_mismatch_worker(rank, world, port, queue):
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    from quantem.cuda import sharded
+
+    # rank 1's planes are wider than rank 0's: the halo exchange must fail
+    slab = torch.rand((1, 6, 4, 8 if rank == 0 else 12))
+    try:
+        sharded.exchange_halos(slab)
+        queue.put((rank, "no error"))
+    except Exception as e:
+        queue.put((rank, f"detected: {type(e).__name__}"))
+    queue.close()
+    queue.join_thread()
+    os._exit(0)
+
+
+def test_a_neighbour_with_another_plane_shape_is_rejected():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shape_mismatch_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        out = dict(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert all(v == "detected: ValueError" for v in out.values()), out
+
+
+def test_peer_objects_reject_ranks_that_disagree():
+    from quantem.cuda.sharded import _same_on_every_rank
+
+    _same_on_every_rank([(2, 64, 8, 8)] * 4, "shape")
+    with pytest.raises(ValueError, match="rank 2"):
+        _same_on_every_rank([(2, 64, 8, 8), (2, 64, 8, 8), (2, 64, 8, 9)], "PeerSlab shape")
