@@ -64,6 +64,73 @@ __device__ __forceinline__ float ld_cg1(const float *p) {
     return v;
 }
 
+// Sums float4 i of chunk [b4, e4) over the ranks in rank order and stores it
+// into every rank's buffer. WORLD > 0: the rank count is a compile-time
+// constant, so all WORLD x U loads of a thread are issued before the first
+// add (U float4s per thread per iteration keep 8-16 NVLink reads in flight).
+template <int WORLD>
+__device__ __forceinline__ void sum_chunk(const qc_peer_group &g, long long b4, long long e4, long long n) {
+    constexpr int U = WORLD <= 4 ? 4 : 2;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    long long i = b4 + (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + (U - 1) * stride < e4; i += U * stride) {
+        // the iteration's largest index; the smaller ones follow
+        if (!QC_IN_BOUNDS(4 * (i + (U - 1) * stride) + 3, n, g_pr_fault_word)) break;
+        float4 v[U][WORLD];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int q = 0; q < WORLD; ++q) v[u][q] = ld_cg4(g.buf[q] + 4 * (i + u * stride));
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float4 s = v[u][0];
+#pragma unroll
+            for (int q = 1; q < WORLD; ++q) {
+                s.x += v[u][q].x;
+                s.y += v[u][q].y;
+                s.z += v[u][q].z;
+                s.w += v[u][q].w;
+            }
+            const long long j = i + u * stride;
+#pragma unroll
+            for (int q = 0; q < WORLD; ++q) *reinterpret_cast<float4 *>(g.buf[q] + 4 * j) = s;
+        }
+    }
+    for (; i < e4; i += stride) {
+        if (!QC_IN_BOUNDS(4 * i + 3, n, g_pr_fault_word)) continue;
+        float4 v[WORLD];
+#pragma unroll
+        for (int q = 0; q < WORLD; ++q) v[q] = ld_cg4(g.buf[q] + 4 * i);
+        float4 s = v[0];
+#pragma unroll
+        for (int q = 1; q < WORLD; ++q) {
+            s.x += v[q].x;
+            s.y += v[q].y;
+            s.z += v[q].z;
+            s.w += v[q].w;
+        }
+#pragma unroll
+        for (int q = 0; q < WORLD; ++q) *reinterpret_cast<float4 *>(g.buf[q] + 4 * i) = s;
+    }
+}
+
+// Any rank count (a runtime loop over the ranks).
+__device__ __forceinline__ void sum_chunk_any(const qc_peer_group &g, long long b4, long long e4, long long n) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = b4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < e4; i += stride) {
+        if (!QC_IN_BOUNDS(4 * i + 3, n, g_pr_fault_word)) continue;
+        float4 s = ld_cg4(g.buf[0] + 4 * i);
+        for (int q = 1; q < g.world; ++q) {
+            const float4 v = ld_cg4(g.buf[q] + 4 * i);
+            s.x += v.x;
+            s.y += v.y;
+            s.z += v.z;
+            s.w += v.w;
+        }
+        for (int q = 0; q < g.world; ++q) *reinterpret_cast<float4 *>(g.buf[q] + 4 * i) = s;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) allreduce_kernel(qc_peer_group g,
                                                              unsigned long long seq, long long n) {
     Comm *self = static_cast<Comm *>(g.comm[g.rank]);
@@ -85,19 +152,11 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(qc_peer_group g,
         const long long per = n4 / g.world;
         const long long b4 = per * g.rank;
         const long long e4 = g.rank == g.world - 1 ? n4 : b4 + per;
-        const long long stride = (long long)gridDim.x * blockDim.x;
-        for (long long i = b4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < e4;
-             i += stride) {
-            if (!QC_IN_BOUNDS(4 * i + 3, n, g_pr_fault_word)) continue;
-            float4 s = ld_cg4(g.buf[0] + 4 * i);
-            for (int q = 1; q < g.world; ++q) {
-                const float4 v = ld_cg4(g.buf[q] + 4 * i);
-                s.x += v.x;
-                s.y += v.y;
-                s.z += v.z;
-                s.w += v.w;
-            }
-            for (int q = 0; q < g.world; ++q) *reinterpret_cast<float4 *>(g.buf[q] + 4 * i) = s;
+        switch (g.world) {
+            case 2: sum_chunk<2>(g, b4, e4, n); break;
+            case 4: sum_chunk<4>(g, b4, e4, n); break;
+            case 8: sum_chunk<8>(g, b4, e4, n); break;
+            default: sum_chunk_any(g, b4, e4, n); break;
         }
         if (g.rank == g.world - 1 && blockIdx.x == 0) {
             for (long long i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) {

@@ -235,6 +235,8 @@ def _kp_worker(rank, world, port, queue):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_kplanes_point_sharding_matches_single_gpu():
+    import quantem.cuda.core.ml  # noqa: F401  (registers the K-Planes ops used below)
+
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
