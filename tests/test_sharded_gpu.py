@@ -267,6 +267,11 @@ def test_kplanes_point_sharding_matches_single_gpu():
 # ── the peer-memory all-reduce on its own ────────────────────────────────────
 
 
+# Sizes: fewer elements than 4 x ranks (tail only), one float4 per rank plus
+# a tail, and a large size that is not a multiple of 4 x ranks.
+ALLREDUCE_SIZES = (3, 37, 1_000_003)
+
+
 def _allreduce_worker(rank, world, port, queue):
     import datetime
 
@@ -279,16 +284,16 @@ def _allreduce_worker(rank, world, port, queue):
     try:
         from quantem.cuda import _core, sharded
 
-        n = 1_000_003  # not a multiple of 4 x world: exercises the tail
-        red = sharded.PeerAllReduce(n, timeout_s=20.0)
         outs = []
-        for call in range(3):
-            gen = torch.Generator().manual_seed(1000 * call + rank)
-            red.buffer.copy_(torch.randn(n, generator=gen).cuda())
-            outs.append(red.all_reduce().cpu().clone())
-        torch.cuda.synchronize()
+        for n in ALLREDUCE_SIZES:
+            red = sharded.PeerAllReduce(n, timeout_s=20.0)
+            for call in range(3):
+                gen = torch.Generator().manual_seed(1000 * call + rank)
+                red.buffer.copy_(torch.randn(n, generator=gen).cuda())
+                outs.append(red.all_reduce().cpu().clone())
+            torch.cuda.synchronize()
+            red.close()
         queue.put((rank, outs, _core.peer_allreduce_fault_word(rank)))
-        red.close()
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
@@ -308,12 +313,14 @@ def test_peer_allreduce_is_the_rank_ordered_sum(world):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    n = 1_000_003
-    for call in range(3):
-        parts = [torch.randn(n, generator=torch.Generator().manual_seed(1000 * call + r)) for r in range(world)]
-        expect = parts[0].clone()
-        for x in parts[1:]:
-            expect += x  # fp32, rank order: what the kernel computes
-        for rank, outs, fault in res:
-            assert fault == 0
-            assert torch.equal(outs[call], expect), (rank, call)
+    k = 0
+    for n in ALLREDUCE_SIZES:
+        for call in range(3):
+            parts = [torch.randn(n, generator=torch.Generator().manual_seed(1000 * call + r)) for r in range(world)]
+            expect = parts[0].clone()
+            for x in parts[1:]:
+                expect += x  # fp32, rank order: what the kernel computes
+            for rank, outs, fault in res:
+                assert fault == 0
+                assert torch.equal(outs[k], expect), (rank, n, call)
+            k += 1
