@@ -41,6 +41,32 @@ def _channels_last(plane: Tensor, stream: int) -> Tensor:
     return dst
 
 
+def _check_kernel_inputs(fn: str, pts: Tensor, rotations: Tensor, plane: Tensor,
+                         grad_out: Tensor | None = None, taps: int = 1) -> None:
+    """Checks what the kernels index by: the op layer passes raw device
+    pointers, so a plane count, an upstream-gradient size or a device that
+    does not match would make a kernel read outside its buffers. Raises
+    ValueError / TypeError (the public wrappers check more, with the
+    reference's messages, before reaching here)."""
+    if pts.ndim != 2 or pts.shape[-1] != 3:
+        raise ValueError(f"{fn}: pts must be [B, 3], got {tuple(pts.shape)}")
+    if rotations.ndim != 3 or tuple(rotations.shape[-2:]) != (3, 3):
+        raise ValueError(f"{fn}: rotations must be [T, 3, 3], got {tuple(rotations.shape)}")
+    t = rotations.shape[0]
+    if plane.ndim != 4 or plane.shape[0] != 3 * t:
+        raise ValueError(f"{fn}: plane must be [3*T, C, H, W] with T={t}, got {tuple(plane.shape)}")
+    for name, x in (("pts", pts), ("rotations", rotations), ("plane", plane)):
+        if x.dtype != torch.float32:
+            raise TypeError(f"{fn}: {name} must be fp32, got {x.dtype}")
+        if not x.is_cuda or x.device != pts.device:
+            raise ValueError(f"{fn}: {name} is on {x.device}; all inputs must be on {pts.device} (CUDA)")
+    if grad_out is not None:
+        want = taps * pts.shape[0] * t * plane.shape[1]
+        if grad_out.numel() != want:
+            shape = (pts.shape[0], t * plane.shape[1]) if taps == 1 else (taps, pts.shape[0], t * plane.shape[1])
+            raise ValueError(f"{fn}: grad_out must have shape {shape}, got {tuple(grad_out.shape)}")
+
+
 def _from_channels_last(grad_cl: Tensor, like: Tensor, stream: int) -> Tensor:
     """(3T, H, W, C) → a (3T, C, H, W) tensor with ``like``'s memory layout."""
     if like.permute(0, 2, 3, 1).is_contiguous():
@@ -56,6 +82,7 @@ def _from_channels_last(grad_cl: Tensor, like: Tensor, stream: int) -> Tensor:
 
 @torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse", mutates_args=())
 def _kplanes_tilted_fuse(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor:
+    _check_kernel_inputs("kplanes_tilted_fuse", pts, rotations, plane)
     p = pts.contiguous()
     r = rotations.contiguous()
     c, h, w = plane.shape[1:]
@@ -80,6 +107,7 @@ def _(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor:
 def _kplanes_tilted_fuse_bwd(
     pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor
 ) -> list[Tensor]:
+    _check_kernel_inputs("kplanes_tilted_fuse_bwd", pts, rotations, plane, grad_out)
     p = pts.contiguous()
     r = rotations.contiguous()
     c, h, w = plane.shape[1:]
@@ -139,6 +167,7 @@ _kplanes_tilted_fuse.register_autograd(_kpt_backward, setup_context=_kpt_setup_c
 
 @torch.library.custom_op("quantem_cuda::kplanes_tilted_tv_fuse", mutates_args=())
 def _kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
+    _check_kernel_inputs("kplanes_tilted_tv_fuse", pts, rotations, plane)
     p = pts.contiguous()
     r = rotations.contiguous()
     c, hh, w = plane.shape[1:]
@@ -163,6 +192,7 @@ def _(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
 def _kplanes_tilted_tv_fuse_bwd(
     pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor, h: float
 ) -> list[Tensor]:
+    _check_kernel_inputs("kplanes_tilted_tv_fuse_bwd", pts, rotations, plane, grad_out, taps=4)
     p = pts.contiguous()
     r = rotations.contiguous()
     c, hh, w = plane.shape[1:]

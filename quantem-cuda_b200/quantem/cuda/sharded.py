@@ -235,6 +235,10 @@ def kplanes_fwd_bwd_sharded(
     order (deterministic, identical on every rank); ``work`` is then None.
     """
     _, world = _rank_world(group)
+    if fwd_bwd is None:
+        from quantem.cuda.core.ml._ops import _check_kernel_inputs
+
+        _check_kernel_inputs("kplanes_fwd_bwd_sharded", pts_local, rotations, plane, grad_out_local)
     if fwd_bwd is not None:
         out, g_pts, g_rot, g_plane = fwd_bwd(pts_local, rotations, plane, grad_out_local)
         works = []

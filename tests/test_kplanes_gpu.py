@@ -490,3 +490,18 @@ def test_ops_replay_from_a_cuda_graph():
     assert torch.equal(out, eager_out)
     for a, b in zip(grads, eager_grads):
         torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5 * b.abs().max().item())
+
+
+def test_raw_ops_refuse_mismatched_buffers_before_launch():
+    """An upstream gradient of the wrong size, or a plane left on the host,
+    would make the kernels read outside their buffers: the ops raise first."""
+    p = torch.rand(64, 3, device="cuda") * 2 - 1
+    r = torch.eye(3, device="cuda").expand(2, 3, 3).contiguous()
+    g = torch.rand(6, 8, 5, 5, device="cuda")
+    with pytest.raises(ValueError, match="grad_out must have shape"):
+        torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, g, torch.rand(64, 15, device="cuda"))
+    with pytest.raises(ValueError, match="grad_out must have shape"):
+        torch.ops.quantem_cuda.kplanes_tilted_tv_fuse_bwd(p, r, g, torch.rand(64, 16, device="cuda"), 0.1)
+    with pytest.raises(ValueError, match="all inputs must be on"):
+        torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, g.cpu())
+    torch.cuda.synchronize()

@@ -121,3 +121,18 @@ def test_fake_impls_give_output_shapes():
             torch.empty(10, 3), torch.empty(2, 3, 3), torch.empty(6, 4, 5, 5)
         )
         assert out.shape == (10, 8)
+
+
+def test_raw_kplanes_ops_check_what_the_kernels_index():
+    """The registered ops (called without the public wrappers) refuse inputs
+    that would make a kernel index outside its buffers, before any launch."""
+    p, r = torch.rand(5, 3), torch.eye(3).expand(2, 3, 3).contiguous()
+    with pytest.raises(ValueError, match=r"plane must be \[3\*T"):
+        torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, torch.rand(5, 4, 6, 6))
+    with pytest.raises(ValueError, match=r"rotations must be \[T, 3, 3\]"):
+        torch.ops.quantem_cuda.kplanes_tilted_fuse(p, torch.rand(2, 3), torch.rand(6, 4, 6, 6))
+    with pytest.raises(ValueError, match=r"pts must be \[B, 3\]"):
+        torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(torch.rand(5, 2), r, torch.rand(6, 4, 6, 6), torch.rand(5, 8))
+    # host tensors never reach a kernel
+    with pytest.raises(ValueError, match="CUDA"):
+        torch.ops.quantem_cuda.kplanes_tilted_tv_fuse(p, r, torch.rand(6, 4, 6, 6), 0.1)
