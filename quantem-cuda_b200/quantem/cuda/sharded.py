@@ -39,6 +39,7 @@ on CPU ranks with the CPU oracle in place of the device kernel.
 
 from __future__ import annotations
 
+import contextlib
 import weakref
 from typing import Callable
 
@@ -353,6 +354,25 @@ def _kplanes_fwd_bwd_bucketed(pts, rotations, plane, grad_out, group, world, buc
 # ── D-slabs over peer memory ────────────────────────────────────────────────
 
 
+@contextlib.contextmanager
+def _unmap_on_error(mapped: list[int]):
+    """Closes the peer mappings opened so far if opening the rest fails (the
+    other ranks then fail at the constructor's barrier, after the process
+    group's timeout)."""
+    from quantem.cuda import _core
+
+    try:
+        yield
+    except BaseException:
+        for ptr in mapped:
+            try:
+                _core.ipc_close(ptr)
+            except RuntimeError:
+                pass
+        mapped.clear()
+        raise
+
+
 def _same_on_every_rank(values: list, what: str) -> None:
     """Raises ValueError (on every rank, which all hold the same gathered
     list) unless every rank passed the same value."""
@@ -433,7 +453,7 @@ class PeerSlab:
         _same_on_every_rank([i[0] for i in infos], "PeerSlab (batch, global_d, height, width)")
         self._mapped: list[int] = []
         comm, prev_ptr, prev_dp, next_ptr, next_dp = [], 0, 0, 0, 0
-        with torch.cuda.device(self.device):
+        with torch.cuda.device(self.device), _unmap_on_error(self._mapped):
             for q, (_, dq, slab_h, comm_h) in enumerate(infos):
                 if q == rank:
                     comm.append(self._comm_mem.ptr)
@@ -597,7 +617,7 @@ class PeerAllReduce:
         _same_on_every_rank([i[0] for i in infos], "PeerAllReduce numel")
         self._mapped: list[int] = []
         bufs, comms = [], []
-        with torch.cuda.device(self.device):
+        with torch.cuda.device(self.device), _unmap_on_error(self._mapped):
             for q, (_, buf_h, comm_h) in enumerate(infos):
                 if q == rank:
                     bufs.append(self._buf_mem.ptr)

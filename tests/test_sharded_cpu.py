@@ -262,3 +262,21 @@ def test_peer_objects_reject_ranks_that_disagree():
     _same_on_every_rank([(2, 64, 8, 8)] * 4, "shape")
     with pytest.raises(ValueError, match="rank 2"):
         _same_on_every_rank([(2, 64, 8, 8), (2, 64, 8, 8), (2, 64, 8, 9)], "PeerSlab shape")
+
+
+def test_peer_mappings_are_closed_when_construction_fails(monkeypatch):
+    from quantem.cuda import _core, sharded
+
+    closed = []
+    monkeypatch.setattr(_core, "ipc_close", lambda ptr: closed.append(ptr))
+    mapped = [11, 22]
+    with pytest.raises(KeyError):
+        with sharded._unmap_on_error(mapped):
+            mapped.append(33)
+            raise KeyError("the third handle would not open")
+    assert closed == [11, 22, 33] and mapped == []
+    # nothing is closed when construction succeeds
+    ok = [44]
+    with sharded._unmap_on_error(ok):
+        pass
+    assert ok == [44] and closed == [11, 22, 33]
