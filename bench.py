@@ -96,7 +96,7 @@ class ClockSampler:
         0x200: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.002):
+    def __init__(self, device_index: int, period_s: float = 0.0005):
         self.period = period_s
         self.samples: list[tuple[int, int, float]] = []
         self.max_mhz = None
@@ -128,12 +128,18 @@ class ClockSampler:
             self.handle = None
 
     def _run(self):
+        # clock and reasons every period (timed regions can be a few ms long);
+        # power, the slowest query, on every 8th sample
         nv = self.nv
+        power = float("nan")
+        k = 0
         while not self._stop.is_set():
             try:
                 mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
                 reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                power = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                if k % 8 == 0:
+                    power = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                k += 1
                 self.samples.append((mhz, reasons, power))
             except Exception:
                 pass
@@ -163,7 +169,7 @@ class ClockSampler:
             "sm_max_mhz": self.max_mhz,
             "reasons": reasons,
             "samples": len(self.samples),
-            "power_w_max": max(s[2] for s in self.samples),
+            "power_w_max": max((s[2] for s in self.samples if s[2] == s[2]), default=None),
         }
 
 
