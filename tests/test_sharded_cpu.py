@@ -90,9 +90,10 @@ def _run(worker, world, *args):
     return sorted(out, key=lambda t: t[0])
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_tv_dslab_matches_whole_volume(world):
-    shape = (2, 11, 9, 12)
+# uneven slabs (11 planes over 2 and 3 ranks), and ranks that own a single
+# plane, whose two halos both come from neighbours (5 planes over 4 ranks)
+@pytest.mark.parametrize("world,shape", [(2, (2, 11, 9, 12)), (3, (2, 11, 9, 12)), (4, (1, 5, 6, 8))])
+def test_tv_dslab_matches_whole_volume(world, shape):
     out = _run(_tv_worker, world, shape)
     gen = torch.Generator().manual_seed(5)
     x = torch.rand(shape, generator=gen).numpy()
