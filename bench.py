@@ -21,11 +21,23 @@ Workloads (synthetic, seeded inputs with the documented shapes/distributions):
   tv_1024     tv_loss_sq_3d + tv_loss_iso_3d forward + gradient on [1024]^3,
               sum of 64 Gaussian blobs (sigma 8..64) + N(0, 0.01) noise, seed 4.
 
+The default line (tv_iso_l1) also carries a `kplanes` object: the kplanes
+workload measured in the same run, with the same keys, so that one run
+reports both halves of the metric.
+
 `value` is whole-job throughput with inputs resident in HBM; `e2e` is the same
-metric through the public API from pinned host buffers (host->device copy of
-the step's input and device->host read of its losses inside the timed
-region). `roofline` reports the dominant kernel's algorithmic bytes per launch
+metric through the public API from pinned host buffers: the host->device copy
+of the step's inputs and the device->host copy of everything the step
+produces (losses and gradients; for K-Planes the output and all gradients)
+inside the timed region (`e2e.losses_only` leaves the TV gradients on the
+device). `roofline` reports the dominant kernel's algorithmic bytes per launch
 over its CUDA-event duration against the measured HBM copy bandwidth.
+`ref_cuda` times the reference's own sm_100a kernels (its `_core` built from
+its sources into oracle/_ref/) on the same GPU, driven with the calls its op
+layer makes. `cpu_baseline` is the C oracle (OpenMP, all host threads) and
+`cpu_baseline_torch` the reference's pure-torch test definitions on the host
+cores, each on a bounded sample. At N > 1 `breakdown` splits a step into the
+local work and the exposed cross-rank exchange.
 `--impl reference` times the reference computation on the host cores (the
 CPU oracle, a restatement of the reference's kernels: the reference itself
 has no CPU implementation), on a bounded sample of the same workload.
@@ -300,7 +312,7 @@ class KernelTimer:
         return sum(s.elapsed_time(e) for s, e in sel) / max(1, len(sel))
 
 
-# ── CPU (oracle) baselines ──────────────────────────────────────────────────
+# ── CPU baselines: the C oracle (OpenMP) and the pure-torch definitions ─────
 
 
 def cpu_oracle():
@@ -312,19 +324,9 @@ def cpu_oracle():
     return oracle, oracle.threads()
 
 
-def cpu_tv_iso_l1(sample_d: int = 32, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
-    oracle, threads = cpu_oracle()
-    x = tv_iso_l1_volume(1, d=sample_d).numpy()
-    voxels = x.size
-    b, d, h, w = x.shape
-    n = b * (d - 1) * (h - 1) * (w - 1)
-
-    def step():
-        oracle.tv_iso_sum(x, 1e-8)
-        oracle.tv_iso_grad(x, 1.0 / n, 1e-8)
-        oracle.tv_l1_loss(x)
-        oracle.tv_l1_grad(x, [1.0, 1.0, 1.0])
-
+def _time_cpu(step, min_seconds: float, reps: int | None, warmup: int) -> tuple[float, int]:
+    """Runs `step` `warmup` times, then `reps` times (or until `min_seconds`
+    have passed); returns (elapsed seconds, steps timed)."""
     for _ in range(warmup):
         step()
     t0 = time.perf_counter()
@@ -334,16 +336,105 @@ def cpu_tv_iso_l1(sample_d: int = 32, min_seconds: float = 10.0, reps: int | Non
         k += 1
         el = time.perf_counter() - t0
         if (reps is not None and k >= reps) or (reps is None and el >= min_seconds):
-            break
-    per_step = el / k
+            return el, k
+
+
+def _torch_threads() -> int:
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def cpu_tv_iso_l1(sample_d: int = 32, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
+    oracle, threads = cpu_oracle()
+    x = tv_iso_l1_volume(1, d=sample_d).numpy()
+    b, d, h, w = x.shape
+    n = b * (d - 1) * (h - 1) * (w - 1)
+
+    def step():
+        oracle.tv_iso_sum(x, 1e-8)
+        oracle.tv_iso_grad(x, 1.0 / n, 1e-8)
+        oracle.tv_l1_loss(x)
+        oracle.tv_l1_grad(x, [1.0, 1.0, 1.0])
+
+    el, k = _time_cpu(step, min_seconds, reps, warmup)
     return {
-        "value": voxels / per_step,
+        "value": x.size / (el / k),
         "unit": "voxels/s",
         "cores": threads,
         "kind": "port",
         "sample": f"[4, {sample_d}, 256, 256] slab of the workload volume (1/{256 // sample_d} of it): "
         f"iso loss + iso grad + L1 sums + L1 grad with the C oracle (OpenMP), {k} reps, {el:.3f} s",
-    }, per_step
+    }, el / k
+
+
+def torch_cpu_tv_iso_l1(sample_d: int = 16, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
+    """The reference's pure-torch definitions (its tests' tv_iso_ref and
+    tv_l1_ref, restated in oracle/torch_ref.py) with autograd gradients."""
+    from oracle import torch_ref
+
+    threads = _torch_threads()
+    vol = tv_iso_l1_volume(1, d=sample_d)
+    ones = torch.ones(3)
+
+    def step():
+        v = vol.clone().requires_grad_(True)
+        torch_ref.tv_iso(v, 1e-8).backward()
+        v2 = vol.clone().requires_grad_(True)
+        torch_ref.tv_l1(v2).backward(ones)
+
+    el, k = _time_cpu(step, min_seconds, reps, warmup)
+    return {
+        "value": vol.numel() / (el / k),
+        "unit": "voxels/s",
+        "cores": threads,
+        "kind": "port (pure torch, the reference's test definitions)",
+        "sample": f"[4, {sample_d}, 256, 256] slab of the workload volume: iso loss + L1 sums with torch "
+        f"autograd gradients, {k} reps, {el:.3f} s",
+    }, el / k
+
+
+def cpu_tv_sq_128(min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
+    oracle, threads = cpu_oracle()
+    x = torch.rand((128, 128, 128), generator=torch.Generator().manual_seed(0)).numpy()
+
+    def step():
+        oracle.tv_sq_loss(x)
+        oracle.tv_sq_grad(x, 1.0)
+
+    el, k = _time_cpu(step, min_seconds, reps, warmup)
+    return {
+        "value": x.size / (el / k),
+        "unit": "voxels/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"the whole [128, 128, 128] volume: sq loss + grad with the C oracle (OpenMP), "
+        f"{k} reps, {el:.3f} s",
+    }, el / k
+
+
+def torch_cpu_tv_sq_128(min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
+    from oracle import torch_ref
+
+    threads = _torch_threads()
+    vol = torch.rand((128, 128, 128), generator=torch.Generator().manual_seed(0))
+
+    def step():
+        v = vol.clone().requires_grad_(True)
+        torch_ref.tv_sq(v).backward()
+
+    el, k = _time_cpu(step, min_seconds, reps, warmup)
+    return {
+        "value": vol.numel() / (el / k),
+        "unit": "voxels/s",
+        "cores": threads,
+        "kind": "port (pure torch, the reference's test definitions)",
+        "sample": f"the whole [128, 128, 128] volume: sq loss with a torch autograd gradient, {k} reps, "
+        f"{el:.3f} s",
+    }, el / k
 
 
 def cpu_kplanes(sample_n: int = 1 << 14, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
@@ -355,31 +446,45 @@ def cpu_kplanes(sample_n: int = 1 << 14, min_seconds: float = 10.0, reps: int | 
         oracle.kplanes_fwd(p, r, g)
         oracle.kplanes_bwd(p, r, g, u)
 
-    for _ in range(warmup):
-        step()
-    t0 = time.perf_counter()
-    k = 0
-    while True:
-        step()
-        k += 1
-        el = time.perf_counter() - t0
-        if (reps is not None and k >= reps) or (reps is None and el >= min_seconds):
-            break
-    per_step = el / k
+    el, k = _time_cpu(step, min_seconds, reps, warmup)
     return {
-        "value": sample_n / per_step,
+        "value": sample_n / (el / k),
         "unit": "points/s",
         "cores": threads,
         "kind": "port",
         "sample": f"first {sample_n} of the 2^20 points, forward + backward with the C oracle "
         f"(OpenMP), {k} reps, {el:.3f} s",
-    }, per_step
+    }, el / k
+
+
+def torch_cpu_kplanes(sample_n: int = 1 << 15, min_seconds: float = 10.0, reps: int | None = None,
+                      warmup: int = 1):
+    """The reference's pure-torch definition (its test's grid_sample
+    `reference`, restated in oracle/torch_ref.py) with autograd gradients."""
+    from oracle import torch_ref
+
+    threads = _torch_threads()
+    pts, rot, plane, up = kplanes_inputs(2)
+    p, u = pts[:sample_n].clone(), up[:sample_n].clone()
+
+    def step():
+        inp = [t.clone().requires_grad_(True) for t in (p, rot, plane)]
+        torch_ref.kplanes_tilted(*inp).backward(u)
+
+    el, k = _time_cpu(step, min_seconds, reps, warmup)
+    return {
+        "value": sample_n / (el / k),
+        "unit": "points/s",
+        "cores": threads,
+        "kind": "port (pure torch, the reference's test definition)",
+        "sample": f"first {sample_n} of the 2^20 points, forward + autograd backward (grid_sample), "
+        f"{k} reps, {el:.3f} s",
+    }, el / k
 
 
 def cpu_tv_1024(sample_d: int = 4, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
     oracle, threads = cpu_oracle()
     x = blob_volume(1024, 4, "cpu", 510, 510 + sample_d).numpy()
-    voxels = x.size
 
     def step():
         oracle.tv_sq_loss(x)
@@ -387,25 +492,15 @@ def cpu_tv_1024(sample_d: int = 4, min_seconds: float = 10.0, reps: int | None =
         oracle.tv_iso_sum(x, 1e-8)
         oracle.tv_iso_grad(x, 1.0, 1e-8)
 
-    for _ in range(warmup):
-        step()
-    t0 = time.perf_counter()
-    k = 0
-    while True:
-        step()
-        k += 1
-        el = time.perf_counter() - t0
-        if (reps is not None and k >= reps) or (reps is None and el >= min_seconds):
-            break
-    per_step = el / k
+    el, k = _time_cpu(step, min_seconds, reps, warmup)
     return {
-        "value": voxels / per_step,
+        "value": x.size / (el / k),
         "unit": "voxels/s",
         "cores": threads,
         "kind": "port",
         "sample": f"[{sample_d}, 1024, 1024] slab (planes 510..) of the volume: sq loss + grad and iso "
         f"loss + grad with the C oracle (OpenMP), {k} reps, {el:.3f} s",
-    }, per_step
+    }, el / k
 
 
 def cpu_kplanes_ms(sample_n: int = 2048, min_seconds: float = 10.0, reps: int | None = None, warmup: int = 1):
@@ -421,41 +516,117 @@ def cpu_kplanes_ms(sample_n: int = 2048, min_seconds: float = 10.0, reps: int | 
             oracle.kplanes_fwd(pts, rot, g)
             oracle.kplanes_bwd(pts, rot, g, up)
 
-    for _ in range(warmup):
-        step()
-    t0 = time.perf_counter()
-    k = 0
-    while True:
-        step()
-        k += 1
-        el = time.perf_counter() - t0
-        if (reps is not None and k >= reps) or (reps is None and el >= min_seconds):
-            break
-    per_step = el / k
+    el, k = _time_cpu(step, min_seconds, reps, warmup)
     return {
-        "value": sample_n / per_step,
+        "value": sample_n / (el / k),
         "unit": "points/s",
         "cores": threads,
         "kind": "port",
         "sample": f"{sample_n} points through all four levels (T=8, C=32), forward + backward with the "
         f"C oracle (OpenMP), {k} reps, {el:.3f} s",
-    }, per_step
+    }, el / k
 
 
 CPU_BASELINES = {
-    "tv_iso_l1": lambda **k: cpu_tv_iso_l1(**k),
-    "tv_sq_128": lambda **k: cpu_tv_iso_l1(**k),
-    "tv_1024": lambda **k: cpu_tv_1024(**k),
-    "kplanes": lambda **k: cpu_kplanes(**k),
-    "kplanes_ms": lambda **k: cpu_kplanes_ms(**k),
+    "tv_iso_l1": cpu_tv_iso_l1,
+    "tv_sq_128": cpu_tv_sq_128,
+    "tv_1024": cpu_tv_1024,
+    "kplanes": cpu_kplanes,
+    "kplanes_ms": cpu_kplanes_ms,
 }
+
+TORCH_CPU_BASELINES = {
+    "tv_iso_l1": torch_cpu_tv_iso_l1,
+    "tv_sq_128": torch_cpu_tv_sq_128,
+    "kplanes": torch_cpu_kplanes,
+}
+
+
+# ── the reference's own CUDA kernels on this GPU ────────────────────────────
+
+
+def reference_core():
+    """(the reference's `_core` built from its sources into oracle/_ref/, or
+    None, and the reason when it is missing)."""
+    try:
+        from oracle import oracle
+    except Exception as e:  # pragma: no cover
+        return None, f"oracle package not importable: {e}"
+    core = oracle.ref_core()
+    if core is None:
+        return None, "the reference's _core was not built into oracle/_ref"
+    return core, None
+
+
+def ref_cuda_tv_iso_l1(ctx: Ctx, vol: torch.Tensor, steps: int, warmup: int) -> dict:
+    """The reference's TV kernels driven as its op layer drives them
+    (src/quantem/cuda/core/_ops.py:39-92, :187-228): per step the isotropic
+    loss (zeroed accumulator, loss kernel, division by the corner count) and
+    its gradient (upstream / corner count, zero-filled gradient, gradient
+    kernel), then the L1 sums and their gradient."""
+    core, why = reference_core()
+    if core is None:
+        return {"unavailable": why}
+    b, d, h, w = vol.shape
+    n = float(max(1, b * (d - 1) * (h - 1) * (w - 1)))
+    dev = vol.device
+    g1 = torch.ones(1, device=dev)
+    g3 = torch.ones(3, device=dev)
+
+    def step():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        acc = torch.zeros(1, dtype=torch.float32, device=dev)
+        core.tv_loss_iso_3d_cuda(vol.data_ptr(), acc.data_ptr(), b, d, h, w, 1e-8, st)
+        _ = acc.squeeze(0) / n
+        g_scaled = (g1.reshape(1) / n).contiguous()
+        grad = torch.zeros_like(vol)
+        core.tv_loss_iso_3d_grad_cuda(vol.data_ptr(), g_scaled.data_ptr(), grad.data_ptr(), b, d, h, w, 1e-8, st)
+        acc3 = torch.zeros(3, dtype=torch.float32, device=dev)
+        core.tv_loss_l1_3d_cuda(vol.data_ptr(), acc3.data_ptr(), b, d, h, w, st)
+        grad3 = torch.empty_like(vol)
+        core.tv_loss_l1_3d_grad_cuda(vol.data_ptr(), g3.data_ptr(), grad3.data_ptr(), b, d, h, w, st)
+
+    ms = time_steps(ctx, step, steps, warmup)
+    return {"value": vol.numel() / (ms / steps / 1e3), "unit": "voxels/s", "ms_per_step": ms / steps,
+            "what": "the reference's sm_100a kernels (oracle/_ref/_core, built from its sources) through its "
+                    "op layer's calls: iso loss + iso gradient + L1 sums + L1 gradient, 4 sweeps"}
+
+
+def ref_cuda_kplanes(ctx: Ctx, p, r, g, u, steps: int, warmup: int) -> dict:
+    """The reference's K-Planes kernels driven as its op layer drives them
+    (src/quantem/cuda/core/ml/_ops.py:21-82): forward (channels-last copy of
+    the planes, output, kernel) and backward (channels-last copy, zero-filled
+    point, rotation and plane gradients, kernel, plane gradient permuted back
+    to the parameter layout)."""
+    core, why = reference_core()
+    if core is None:
+        return {"unavailable": why}
+    N, T = p.shape[0], r.shape[0]
+    C, H, W = g.shape[1:]
+    dev = p.device
+
+    def step():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        gc = g.permute(0, 2, 3, 1).contiguous()
+        out = torch.empty((N, T * C), dtype=torch.float32, device=dev)
+        core.kplanes_tilted_fuse_cuda(p.data_ptr(), r.data_ptr(), gc.data_ptr(), out.data_ptr(), N, T, C, H, W, st)
+        gc = g.permute(0, 2, 3, 1).contiguous()
+        g_pts, g_r, g_cl = torch.zeros_like(p), torch.zeros_like(r), torch.zeros_like(gc)
+        core.kplanes_tilted_fuse_grad_cuda(p.data_ptr(), r.data_ptr(), gc.data_ptr(), u.data_ptr(), g_cl.data_ptr(),
+                                           g_r.data_ptr(), g_pts.data_ptr(), N, T, C, H, W, st)
+        _ = g_cl.permute(0, 3, 1, 2).contiguous()
+
+    ms = time_steps(ctx, step, steps, warmup)
+    return {"value": N / (ms / steps / 1e3), "unit": "points/s", "ms_per_step": ms / steps,
+            "what": "the reference's sm_100a kernels (oracle/_ref/_core, built from its sources) through its "
+                    "op layer's calls: forward op + backward op"}
 
 
 # ── workloads (ours) ────────────────────────────────────────────────────────
 
 
 def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
-    from quantem.cuda import sharded
+    from quantem.cuda import _core, sharded
     from quantem.cuda.core import tv_loss_iso_3d_fwd_grad, tv_loss_l1_3d_fwd_grad
 
     dev = ctx.device
@@ -519,43 +690,99 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
         dom_ms = max(iso_ms, l1_ms)
         dom = "tv iso single sweep" if iso_ms >= l1_ms else "tv L1 single sweep"
 
-    # end to end: the public API from pinned host memory (each rank copies
-    # its own slab in, and reads the global losses back, every step)
+    # Cross-rank pieces at N > 1: the same sweeps on this rank's slab with no
+    # halo exchange and only a local finalize, timed alone; the difference to
+    # the step is the exposed halo exchange + cross-rank finalize wait.
+    breakdown = None
+    if ctx.world > 1:
+        from quantem.cuda._common import _workspace
+
+        dp = slab.shape[1]
+        has_prev, has_next = int(ctx.rank > 0), int(ctx.rank < ctx.world - 1)
+        loc_grads = [torch.empty_like(slab), torch.empty_like(slab)]
+        loc_acc = [torch.empty(1, device=dev), torch.empty(3, device=dev)]
+        loc_ws = _workspace(dev)
+        iso_scale = 1.0 / (4 * (global_d - 1) * 255 * 255)
+        flags = sharded._LOSS | sharded._GRAD | sharded._OVERWRITE
+
+        def local_step():
+            st = torch.cuda.current_stream(dev).cuda_stream
+            for (variant, g, eps, scale), acc, grad in zip(((sharded.ISO, g1, 1e-8, iso_scale), (sharded.L1, g3, 0.0, 1.0)),
+                                                          loc_acc, loc_grads):
+                _core.tv_loss_3d_slab_cuda(variant, flags, slab.data_ptr(), g.data_ptr(), acc.data_ptr(),
+                                           grad.data_ptr(), 4, dp, 256, 256, 1, dp - 1, has_prev, has_next,
+                                           eps, scale, loc_ws.data_ptr(), loc_ws.numel(), st)
+
+        local_ms = time_steps(ctx, local_step, steps, min(warmup, 3)) / steps
+        breakdown = {"step_ms": ms_step, "local_sweeps_ms": local_ms,
+                     "exposed_halo_and_cross_rank_sum_ms": ms_step - local_ms,
+                     "what": "local_sweeps_ms: both sweeps with a local finalize, no halo exchange and no "
+                             "cross-rank wait (max over ranks)"}
+
+    # end to end: the public API from pinned host memory. Each step copies its
+    # volume (slab) in and reads both losses and both gradients back into
+    # pinned host buffers, as the CPU computation leaves them in host memory.
     host = vol_cpu.pin_memory()
     res_host = torch.empty(4, pin_memory=True)
+    grad_host = [torch.empty(vol_cpu.shape, pin_memory=True) for _ in range(2)]
+    owned = (slice(None), slice(1, D_LOCAL + 1))
+
+    def read_back(li, ls, gi, gl, sl=None):
+        res_host[:1].copy_(li.reshape(1), non_blocking=True)
+        res_host[1:].copy_(ls, non_blocking=True)
+        grad_host[0].copy_(gi if sl is None else gi[sl], non_blocking=True)
+        grad_host[1].copy_(gl if sl is None else gl[sl], non_blocking=True)
+
     if ctx.world == 1:
-        def e2e_step():
+        def e2e_step(with_grads=True):
             v = host.to(dev, non_blocking=True)
-            li, _ = tv_loss_iso_3d_fwd_grad(v, g1, eps=1e-8)
-            ls, _ = tv_loss_l1_3d_fwd_grad(v, g3)
-            res_host[:1].copy_(li.reshape(1), non_blocking=True)
-            res_host[1:].copy_(ls, non_blocking=True)
+            li, gi = tv_loss_iso_3d_fwd_grad(v, g1, eps=1e-8)
+            ls, gl = tv_loss_l1_3d_fwd_grad(v, g3)
+            if with_grads:
+                read_back(li, ls, gi, gl)
+            else:
+                res_host[:1].copy_(li.reshape(1), non_blocking=True)
+                res_host[1:].copy_(ls, non_blocking=True)
             torch.cuda.current_stream().synchronize()
     elif ctx.args.tv_transport == "peer":
-        def e2e_step():
+        def e2e_step(with_grads=True):
             ps.owned.copy_(host, non_blocking=True)
-            (li, _), (ls, _) = ps.fwd_grad_many(terms, exchange=True, grads=grads)
-            res_host[:1].copy_(li.reshape(1), non_blocking=True)
-            res_host[1:].copy_(ls, non_blocking=True)
+            (li, gi), (ls, gl) = ps.fwd_grad_many(terms, exchange=True, grads=grads)
+            if with_grads:
+                read_back(li, ls, gi, gl, owned)
+            else:
+                res_host[:1].copy_(li.reshape(1), non_blocking=True)
+                res_host[1:].copy_(ls, non_blocking=True)
             torch.cuda.current_stream().synchronize()
     else:
-        def e2e_step():
+        def e2e_step(with_grads=True):
             slab[:, 1 : D_LOCAL + 1].copy_(host, non_blocking=True)
             sharded.exchange_halos(slab, check_shapes=False)
-            li, _ = sharded.tv_loss_slab_fwd_grad(sharded.ISO, slab, g1, global_d, 1e-8, exchange=False)
-            ls, _ = sharded.tv_loss_slab_fwd_grad(sharded.L1, slab, g3, global_d, exchange=False)
-            res_host[:1].copy_(li.reshape(1), non_blocking=True)
-            res_host[1:].copy_(ls, non_blocking=True)
+            li, gi = sharded.tv_loss_slab_fwd_grad(sharded.ISO, slab, g1, global_d, 1e-8, exchange=False)
+            ls, gl = sharded.tv_loss_slab_fwd_grad(sharded.L1, slab, g3, global_d, exchange=False)
+            if with_grads:
+                read_back(li, ls, gi, gl, owned)
+            else:
+                res_host[:1].copy_(li.reshape(1), non_blocking=True)
+                res_host[1:].copy_(ls, non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
     e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
+    e2e_losses_ms = time_steps(ctx, lambda: e2e_step(False), steps, min(warmup, 3))
+    ref_cuda = None
+    if ctx.world == 1:
+        ref_cuda = ref_cuda_tv_iso_l1(ctx, vol, steps, warmup)
     if ctx.world > 1 and ctx.args.tv_transport == "peer":
         ps.close()
     e2e = {
         "value": voxels_local * ctx.world / (e2e_ms / steps / 1e3),
         "unit": "voxels/s",
         "h2d_bytes_per_step": host.numel() * 4 * ctx.world,
-        "d2h_bytes_per_step": 16 * ctx.world,
+        "d2h_bytes_per_step": (16 + 2 * host.numel() * 4) * ctx.world,
+        "what": "volume copied in, both losses and both gradients copied back to pinned host memory",
+        "losses_only": {"value": voxels_local * ctx.world / (e2e_losses_ms / steps / 1e3),
+                        "d2h_bytes_per_step": 16 * ctx.world,
+                        "what": "gradients left on the device, losses read back"},
     }
 
     peak, peak_kind = measured_hbm_peak()
@@ -589,6 +816,8 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
         },
         "clocks": sampler.summary(),
         "e2e": e2e,
+        "ref_cuda": ref_cuda,
+        "breakdown": breakdown,
         "dtype": "f32",
     }
 
@@ -837,10 +1066,30 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
     tr = ncu_traffic("kplanes")
     kp_traffic = None if tr is None else tr["bytes_per_unit"] * N
 
+    # Cross-rank piece at N > 1: this rank's forward and backward ops with no
+    # gradient sum, timed alone; the difference to the step is the exposed
+    # sum of the plane and rotation gradients over the ranks.
+    breakdown = None
+    if ctx.world > 1:
+        def local_step():
+            torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, g)
+            torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(p, r, g, u)
+
+        local_ms = time_steps(ctx, local_step, steps, min(warmup, 3)) / steps
+        breakdown = {"step_ms": ms_step, "local_fwd_bwd_ms": local_ms,
+                     "exposed_gradient_sum_ms": ms_step - local_ms,
+                     "what": "local_fwd_bwd_ms: forward + backward ops on this rank's points with no gradient "
+                             "sum (max over ranks)"}
+
+    # End to end through the public API from pinned host memory: each step
+    # copies its inputs in and reads the output and every gradient back into
+    # pinned host buffers, as the CPU computation leaves them in host memory.
     e2e = None
+    ref_cuda = None
     if ctx.world == 1:
         hp, hr, hg, hu = (t.pin_memory() for t in (pts, rot, plane, up))
-        res_host = torch.empty(1, pin_memory=True)
+        out_host = torch.empty((N, T * C), pin_memory=True)
+        gh = [torch.empty(t.shape, pin_memory=True) for t in (pts, rot, plane)]
 
         def e2e_step():
             pp = hp.to(dev, non_blocking=True).requires_grad_(True)
@@ -848,35 +1097,51 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
             gg = hg.to(dev, non_blocking=True).requires_grad_(True)
             uu = hu.to(dev, non_blocking=True)
             out = kplanes_tilted_fuse(pp, rr, gg)
-            loss = (out * uu).sum()
-            loss.backward()
-            res_host.copy_(loss.detach().reshape(1), non_blocking=True)
+            out.backward(uu)
+            out_host.copy_(out.detach(), non_blocking=True)
+            for h_, t_ in zip(gh, (pp, rr, gg)):
+                h_.copy_(t_.grad, non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
         e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
         e2e = {"value": N / (e2e_ms / steps / 1e3), "unit": "points/s",
-               "h2d_bytes_per_step": sum(t.numel() * 4 for t in (hp, hr, hg, hu)), "d2h_bytes_per_step": 4}
+               "h2d_bytes_per_step": sum(t.numel() * 4 for t in (hp, hr, hg, hu)),
+               "d2h_bytes_per_step": (out_host.numel() + sum(t.numel() for t in gh)) * 4,
+               "what": "points, rotations, planes and upstream gradient copied in; output and the point, "
+                       "rotation and plane gradients copied back to pinned host memory"}
+        ref_cuda = ref_cuda_kplanes(ctx, p, r, g, u, steps, warmup)
     else:
         # each rank brings its points and upstream gradient in from pinned host
         # memory (planes and rotations are parameters resident on the device)
-        # and reads the summed rotation gradient back
+        # and reads its output, its point gradient and the summed rotation and
+        # plane gradients back
         hp, hu = pts.pin_memory(), up.pin_memory()
-        res_host = torch.empty(T * 9, pin_memory=True)
+        out_host = torch.empty((N, T * C), pin_memory=True)
+        gp_host = torch.empty((N, 3), pin_memory=True)
+        gr_host = torch.empty(T * 9, pin_memory=True)
+        gg_host = torch.empty(plane.shape, pin_memory=True)
 
         def e2e_step():
             pp = hp.to(dev, non_blocking=True)
             uu = hu.to(dev, non_blocking=True)
             if ctx.args.kp_reduce == "peer":
-                _, _, g_rot, _, _ = sharded.kplanes_fwd_bwd_sharded(pp, r, g, uu, reducer=reducer)
+                out, g_pts, g_rot, g_plane, _ = sharded.kplanes_fwd_bwd_sharded(pp, r, g, uu, reducer=reducer)
             else:
-                _, _, g_rot, _, _ = sharded.kplanes_fwd_bwd_sharded(pp, r, g, uu, buckets=ctx.args.kp_buckets)
-            res_host.copy_(g_rot.reshape(-1), non_blocking=True)
+                out, g_pts, g_rot, g_plane, _ = sharded.kplanes_fwd_bwd_sharded(pp, r, g, uu,
+                                                                              buckets=ctx.args.kp_buckets)
+            out_host.copy_(out, non_blocking=True)
+            gp_host.copy_(g_pts, non_blocking=True)
+            gr_host.copy_(g_rot.reshape(-1), non_blocking=True)
+            gg_host.copy_(g_plane, non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
         e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
         e2e = {"value": N * ctx.world / (e2e_ms / steps / 1e3), "unit": "points/s",
                "h2d_bytes_per_step": (hp.numel() + hu.numel()) * 4 * ctx.world,
-               "d2h_bytes_per_step": T * 9 * 4 * ctx.world}
+               "d2h_bytes_per_step": (out_host.numel() + gp_host.numel() + gr_host.numel() + gg_host.numel())
+               * 4 * ctx.world,
+               "what": "each rank's points and upstream gradient copied in; its output, point gradient and the "
+                       "summed rotation and plane gradients copied back to pinned host memory"}
     if ctx.world > 1 and ctx.args.kp_reduce == "peer":
         reducer.close()
 
@@ -904,6 +1169,8 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
                      "step_frac": (fwd_bytes + bwd_bytes) / (ms_step / 1e3) / 1e9 / peak},
         "clocks": sampler.summary(),
         "e2e": e2e,
+        "ref_cuda": ref_cuda,
+        "breakdown": breakdown,
         "dtype": "f32",
     }
 
@@ -934,7 +1201,7 @@ def run_reference(ctx: Ctx, args) -> dict | None:
     warmup = max(args.warmup, 3)
     cb, per_step = CPU_BASELINES[args.workload](reps=args.steps, warmup=warmup)
     metric = "K-Planes fwd+bwd points/sec" if args.workload.startswith("kplanes") else "TV fwd+grad voxels/sec"
-    return {
+    res = {
         "metric": metric,
         "value": cb["value"],
         "unit": cb["unit"],
@@ -945,6 +1212,14 @@ def run_reference(ctx: Ctx, args) -> dict | None:
         "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "dtype": "f32",
     }
+    if args.workload == "tv_iso_l1" and not args.no_kplanes:
+        # the other half of the metric, as in our arm's line
+        kb, kstep = cpu_kplanes(reps=max(1, args.steps // 4), warmup=1)
+        res["kplanes"] = {"metric": "K-Planes fwd+bwd points/sec", "value": kb["value"], "unit": kb["unit"],
+                          "ms_per_step": kstep * 1e3, "config": {"workload": DESCRIPTIONS["kplanes"],
+                                                                 "sample": kb["sample"]},
+                          "cpu_baseline": kb}
+    return res
 
 
 def _emit(line: str) -> None:
@@ -969,6 +1244,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tv_iso_l1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kplanes", action="store_true",
+                    help="default workload only: leave out the K-Planes half of the line")
     ap.add_argument("--kp-reduce", choices=("peer", "nccl"), default="peer",
                     help="multi-GPU K-Planes: gradient sum over peer memory or with NCCL all_reduce")
     ap.add_argument("--kp-buckets", type=int, default=1,
@@ -996,9 +1273,25 @@ def main() -> None:
     torch.cuda.set_device(ctx.device)
 
     res = WORKLOADS[args.workload](ctx, args.steps, warmup)
+    kp = None
+    if args.workload == "tv_iso_l1" and not args.no_kplanes:
+        # the default line carries both halves of the metric: TV (headline)
+        # and K-Planes, each timed in its own region of this run
+        kp = run_kplanes(ctx, args.steps, warmup)
 
     if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"], _ = CPU_BASELINES[args.workload]()
+        if args.workload in TORCH_CPU_BASELINES:
+            res["cpu_baseline_torch"], _ = TORCH_CPU_BASELINES[args.workload]()
+        if kp is not None:
+            kp["cpu_baseline"], _ = cpu_kplanes()
+            kp["cpu_baseline_torch"], _ = torch_cpu_kplanes()
+    for r_ in (res, kp):
+        if r_ is not None and isinstance(r_.get("ref_cuda"), dict) and "value" in r_["ref_cuda"]:
+            r_["ref_cuda"]["ours_over_reference"] = r_["value"] / r_["ref_cuda"]["value"]
+    if kp is not None:
+        kp.pop("dtype", None)
+        res["kplanes"] = kp
 
     if ctx.world > 1:
         dist.barrier(device_ids=[ctx.local_rank])

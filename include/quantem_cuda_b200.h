@@ -19,12 +19,10 @@
  *   K-Planes output     [N, T*C]          out[b, t*C + c]
  *
  * Differences from the reference launchers (csrc/ops/core.h, csrc/ops/core/ml.h):
- *   - each returns an int status instead of throwing std::runtime_error;
- *   - the TV loss entries take a caller-owned scratch buffer (`workspace`,
- *     `workspace_bytes`, at least tv_loss_3d_workspace_bytes()) that holds the
- *     per-CTA partial sums of the deterministic two-pass reduction. Its
- *     contents need no initialisation; calls that share one workspace must be
- *     ordered on the GPU (one stream, or events).
+ * each returns an int status instead of throwing std::runtime_error. The
+ * entries that replace a reference launcher keep its name and its argument
+ * list; everything else (deterministic *_ws_cuda loss forms, single sweeps,
+ * D-slabs, peer memory) is an addition under a new name.
  */
 #ifndef QUANTEM_CUDA_B200_H
 #define QUANTEM_CUDA_B200_H
@@ -64,14 +62,49 @@ int quantem_cuda_device_fault_word(int device, unsigned int *word, int clear);
 
 /* ── 3-D total variation ────────────────────────────────────────────────── */
 
-/* Bytes of scratch the TV loss entry points need for a [B, D, H, W] volume. */
+/* Bytes of scratch the deterministic TV loss entry points (*_ws_cuda, the
+ * single-sweep *_fwd_grad_cuda, tv_loss_3d_slab_cuda) need for a
+ * [B, D, H, W] volume. */
 size_t tv_loss_3d_workspace_bytes(int B, int D, int H, int W);
 
+/* The reference's three loss launchers, same arguments in the same order
+ * (csrc/ops/core.h:16-22, :40-45, :62-67; bound in Python as
+ * csrc/bindings/core.cpp:101-148). acc is pre-zeroed by the caller and
+ * receives acc += Σ; as in the reference, every CTA adds its sum with an fp32
+ * atomic, so the last bits can differ from run to run. The *_ws_cuda forms
+ * below compute the same sums deterministically. */
+
 /* Isotropic TV: acc[0] += Σ_b Σ_corners sqrt(dd² + dh² + dw² + eps), corners
- * [0,D-2]×[0,H-2]×[0,W-2]. Deterministic. Replaces tv_loss_iso_3d_cuda
+ * [0,D-2]×[0,H-2]×[0,W-2]. Replaces tv_loss_iso_3d_cuda
  * (reference csrc/ops/core.h:16-22, csrc/cuda/core/tv_loss.cu:98-121). */
 int tv_loss_iso_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W, float eps,
-                        void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+                        cudaStream_t stream);
+
+/* Squared-anisotropic TV: acc[0] += Σ_b Σ_axes Σ (forward difference)², each axis
+ * over its full complementary range. Replaces tv_loss_sq_3d_cuda
+ * (reference csrc/ops/core.h:40-45, tv_loss.cu:276-294). */
+int tv_loss_sq_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                       cudaStream_t stream);
+
+/* L1-anisotropic TV: acc[axis] += Σ_b Σ |forward difference along axis|, axis
+ * order (D, H, W). Replaces tv_loss_l1_3d_cuda (reference csrc/ops/core.h:62-67,
+ * tv_loss.cu:411-429). */
+int tv_loss_l1_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                       cudaStream_t stream);
+
+/* The same three sums, deterministic: each CTA writes an fp64 partial into a
+ * caller-owned scratch buffer (`workspace`, at least
+ * tv_loss_3d_workspace_bytes() bytes, contents need no initialisation) and
+ * one finalize kernel adds the partials in a fixed order, so acc receives the
+ * same bits on every run. Calls that share one workspace must be ordered on
+ * the GPU (one stream, or events). No counterpart in the reference, whose
+ * sums are atomic (tv_loss.cu:95, :273, :404-408). */
+int tv_loss_iso_3d_ws_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W, float eps,
+                           void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+int tv_loss_sq_3d_ws_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                          void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
+int tv_loss_l1_3d_ws_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                          void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* Gradient of the isotropic sum times *d_g_scaled (upstream / N); grad_vol is
  * fully written (zero when a dim is < 2). Replaces tv_loss_iso_3d_grad_cuda
@@ -79,22 +112,10 @@ int tv_loss_iso_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, i
 int tv_loss_iso_3d_grad_cuda(const float *d_vol, const float *d_g_scaled, float *d_grad_vol,
                              int B, int D, int H, int W, float eps, cudaStream_t stream);
 
-/* Squared-anisotropic TV: acc[0] += Σ_b Σ_axes Σ (forward difference)², each axis
- * over its full complementary range. Replaces tv_loss_sq_3d_cuda
- * (reference csrc/ops/core.h:40-45, tv_loss.cu:276-294). */
-int tv_loss_sq_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
-                       void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
-
 /* 2·g·∇ of the squared sum; grad_vol fully written. Replaces
  * tv_loss_sq_3d_grad_cuda (reference csrc/ops/core.h:50-56, tv_loss.cu:334-352). */
 int tv_loss_sq_3d_grad_cuda(const float *d_vol, const float *d_g, float *d_grad_vol, int B, int D,
                             int H, int W, cudaStream_t stream);
-
-/* L1-anisotropic TV: acc[axis] += Σ_b Σ |forward difference along axis|, axis
- * order (D, H, W). Replaces tv_loss_l1_3d_cuda (reference csrc/ops/core.h:62-67,
- * tv_loss.cu:411-429). */
-int tv_loss_l1_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
-                       void *d_workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* Σ_axis g[axis]·∇ of the per-axis L1 sums, sign(0) = 0; grad_vol fully
  * written. Replaces tv_loss_l1_3d_grad_cuda (reference csrc/ops/core.h:72-78,
@@ -103,7 +124,8 @@ int tv_loss_l1_3d_grad_cuda(const float *d_vol, const float *d_g, float *d_grad_
                             int H, int W, cudaStream_t stream);
 
 /* Single-sweep forward + gradient: one HBM pass reads the volume once and
- * writes both the loss (acc, as the *_cuda entries: acc += Σ) and the gradient
+ * writes both the loss (acc += Σ, deterministic as in the *_ws_cuda entries,
+ * same workspace) and the gradient
  * (as the *_grad_cuda entries, scaled by the device scalar(s) at d_g). No
  * reference counterpart: the reference runs the loss and gradient kernels as
  * two passes (tv_loss.cu:47-96 then :140-192, and likewise for sq and L1). */
@@ -117,17 +139,22 @@ int tv_loss_l1_3d_fwd_grad_cuda(const float *d_vol, const float *d_g, float *d_a
                                 float *d_grad_vol, int B, int D, int H, int W, void *d_workspace,
                                 size_t workspace_bytes, cudaStream_t stream);
 
-/* tv_loss_iso_3d_fwd_grad_cuda for callers that cannot allocate device memory
- * (code running where allocating or synchronising CUDA calls are not allowed,
- * or whose device memory is owned up front by another allocator). No
- * counterpart in the reference. The reduction scratch is a 48 KiB array
- * statically allocated in the library's device code (held by every GPU that
- * loads the library until exit); it covers every volume shape, and a request
- * for more scratch than it holds is rejected with QC_ERR_WORKSPACE_TOO_SMALL.
- * The first call on a device looks up the array's device address (once per
- * device, with that device current): make that first call before any stream
- * capture. All calls share the array: calls that overlap on the GPU (other
- * streams, other threads) race; nothing in it needs to start at zero. */
+/* tv_loss_iso_3d_fwd_grad_cuda without a workspace, for callers that cannot
+ * call cudaMalloc where they compute the loss: applications whose device
+ * memory is owned up front by one allocator or a fixed budget, and hosts that
+ * allocate only at start-up. No counterpart in the reference. The reduction
+ * scratch is a 48 KiB array statically allocated in the library's device code
+ * (every GPU that loads the library holds it until exit); it covers every
+ * volume shape, since the planner never uses more CTAs than it has slots.
+ * Shapes beyond the largest volume (H*W or B*D at or above 2^31) are refused
+ * with QC_ERR_INVALID_ARGUMENT. The entry allocates nothing, but it still
+ * launches kernels, and its first call on a device also does host-side set-up
+ * (it looks up the array's device address with that device current, sets
+ * kernel attributes, may load the module): make that first call before any
+ * stream capture. Do not use it across a cudaDeviceReset (the looked-up
+ * address is kept). Every call shares the array, which keeps the previous
+ * call's partial sums (nothing in it needs to start at zero): calls that
+ * overlap on the GPU (other streams, other threads) race. */
 int tv_loss_iso_3d_fwd_grad_noalloc_cuda(const float *d_vol, const float *d_g_scaled, float *d_acc,
                                          float *d_grad_vol, int B, int D, int H, int W, float eps,
                                          cudaStream_t stream);

@@ -79,15 +79,19 @@ PYBIND11_MODULE(_core, m) {
     m.def("tv_loss_3d_workspace_bytes", &tv_loss_3d_workspace_bytes, py::arg("B"), py::arg("D"),
           py::arg("H"), py::arg("W"));
 
+    // The reference's TV bindings, same names, arguments and argument names
+    // (csrc/bindings/core.cpp:101-148): loss sums accumulate into acc with
+    // fp32 atomics, as the reference's kernels do.
     m.def(
         "tv_loss_iso_3d_cuda",
-        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, float eps, uintptr_t ws,
-           size_t ws_bytes, uintptr_t stream) {
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, float eps, uintptr_t stream) {
             check(tv_loss_iso_3d_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W, eps,
-                                      ptr<void>(ws), ws_bytes, stream_of(stream)));
+                                      stream_of(stream)));
         },
+        "Isotropic 3-D TV forward. vol_ptr: fp32 [B,D,H,W]; acc_ptr: pre-zeroed one-element fp32 "
+        "accumulator (unnormalised corner sum added).",
         py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
-        py::arg("W"), py::arg("eps"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
+        py::arg("W"), py::arg("eps"), py::arg("stream_ptr"));
 
     m.def(
         "tv_loss_iso_3d_grad_cuda",
@@ -96,18 +100,20 @@ PYBIND11_MODULE(_core, m) {
             check(tv_loss_iso_3d_grad_cuda(ptr<const float>(vol), ptr<const float>(g),
                                            ptr<float>(grad), B, D, H, W, eps, stream_of(stream)));
         },
+        "Backward of tv_loss_iso_3d; g_scaled_ptr = upstream / N (device scalar); grad_vol fully "
+        "written.",
         py::arg("vol_ptr"), py::arg("g_scaled_ptr"), py::arg("grad_vol_ptr"), py::arg("B"),
         py::arg("D"), py::arg("H"), py::arg("W"), py::arg("eps"), py::arg("stream_ptr"));
 
     m.def(
         "tv_loss_sq_3d_cuda",
-        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, uintptr_t ws, size_t ws_bytes,
-           uintptr_t stream) {
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, uintptr_t stream) {
             check(tv_loss_sq_3d_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W,
-                                     ptr<void>(ws), ws_bytes, stream_of(stream)));
+                                     stream_of(stream)));
         },
+        "Squared-anisotropic 3-D TV forward; acc_ptr: pre-zeroed one-element accumulator.",
         py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
-        py::arg("W"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
+        py::arg("W"), py::arg("stream_ptr"));
 
     m.def(
         "tv_loss_sq_3d_grad_cuda",
@@ -116,18 +122,20 @@ PYBIND11_MODULE(_core, m) {
             check(tv_loss_sq_3d_grad_cuda(ptr<const float>(vol), ptr<const float>(g),
                                           ptr<float>(grad), B, D, H, W, stream_of(stream)));
         },
+        "Backward of tv_loss_sq_3d; g_ptr = raw upstream grad (x2 in the kernel); grad_vol fully "
+        "written.",
         py::arg("vol_ptr"), py::arg("g_ptr"), py::arg("grad_vol_ptr"), py::arg("B"), py::arg("D"),
         py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
 
     m.def(
         "tv_loss_l1_3d_cuda",
-        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, uintptr_t ws, size_t ws_bytes,
-           uintptr_t stream) {
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, uintptr_t stream) {
             check(tv_loss_l1_3d_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W,
-                                     ptr<void>(ws), ws_bytes, stream_of(stream)));
+                                     stream_of(stream)));
         },
+        "L1-anisotropic 3-D TV forward; acc_ptr: pre-zeroed 3-element accumulator (d, h, w).",
         py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
-        py::arg("W"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
+        py::arg("W"), py::arg("stream_ptr"));
 
     m.def(
         "tv_loss_l1_3d_grad_cuda",
@@ -136,8 +144,41 @@ PYBIND11_MODULE(_core, m) {
             check(tv_loss_l1_3d_grad_cuda(ptr<const float>(vol), ptr<const float>(g),
                                           ptr<float>(grad), B, D, H, W, stream_of(stream)));
         },
+        "Backward of tv_loss_l1_3d; g_ptr: 3 per-axis upstream grads (d, h, w); sign(0) = 0.",
         py::arg("vol_ptr"), py::arg("g_ptr"), py::arg("grad_vol_ptr"), py::arg("B"), py::arg("D"),
         py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
+
+    // Deterministic forms of the three sums (fixed-order reduction through a
+    // caller-owned workspace of tv_loss_3d_workspace_bytes() bytes).
+    m.def(
+        "tv_loss_iso_3d_ws_cuda",
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, float eps, uintptr_t ws,
+           size_t ws_bytes, uintptr_t stream) {
+            check(tv_loss_iso_3d_ws_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W, eps,
+                                         ptr<void>(ws), ws_bytes, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
+        py::arg("W"), py::arg("eps"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_sq_3d_ws_cuda",
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, uintptr_t ws, size_t ws_bytes,
+           uintptr_t stream) {
+            check(tv_loss_sq_3d_ws_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W,
+                                        ptr<void>(ws), ws_bytes, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
+        py::arg("W"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
+
+    m.def(
+        "tv_loss_l1_3d_ws_cuda",
+        [](uintptr_t vol, uintptr_t acc, int B, int D, int H, int W, uintptr_t ws, size_t ws_bytes,
+           uintptr_t stream) {
+            check(tv_loss_l1_3d_ws_cuda(ptr<const float>(vol), ptr<float>(acc), B, D, H, W,
+                                        ptr<void>(ws), ws_bytes, stream_of(stream)));
+        },
+        py::arg("vol_ptr"), py::arg("acc_ptr"), py::arg("B"), py::arg("D"), py::arg("H"),
+        py::arg("W"), py::arg("ws_ptr"), py::arg("ws_bytes"), py::arg("stream_ptr"));
 
     m.def(
         "tv_loss_3d_slab_cuda",

@@ -209,7 +209,22 @@ struct Plan {
     long long n_units;       // n_chunks * n_cols, chunk-major
     float eps;
     float scale;             // multiplies the gradient (and, on the host side, the sum)
+    float *acc_atomic;       // non-null: each CTA adds scale·(its sums) here with fp32
+                             // atomics instead of writing a workspace partial
 };
+
+// A CTA's sum of loss slot `slot` (threadIdx.x < kAccSlots): into the
+// workspace for the fixed-order finalize, or (reference-signature entries,
+// which have no workspace) added to the caller's accumulator atomically, as
+// the reference's loss kernels do (tv_loss.cu:95, :273, :404-408).
+template <int V>
+__device__ __forceinline__ void store_cta_sum(const Plan &pl, double *partials, int slot, double t) {
+    if (pl.acc_atomic != nullptr) {
+        if (slot < (V == QC_TV_L1 ? 3 : 1)) atomicAdd(pl.acc_atomic + slot, (float)(t * (double)pl.scale));
+    } else {
+        partials[(size_t)blockIdx.x * kAccSlots + slot] = t;
+    }
+}
 
 struct Unit {
     int n, h0, w0;
@@ -895,7 +910,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
         if (threadIdx.x < kAccSlots) {
             double t = 0.0;
             for (int w = 0; w < NW; ++w) t += sm.red[w][threadIdx.x];
-            partials[(size_t)blockIdx.x * kAccSlots + threadIdx.x] = t;
+            store_cta_sum<V>(pl, partials, threadIdx.x, t);
         }
     }
 }
@@ -989,7 +1004,7 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
         if (threadIdx.x < kAccSlots) {
             double t = 0.0;
             for (int w = 0; w < kGenThreads / 32; ++w) t += red[w][threadIdx.x];
-            partials[(size_t)blockIdx.x * kAccSlots + threadIdx.x] = t;
+            store_cta_sum<V>(pl, partials, threadIdx.x, t);
         }
     }
 }
@@ -1279,7 +1294,8 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
         int Dp, int H, int W, int d_lo, int d_hi, int has_prev, int has_next, float eps,
         float acc_scale, void *ws, size_t ws_bytes, cudaStream_t stream,
         const qc_tv_peers *peers = nullptr, unsigned long long seq = 0,
-        unsigned long long halo_seq = 0, int *n_partials_out = nullptr) {
+        unsigned long long halo_seq = 0, int *n_partials_out = nullptr,
+        bool atomic_acc = false) {
     QC_NVTX(variant == QC_TV_SQ ? "quantem::tv_sq" : variant == QC_TV_ISO ? "quantem::tv_iso" : "quantem::tv_l1");
     // n_partials_out != nullptr: launch the sweep only (its CTA partials stay
     // in ws, *n_partials_out of them) for a later tv_loss_3d_peer_finalize_cuda.
@@ -1302,8 +1318,12 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
                  "tv: H*W must be < 2^31");
     const int n_acc = variant == QC_TV_L1 ? 3 : 1;
     const bool empty = B == 0 || H == 0 || W == 0 || d_hi == d_lo;
+    QC_RETURN_IF(atomic_acc && (peers != nullptr || sweep_only || (flags & QC_TV_ACC_OVERWRITE)),
+                 QC_ERR_INVALID_ARGUMENT, "tv: atomic accumulation is for single-GPU acc += calls");
     if (want_loss) {
         QC_RETURN_IF(acc == nullptr, QC_ERR_INVALID_ARGUMENT, "tv: null acc");
+    }
+    if (want_loss && !atomic_acc) {
         QC_RETURN_IF(ws == nullptr || ws_bytes < workspace_bytes(), QC_ERR_WORKSPACE_TOO_SMALL,
                      "tv: workspace of %zu bytes is below the %zu required", ws_bytes,
                      workspace_bytes());
@@ -1331,12 +1351,13 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     pl.has_next = has_next ? 1 : 0;
     pl.eps = eps;
     pl.scale = acc_scale;
+    pl.acc_atomic = (atomic_acc && want_loss) ? acc : nullptr;
 
     const bool aligned = (reinterpret_cast<uintptr_t>(vol) % 16 == 0) &&
                          (!want_grad || reinterpret_cast<uintptr_t>(grad) % 16 == 0);
     const bool use_tma = (W % 4 == 0) && aligned && ((long long)B * Dp < (1LL << 31));
 
-    double *partials = reinterpret_cast<double *>(ws);
+    double *partials = atomic_acc ? nullptr : reinterpret_cast<double *>(ws);
     int grid = 0;
     int st = 0;
     HaloXchg xc{};
@@ -1372,7 +1393,7 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
         *n_partials_out = want_loss ? grid : 0;
         return 0;
     }
-    if (want_loss) {
+    if (want_loss && !atomic_acc) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(1);
         cfg.blockDim = dim3(kFinThreads);
@@ -1417,8 +1438,31 @@ int tv_loss_3d_slab_cuda(int variant, int flags, const float *d_vol, const float
                        has_prev, has_next, eps, acc_scale, d_workspace, workspace_bytes, stream);
 }
 
+// The reference's loss launchers (csrc/ops/core.h:16-22, :40-45, :62-67):
+// acc += Σ with each CTA's sum added by an fp32 atomic, as the reference's
+// kernels do; no workspace, not bitwise reproducible run to run.
 int tv_loss_iso_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W, float eps,
-                        void *d_workspace, size_t workspace_bytes, cudaStream_t stream) {
+                        cudaStream_t stream) {
+    return qc::tv::run(QC_TV_ISO, QC_TV_LOSS, d_vol, nullptr, d_acc, nullptr, B, D, H, W, 0, D, 0,
+                       0, eps, 1.0f, nullptr, 0, stream, nullptr, 0, 0, nullptr, true);
+}
+
+int tv_loss_sq_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                       cudaStream_t stream) {
+    return qc::tv::run(QC_TV_SQ, QC_TV_LOSS, d_vol, nullptr, d_acc, nullptr, B, D, H, W, 0, D, 0,
+                       0, 0.f, 1.0f, nullptr, 0, stream, nullptr, 0, 0, nullptr, true);
+}
+
+int tv_loss_l1_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                       cudaStream_t stream) {
+    return qc::tv::run(QC_TV_L1, QC_TV_LOSS, d_vol, nullptr, d_acc, nullptr, B, D, H, W, 0, D, 0,
+                       0, 0.f, 1.0f, nullptr, 0, stream, nullptr, 0, 0, nullptr, true);
+}
+
+// Deterministic forms: CTA sums go to the caller's workspace and one
+// finalize kernel adds them in a fixed order (bitwise reproducible).
+int tv_loss_iso_3d_ws_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W, float eps,
+                           void *d_workspace, size_t workspace_bytes, cudaStream_t stream) {
     return qc::tv::run(QC_TV_ISO, QC_TV_LOSS, d_vol, nullptr, d_acc, nullptr, B, D, H, W, 0, D, 0,
                        0, eps, 1.0f, d_workspace, workspace_bytes, stream);
 }
@@ -1429,8 +1473,8 @@ int tv_loss_iso_3d_grad_cuda(const float *d_vol, const float *d_g_scaled, float 
                        0, D, 0, 0, eps, 1.0f, nullptr, 0, stream);
 }
 
-int tv_loss_sq_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
-                       void *d_workspace, size_t workspace_bytes, cudaStream_t stream) {
+int tv_loss_sq_3d_ws_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                          void *d_workspace, size_t workspace_bytes, cudaStream_t stream) {
     return qc::tv::run(QC_TV_SQ, QC_TV_LOSS, d_vol, nullptr, d_acc, nullptr, B, D, H, W, 0, D, 0,
                        0, 0.f, 1.0f, d_workspace, workspace_bytes, stream);
 }
@@ -1441,8 +1485,8 @@ int tv_loss_sq_3d_grad_cuda(const float *d_vol, const float *d_g, float *d_grad_
                        0, 0.f, 1.0f, nullptr, 0, stream);
 }
 
-int tv_loss_l1_3d_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
-                       void *d_workspace, size_t workspace_bytes, cudaStream_t stream) {
+int tv_loss_l1_3d_ws_cuda(const float *d_vol, float *d_acc, int B, int D, int H, int W,
+                          void *d_workspace, size_t workspace_bytes, cudaStream_t stream) {
     return qc::tv::run(QC_TV_L1, QC_TV_LOSS, d_vol, nullptr, d_acc, nullptr, B, D, H, W, 0, D, 0,
                        0, 0.f, 1.0f, d_workspace, workspace_bytes, stream);
 }
@@ -1498,39 +1542,45 @@ int quantem_cuda_device_fault_word(int device, unsigned int *word, int clear) {
 // ── isotropic single sweep for callers that cannot allocate ────────────────
 //
 // Some callers of this library cannot call cudaMalloc (or any allocating
-// routine) at the point where they need the loss: code that runs inside a
-// host callback or another context where CUDA calls that may synchronise are
-// not allowed, and applications whose device memory is owned up front by a
-// single allocator (a framework's caching allocator, a fixed memory budget)
-// that another cudaMalloc would defeat or fail against. For them the
-// workspace of the deterministic reduction lives in this file instead: a
-// statically allocated device array, present on every GPU that loads the
-// library until the process exits.
+// routine) where they compute the loss: applications whose device memory is
+// owned up front by a single allocator (a framework's caching allocator, an
+// arena sized to a fixed budget) that another cudaMalloc would defeat or fail
+// against, and embedded or real-time hosts that allocate only at start-up.
+// For them the workspace of the deterministic reduction lives in this file
+// instead: a statically allocated device array, present on every GPU that
+// loads the library until the process exits. The entry still launches the
+// sweep and finalize kernels like every other entry point; it only avoids
+// allocating.
 
 namespace qc {
 namespace tv {
 
 // 2048 CTA partial-sum slots × 3 fp64 = 48 KiB: the most the sweep planner
-// uses for any volume shape (its grid is capped at kMaxPartials CTAs).
+// uses for any volume shape (it caps the grid at kMaxPartials CTAs).
 static __device__ __align__(256) double g_static_partials[kMaxPartials * kAccSlots];
+static_assert(sizeof(g_static_partials) >= (size_t)kMaxPartials * kAccSlots * sizeof(double),
+              "the static scratch must hold the planner's largest grid");
 
 // Device address of g_static_partials on the current device. The host-side
-// name is only a stand-in for the array, so it must be translated once per
-// device, with that device current, before a kernel may be given it.
+// name is only a stand-in for the array, so it is translated once per device,
+// with that device current, on the entry's first call there. The address is
+// kept for the life of the process: after cudaDeviceReset the module is
+// reloaded and the cached address is stale, so the entry must not be used
+// across a device reset.
 int static_partials_address(double **out) {
     static std::mutex mu;
-    static double *addr[64] = {nullptr};
+    static double *addr[kMaxDevices] = {nullptr};
     int dev = 0;
     QC_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
     std::lock_guard<std::mutex> lock(mu);
-    if (dev >= 0 && dev < 64 && addr[dev] != nullptr) {
+    if (dev >= 0 && dev < kMaxDevices && addr[dev] != nullptr) {
         *out = addr[dev];
         return 0;
     }
     double *p = nullptr;
     QC_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&p), g_static_partials),
                 "cudaGetSymbolAddress(static TV scratch)");
-    if (dev >= 0 && dev < 64) addr[dev] = p;
+    if (dev >= 0 && dev < kMaxDevices) addr[dev] = p;
     *out = p;
     return 0;
 }
@@ -1541,16 +1591,20 @@ int static_partials_address(double **out) {
 extern "C" int tv_loss_iso_3d_fwd_grad_noalloc_cuda(const float *d_vol, const float *d_g_scaled,
                                                     float *d_acc, float *d_grad_vol, int B, int D,
                                                     int H, int W, float eps, cudaStream_t stream) {
-    const size_t have = sizeof(qc::tv::g_static_partials);
-    const size_t need = tv_loss_3d_workspace_bytes(B, D, H, W);
-    QC_RETURN_IF(need > have, QC_ERR_WORKSPACE_TOO_SMALL,
-                 "tv_loss_iso_3d_fwd_grad_noalloc_cuda: [%d, %d, %d, %d] needs %zu bytes of "
-                 "scratch; the static scratch holds %zu",
-                 B, D, H, W, need, have);
+    // Shapes the sweep cannot index are refused before any CUDA call; every
+    // other shape fits the static scratch (static_assert above).
+    QC_RETURN_IF(B < 0 || D < 0 || H < 0 || W < 0, QC_ERR_INVALID_ARGUMENT,
+                 "tv_loss_iso_3d_fwd_grad_noalloc_cuda: negative shape [%d, %d, %d, %d]", B, D, H, W);
+    QC_RETURN_IF((long long)H * W >= (1LL << 31) || (long long)B * D >= (1LL << 31),
+                 QC_ERR_INVALID_ARGUMENT,
+                 "tv_loss_iso_3d_fwd_grad_noalloc_cuda: [%d, %d, %d, %d] exceeds the largest volume "
+                 "(H*W and B*D below 2^31)",
+                 B, D, H, W);
     double *scratch = nullptr;
     if (int st = qc::tv::static_partials_address(&scratch)) return st;
     return qc::tv::run(QC_TV_ISO, QC_TV_LOSS | QC_TV_GRAD, d_vol, d_g_scaled, d_acc, d_grad_vol, B,
-                       D, H, W, 0, D, 0, 0, eps, 1.0f, scratch, have, stream);
+                       D, H, W, 0, D, 0, 0, eps, 1.0f, scratch, sizeof(qc::tv::g_static_partials),
+                       stream);
 }
 
 // ── D-slabs over peer memory: halo exchange and the C ABI ─────────────────

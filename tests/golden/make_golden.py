@@ -7,12 +7,13 @@ live in its test files:
     tests/core/test_tv_loss.py:144-167    tv_l1_ref, ptycho_tv_ref
     tests/core/ml/test_kplanes_tilted.py:26-40  reference (einsum + grid_sample)
     tests/core/ml/test_kplanes_tilted.py:200-220 reference_tv (four taps)
-This script imports those modules from a checkout of the reference (default
-/root/reference, or $QUANTEM_CUDA_REFERENCE), runs them on CPU with seeded
-CPU-generated inputs, and stores inputs, outputs and autograd gradients as
-.npz files. The fixtures are committed; the tests read only the .npz files.
+This script imports those modules from a checkout of the reference (its root
+given as the first argument or in $QUANTEM_CUDA_REFERENCE), runs them on CPU
+with seeded CPU-generated inputs, and stores inputs, outputs and autograd
+gradients as .npz files. The fixtures are committed; the tests read only the
+.npz files.
 
-    python tests/golden/make_golden.py
+    QUANTEM_CUDA_REFERENCE=<quantem-cuda checkout> python tests/golden/make_golden.py
 """
 
 from __future__ import annotations
@@ -27,7 +28,17 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("QUANTEM_CUDA_REFERENCE", "/root/reference"))
+REF: Path | None = None
+
+
+def _reference_root() -> Path:
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QUANTEM_CUDA_REFERENCE")
+    if not root or not (Path(root) / "tests" / "core").is_dir():
+        raise SystemExit(
+            "make_golden.py: give the quantem-cuda checkout as the first argument or in "
+            "$QUANTEM_CUDA_REFERENCE (a directory holding tests/core/)"
+        )
+    return Path(root)
 
 
 def _import_reference_tests():
@@ -202,6 +213,8 @@ def make_kplanes_tv(kpmod) -> dict:
 
 
 def main() -> None:
+    global REF
+    REF = _reference_root()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     tvmod, kpmod = _import_reference_tests()
     np.savez_compressed(HERE / "tv_golden.npz", **make_tv(tvmod))

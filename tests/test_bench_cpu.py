@@ -42,3 +42,13 @@ def test_reference_arm_prints_one_json_line():
     res = json.loads(lines[0])
     assert res["impl"] == "reference" and res["unit"] == "voxels/s" and res["value"] > 0
     assert res["cpu_baseline"]["kind"] == "port" and res["e2e"]["h2d_bytes_per_step"] == 0
+    assert res["kplanes"]["unit"] == "points/s" and res["kplanes"]["value"] > 0
+
+
+def test_cpu_baselines_report_their_sample():
+    for fn, kw in ((bench.cpu_tv_sq_128, {}), (bench.torch_cpu_tv_sq_128, {}),
+                   (bench.torch_cpu_tv_iso_l1, {"sample_d": 4}), (bench.torch_cpu_kplanes, {"sample_n": 256})):
+        cb, per_step = fn(reps=1, warmup=0, **kw)
+        assert cb["value"] > 0 and cb["cores"] >= 1 and per_step > 0 and cb["sample"]
+    cb, _ = bench.cpu_tv_sq_128(reps=1, warmup=0)
+    assert cb["unit"] == "voxels/s" and "[128, 128, 128]" in cb["sample"]

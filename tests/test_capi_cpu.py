@@ -73,6 +73,17 @@ def test_argument_errors_need_no_device():
     # unknown variant
     assert f(7, 1, None, None, None, None, 1, 4, 4, 4, 0, 4, 0, 0, 0.0, 1.0, None, 0, None) == 10001
     assert b"variant" in lib.quantem_cuda_last_error()
+    # the reference-signature loss entries need no workspace, but check their shape
+    r = lib.tv_loss_sq_3d_cuda
+    r.restype = ctypes.c_int
+    r.argtypes = [vp, vp, i, i, i, i, vp]
+    assert r(vp(16), vp(16), -1, 4, 4, 4, None) == 10001
+    # the allocation-free entry refuses shapes beyond the largest volume before any CUDA call
+    na = lib.tv_loss_iso_3d_fwd_grad_noalloc_cuda
+    na.restype = ctypes.c_int
+    na.argtypes = [vp, vp, vp, vp, i, i, i, i, fl, vp]
+    assert na(vp(16), vp(16), vp(16), vp(16), 1, 4, 1 << 16, 1 << 15, 1e-8, None) == 10001
+    assert b"exceeds the largest volume" in lib.quantem_cuda_last_error()
     # loss without a workspace
     st = f(0, 1, vp(16), None, vp(16), None, 1, 4, 4, 4, 0, 4, 0, 0, 0.0, 1.0, None, 0, None)
     assert st == 10002
@@ -101,6 +112,34 @@ def test_core_binding_has_reference_names():
     assert int(_core.__cudart_version__) >= 12000
     with pytest.raises(RuntimeError, match="QC_ERR_INVALID_ARGUMENT"):
         _core.tv_loss_3d_slab_cuda(9, 1, 0, 0, 0, 0, 1, 2, 2, 2, 0, 2, 0, 0, 0.0, 1.0, 0, 0, 0)
+
+
+def _signature(fn) -> list[tuple[str, str]]:
+    """(argument name, Python type) pairs from a pybind11 function's docstring."""
+    head = fn.__doc__.strip().splitlines()[0]
+    args = head[head.index("(") + 1 : head.rindex(")")]
+    out = []
+    for part in re.split(r",\s*(?=[A-Za-z_]+:)", args):
+        name, typ = part.split(":", 1)
+        out.append((name.strip(), "float" if "Float" in typ else "int"))
+    return out
+
+
+def test_core_binding_takes_the_reference_arguments():
+    """Every function of the reference's `_core` (built from its sources into
+    oracle/_ref/ when the reference tree was present; csrc/bindings/core.cpp:101-148,
+    csrc/bindings/core/ml.cpp:89-128) exists here with the same argument names,
+    order and kinds, so the reference's op layer calls this binding unchanged."""
+    from oracle import oracle
+    from quantem.cuda import _core
+
+    ref = oracle.ref_core()
+    if ref is None:
+        pytest.skip("reference _core not built into oracle/_ref")
+    names = [n for n in dir(ref) if n.endswith("_cuda")]
+    assert len(names) == 10
+    for name in names:
+        assert _signature(getattr(_core, name)) == _signature(getattr(ref, name)), name
 
 
 def test_peer_entries_reject_bad_arguments_without_a_device():

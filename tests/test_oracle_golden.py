@@ -142,3 +142,25 @@ def test_kplanes_tv_border_points(kp_tv_golden):
     np.testing.assert_allclose(out, kp_tv_golden["tv_border/out_f32"], rtol=1e-4, atol=1e-6)
     gp, _, _ = oracle.kplanes_tv_bwd(pts, rot, plane, np.ones_like(out), h)
     np.testing.assert_allclose(gp, kp_tv_golden["tv_border/grad_pts_f32"], rtol=1e-4, atol=1e-6)
+
+
+def test_torch_restatement_matches_reference_definitions(tv_golden, kp_golden):
+    """The pure-torch CPU restatement timed as a baseline by bench.py
+    (oracle/torch_ref.py) gives the golden fp64 results of the reference's own
+    torch definitions."""
+    import torch
+
+    from oracle import torch_ref
+
+    for name in _tv_names(tv_golden):
+        vol = torch.from_numpy(tv_golden[f"{name}/vol"]).double()
+        iso_ref = tv_golden[f"{name}/iso_loss"]
+        if not np.isnan(iso_ref):
+            np.testing.assert_allclose(torch_ref.tv_iso(vol, 1e-8).item(), iso_ref, rtol=1e-10)
+        np.testing.assert_allclose(torch_ref.tv_sq(vol).item(), tv_golden[f"{name}/sq_loss"], rtol=1e-10)
+        np.testing.assert_allclose(torch_ref.tv_l1(vol).numpy(), tv_golden[f"{name}/l1_sums"], rtol=1e-10)
+    names = sorted({k.split("/")[0] for k in kp_golden if not k.startswith("border")})
+    for name in names:
+        t = [torch.from_numpy(kp_golden[f"{name}/{k}"]).double() for k in ("pts", "rotations", "plane")]
+        out = torch_ref.kplanes_tilted(*t).numpy()
+        np.testing.assert_allclose(out, kp_golden[f"{name}/out_f64"], rtol=1e-10, atol=1e-12)

@@ -39,6 +39,7 @@ SHAPES = [
     (2, 9, 31, 37),
     (1, 64, 64, 64),
     (5, 2, 3, 8),
+    (128, 128, 128),  # the single-volume squared-TV benchmark shape
 ]
 
 FWD_RTOL = 1e-5  # forward tolerance (relative)
@@ -250,18 +251,34 @@ def test_slab_decomposition_reassembles_whole_volume():
 
 def test_c_abi_reference_signatures():
     """Calls the reference-named entry points through the C ABI with the
-    reference's conventions (pre-zeroed accumulator, acc += sum)."""
+    reference's argument lists and conventions (pre-zeroed accumulator,
+    acc += sum; csrc/ops/core.h:16-78), and the deterministic workspace form."""
     lib = ctypes.CDLL(str(Path(_core.__file__).parent / "libquantem_cuda_b200.so"))
     vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
-    lib.tv_loss_sq_3d_cuda.argtypes = [vp, vp, i, i, i, i, vp, ctypes.c_size_t, vp]
+    lib.tv_loss_sq_3d_cuda.argtypes = [vp, vp, i, i, i, i, vp]
+    lib.tv_loss_iso_3d_cuda.argtypes = [vp, vp, i, i, i, i, f, vp]
+    lib.tv_loss_l1_3d_cuda.argtypes = [vp, vp, i, i, i, i, vp]
+    lib.tv_loss_sq_3d_ws_cuda.argtypes = [vp, vp, i, i, i, i, vp, ctypes.c_size_t, vp]
     lib.tv_loss_iso_3d_grad_cuda.argtypes = [vp, vp, vp, i, i, i, i, f, vp]
     vol = rand_vol((3, 20, 24, 68), 16)
     v = vol.cuda()
-    ws = torch.empty(lib.tv_loss_3d_workspace_bytes(0, 0, 0, 0), dtype=torch.uint8, device="cuda")
-    acc = torch.full((1,), 2.0, device="cuda")  # accumulates on top of 2.0
+    x = vol.numpy()
     st = torch.cuda.current_stream().cuda_stream
-    assert lib.tv_loss_sq_3d_cuda(v.data_ptr(), acc.data_ptr(), 3, 20, 24, 68, ws.data_ptr(), ws.numel(), st) == 0
-    np.testing.assert_allclose(acc.item() - 2.0, oracle.tv_sq_loss(vol.numpy()), rtol=FWD_RTOL)
+    acc = torch.full((1,), 2.0, device="cuda")  # accumulates on top of 2.0
+    assert lib.tv_loss_sq_3d_cuda(v.data_ptr(), acc.data_ptr(), 3, 20, 24, 68, st) == 0
+    np.testing.assert_allclose(acc.item() - 2.0, oracle.tv_sq_loss(x), rtol=FWD_RTOL)
+    acc = torch.zeros(1, device="cuda")
+    assert lib.tv_loss_iso_3d_cuda(v.data_ptr(), acc.data_ptr(), 3, 20, 24, 68, f(1e-8), st) == 0
+    np.testing.assert_allclose(acc.item(), oracle.tv_iso_sum(x, 1e-8), rtol=FWD_RTOL)
+    acc3 = torch.zeros(3, device="cuda")
+    assert lib.tv_loss_l1_3d_cuda(v.data_ptr(), acc3.data_ptr(), 3, 20, 24, 68, st) == 0
+    np.testing.assert_allclose(acc3.cpu().numpy(), oracle.tv_l1_loss(x), rtol=FWD_RTOL)
+    ws = torch.empty(lib.tv_loss_3d_workspace_bytes(0, 0, 0, 0), dtype=torch.uint8, device="cuda")
+    acc_ws = [torch.full((1,), 2.0, device="cuda") for _ in range(2)]
+    for a in acc_ws:
+        assert lib.tv_loss_sq_3d_ws_cuda(v.data_ptr(), a.data_ptr(), 3, 20, 24, 68, ws.data_ptr(), ws.numel(), st) == 0
+    np.testing.assert_allclose(acc_ws[0].item() - 2.0, oracle.tv_sq_loss(x), rtol=FWD_RTOL)
+    assert torch.equal(acc_ws[0], acc_ws[1])  # fixed-order reduction: the same bits every call
     g = torch.tensor([0.25], device="cuda")
     grad = torch.empty_like(v)
     assert lib.tv_loss_iso_3d_grad_cuda(v.data_ptr(), g.data_ptr(), grad.data_ptr(), 3, 20, 24, 68, f(1e-6), st) == 0
@@ -322,6 +339,49 @@ def test_full_size_iso_l1_workload():
     assert_grad_close(grad, oracle.tv_l1_grad(x, [1.0, 1.0, 1.0]))
 
 
+def _compare_grad_chunked(grad: torch.Tensor, expected: np.ndarray, planes: int = 32) -> tuple[float, float]:
+    """Element-wise gradient check of a large volume, plane slab by plane slab
+    (keeps the fp64 temporaries small): |got - expected| <= GRAD_RTOL·|expected|
+    + 1e-6·max|expected|. Returns (largest error, largest magnitude)."""
+    g = grad.reshape(-1, *grad.shape[-2:])
+    e = expected.reshape(-1, *expected.shape[-2:])
+    scale = max(float(np.abs(e[k : k + planes]).max()) for k in range(0, e.shape[0], planes))
+    worst = 0.0
+    for k in range(0, e.shape[0], planes):
+        a = g[k : k + planes].cpu().numpy().astype(np.float64)
+        b = e[k : k + planes].astype(np.float64)
+        err = np.abs(a - b)
+        assert np.all(err <= GRAD_RTOL * np.abs(b) + 1e-6 * scale), f"planes {k}..{k + planes}: max err {err.max():.3e}"
+        worst = max(worst, float(err.max()))
+    return worst, scale
+
+
+def test_tomography_scale_blob_volume():
+    """[1024, 1024, 1024] sum of 64 Gaussian blobs + N(0, 0.01) noise, seed 4
+    (the tomography-scale configuration): squared and isotropic loss and
+    gradient from the single-sweep ops against the oracle on the whole volume.
+    On this smooth field most differences are small against the values, which
+    is where the isotropic sweep's approximate square roots would show."""
+    import bench
+
+    v = bench.blob_volume(1024, 4, "cuda")
+    x = v.cpu().numpy()
+    loss, grad = tv_loss_sq_3d_fwd_grad(v, 1.0)
+    ref = oracle.tv_sq_loss(x)
+    rel = abs(loss.item() - ref) / ref
+    assert rel <= FWD_RTOL, rel
+    _compare_grad_chunked(grad, oracle.tv_sq_grad(x, 1.0))
+    del grad
+    loss, grad = tv_loss_iso_3d_fwd_grad(v, 1.0, eps=1e-8)
+    ref = oracle.tv_iso_loss(x, 1e-8)
+    rel = abs(loss.item() - ref) / ref
+    # the loss term uses the MUFU square root (relative error below 2^-22 per
+    # term, accumulated in fp64): 1e-5 is the stated tolerance
+    assert rel <= FWD_RTOL, rel
+    print(f"iso loss rel err on the blob volume: {rel:.3e} (tolerance {FWD_RTOL:g})")
+    _compare_grad_chunked(grad, oracle.tv_iso_grad(x, 1.0 / n_corners(x.shape), 1e-8))
+
+
 def test_no_kernel_gave_up_waiting():
     torch.cuda.synchronize()
     assert _core.device_fault_word(torch.cuda.current_device()) == 0
@@ -373,3 +433,89 @@ def test_ops_replay_from_a_cuda_graph():
         graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(loss, eager[0][0]) and torch.equal(grad, eager[0][1]) and torch.equal(sums, eager[1])
+
+
+class _ReferenceOpLayerCalls:
+    """The `_core` calls the reference's TV op layer makes, in its order and
+    with its buffers (src/quantem/cuda/core/_ops.py:39-228): a zeroed
+    accumulator for each loss (the iso sum then divided by the corner count),
+    an upstream scalar (iso: divided by the corner count) and a zero- or
+    empty-initialised gradient for each backward. Bound to either `_core`."""
+
+    def __init__(self, core):
+        self.core = core
+
+    def _args(self, vol):
+        b, d, h, w = vol.shape
+        return b, d, h, w, torch.cuda.current_stream().cuda_stream
+
+    def iso(self, vol, eps):
+        b, d, h, w, st = self._args(vol)
+        acc = torch.zeros(1, dtype=torch.float32, device=vol.device)
+        self.core.tv_loss_iso_3d_cuda(vol.data_ptr(), acc.data_ptr(), b, d, h, w, float(eps), st)
+        return acc.squeeze(0) / float(n_corners(vol.shape))
+
+    def iso_bwd(self, vol, grad_out, eps):
+        b, d, h, w, st = self._args(vol)
+        g = (grad_out.reshape(1) / float(n_corners(vol.shape))).contiguous()
+        grad = torch.zeros_like(vol)
+        self.core.tv_loss_iso_3d_grad_cuda(vol.data_ptr(), g.data_ptr(), grad.data_ptr(), b, d, h, w, float(eps), st)
+        return grad
+
+    def sq(self, vol):
+        b, d, h, w, st = self._args(vol)
+        acc = torch.zeros(1, dtype=torch.float32, device=vol.device)
+        self.core.tv_loss_sq_3d_cuda(vol.data_ptr(), acc.data_ptr(), b, d, h, w, st)
+        return acc.squeeze(0)
+
+    def sq_bwd(self, vol, grad_out):
+        b, d, h, w, st = self._args(vol)
+        g = grad_out.reshape(1).contiguous()
+        grad = torch.empty_like(vol)
+        self.core.tv_loss_sq_3d_grad_cuda(vol.data_ptr(), g.data_ptr(), grad.data_ptr(), b, d, h, w, st)
+        return grad
+
+    def l1(self, vol):
+        b, d, h, w, st = self._args(vol)
+        acc = torch.zeros(3, dtype=torch.float32, device=vol.device)
+        self.core.tv_loss_l1_3d_cuda(vol.data_ptr(), acc.data_ptr(), b, d, h, w, st)
+        return acc
+
+    def l1_bwd(self, vol, grad_out):
+        b, d, h, w, st = self._args(vol)
+        g = grad_out.reshape(3).contiguous()
+        grad = torch.empty_like(vol)
+        self.core.tv_loss_l1_3d_grad_cuda(vol.data_ptr(), g.data_ptr(), grad.data_ptr(), b, d, h, w, st)
+        return grad
+
+
+@pytest.mark.parametrize("shape", [(3, 32, 32, 32), (2, 40, 70, 260), (1, 33, 57, 18), (1, 128, 128, 128)])
+def test_reference_op_layer_calls_run_unchanged_on_this_core(shape):
+    """The reference's op layer, re-pointed at this `_core`, gives the oracle's
+    results; and the same calls on the reference's own `_core` (when built)
+    agree with it."""
+    x = rand_vol(shape, 23).numpy()
+    v = torch.from_numpy(x).cuda()
+    eps = 1e-8
+    layers = [("here", _ReferenceOpLayerCalls(_core))]
+    if oracle.ref_core() is not None:
+        layers.append(("reference", _ReferenceOpLayerCalls(oracle.ref_core())))
+    up = torch.tensor([0.8], device="cuda")
+    up3 = torch.tensor([0.7, 1.3, 0.2], device="cuda")
+    results = {}
+    for tag, ops in layers:
+        results[tag] = (ops.iso(v, eps), ops.sq(v), ops.l1(v), ops.iso_bwd(v, up, 1e-6), ops.sq_bwd(v, up),
+                        ops.l1_bwd(v, up3))
+    iso, sq, l1, g_iso, g_sq, g_l1 = results["here"]
+    np.testing.assert_allclose(iso.item(), oracle.tv_iso_loss(x, eps), rtol=FWD_RTOL)
+    np.testing.assert_allclose(sq.item(), oracle.tv_sq_loss(x), rtol=FWD_RTOL)
+    np.testing.assert_allclose(l1.cpu().numpy(), oracle.tv_l1_loss(x), rtol=FWD_RTOL)
+    assert_grad_close(g_iso, oracle.tv_iso_grad(x, 0.8 / n_corners(shape), 1e-6))
+    assert_grad_close(g_sq, oracle.tv_sq_grad(x, 0.8))
+    assert_grad_close(g_l1, oracle.tv_l1_grad(x, np.array([0.7, 1.3, 0.2], np.float32)))
+    if "reference" in results:
+        for mine, theirs in zip(results["here"][:3], results["reference"][:3]):
+            torch.testing.assert_close(mine, theirs, rtol=FWD_RTOL, atol=0)
+        for mine, theirs in zip(results["here"][3:], results["reference"][3:]):
+            scale = theirs.abs().max().item()
+            torch.testing.assert_close(mine, theirs, rtol=GRAD_RTOL, atol=1e-6 * scale)
