@@ -770,8 +770,22 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
     e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
     e2e_losses_ms = time_steps(ctx, lambda: e2e_step(False), steps, min(warmup, 3))
     ref_cuda = None
+    one_sweep = None
     if ctx.world == 1:
         ref_cuda = ref_cuda_tv_iso_l1(ctx, vol, steps, warmup)
+        # the same two losses and their summed gradient from one sweep
+        # (tv_loss_multi_3d_fwd_grad), timed on its own: not the headline step
+        from quantem.cuda.core import tv_loss_multi_3d_fwd_grad
+
+        t_one = KernelTimer()
+        both = t_one.wrap(lambda: tv_loss_multi_3d_fwd_grad(vol, iso=g1, l1=g3, eps=1e-8))
+        one_ms = time_steps(ctx, both, steps, warmup) / steps
+        peak_, _ = measured_hbm_peak()
+        one_sweep = {"value": voxels_local / (one_ms / 1e3), "unit": "voxels/s", "ms_per_step": one_ms,
+                     "op_ms": t_one.mean_ms(steps),
+                     "roofline_frac": 8.0 * voxels_local / (t_one.mean_ms(steps) / 1e3) / 1e9 / peak_,
+                     "what": "iso + L1 losses and their summed gradient in one sweep "
+                             "(tv_loss_multi_3d_fwd_grad; 8 B/voxel for both terms)"}
     if ctx.world > 1 and ctx.args.tv_transport == "peer":
         ps.close()
     e2e = {
@@ -817,6 +831,7 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
         "clocks": sampler.summary(),
         "e2e": e2e,
         "ref_cuda": ref_cuda,
+        "one_sweep": one_sweep,
         "breakdown": breakdown,
         "dtype": "f32",
     }

@@ -139,6 +139,29 @@ int tv_loss_l1_3d_fwd_grad_cuda(const float *d_vol, const float *d_g, float *d_a
                                 float *d_grad_vol, int B, int D, int H, int W, void *d_workspace,
                                 size_t workspace_bytes, cudaStream_t stream);
 
+/* Several TV terms of one volume in one sweep: the volume is read once, each
+ * term's loss sums are accumulated, and one gradient — the gain-weighted sum
+ * of the terms' gradients — is written. No counterpart in the reference,
+ * which runs one loss kernel and one gradient kernel per term; a caller that
+ * regularises with two or three terms (isotropic + L1, squared + isotropic)
+ * reads the volume once instead of once per term.
+ *   terms: two or three of QC_TV_TERM_SQ, QC_TV_TERM_ISO, QC_TV_TERM_L1
+ *   flags: 0 (acc += ...) or QC_TV_ACC_OVERWRITE (acc = ...)
+ *   d_g:   5 device floats [g_sq, g_iso, g_d, g_h, g_w]: the gradient written
+ *          is g_sq·∇Σsq + g_iso·∇Σiso + Σ_axis g_axis·∇Σ|Δ_axis| (the raw
+ *          sums; for the mean isotropic loss pass g_iso = upstream / N)
+ *   d_acc: 5 device floats [Σsq, iso_scale·Σiso, Σ|Δd|, Σ|Δh|, Σ|Δw|]; slots
+ *          of terms not requested receive 0 (or are left as they were)
+ * Deterministic (fixed-order reduction through the workspace, at least
+ * tv_loss_3d_workspace_bytes() bytes). */
+#define QC_TV_TERM_SQ 1
+#define QC_TV_TERM_ISO 2
+#define QC_TV_TERM_L1 4
+int tv_loss_mix_3d_fwd_grad_cuda(int terms, int flags, const float *d_vol, const float *d_g,
+                                 float *d_acc, float *d_grad_vol, int B, int D, int H, int W,
+                                 float eps, float iso_scale, void *d_workspace,
+                                 size_t workspace_bytes, cudaStream_t stream);
+
 /* tv_loss_iso_3d_fwd_grad_cuda without a workspace, for callers that cannot
  * call cudaMalloc where they compute the loss: applications whose device
  * memory is owned up front by one allocator or a fixed budget, and hosts that

@@ -196,6 +196,26 @@ PYBIND11_MODULE(_core, m) {
         py::arg("eps"), py::arg("acc_scale"), py::arg("ws_ptr"), py::arg("ws_bytes"),
         py::arg("stream_ptr"));
 
+    m.def(
+        "tv_loss_mix_3d_fwd_grad_cuda",
+        [](int terms, int flags, uintptr_t vol, uintptr_t g, uintptr_t acc, uintptr_t grad, int B,
+           int D, int H, int W, float eps, float iso_scale, uintptr_t ws, size_t ws_bytes,
+           uintptr_t stream) {
+            check(tv_loss_mix_3d_fwd_grad_cuda(terms, flags, ptr<const float>(vol),
+                                               ptr<const float>(g), ptr<float>(acc),
+                                               ptr<float>(grad), B, D, H, W, eps, iso_scale,
+                                               ptr<void>(ws), ws_bytes, stream_of(stream)));
+        },
+        "Two or three TV terms in one sweep: g = [g_sq, g_iso, g_d, g_h, g_w], acc = [sq, "
+        "iso_scale*iso, l1_d, l1_h, l1_w], grad = the weighted sum of the terms' gradients.",
+        py::arg("terms"), py::arg("flags"), py::arg("vol_ptr"), py::arg("g_ptr"), py::arg("acc_ptr"),
+        py::arg("grad_vol_ptr"), py::arg("B"), py::arg("D"), py::arg("H"), py::arg("W"),
+        py::arg("eps"), py::arg("iso_scale"), py::arg("ws_ptr"), py::arg("ws_bytes"),
+        py::arg("stream_ptr"));
+    m.attr("TV_TERM_SQ") = QC_TV_TERM_SQ;
+    m.attr("TV_TERM_ISO") = QC_TV_TERM_ISO;
+    m.attr("TV_TERM_L1") = QC_TV_TERM_L1;
+
     m.attr("TV_SQ") = QC_TV_SQ;
     m.attr("TV_ISO") = QC_TV_ISO;
     m.attr("TV_L1") = QC_TV_L1;

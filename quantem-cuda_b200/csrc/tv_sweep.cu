@@ -67,6 +67,21 @@ constexpr int kMaxPartials = 2048;  // CTA partial-sum slots in the workspace
 constexpr int kMaxDevices = 64;     // per-device host-side caches
 constexpr int kAccSlots = 3;        // L1 keeps one sum per axis
 
+// Several terms of one volume in one sweep ("mixed" variants, V = kMix |
+// mask): mask bit 0 the squared term, bit 1 the isotropic term, bit 2 the L1
+// term. The gradient is linear in the terms' fluxes, so one divergence of the
+// gain-weighted sum of fluxes gives the summed gradient; the loss slots are
+// [Σ sq, Σ iso, Σ|Δd|, Σ|Δh|, Σ|Δw|].
+constexpr int kMix = 8;
+constexpr int kMixSlots = 5;
+constexpr int kMaxSlots = kMixSlots;
+__host__ __device__ constexpr bool is_mix(int V) { return V >= kMix; }
+__host__ __device__ constexpr bool has_sq(int V) { return V == QC_TV_SQ || (V >= kMix && (V & 1)); }
+__host__ __device__ constexpr bool has_iso(int V) { return V == QC_TV_ISO || (V >= kMix && (V & 2)); }
+__host__ __device__ constexpr bool has_l1(int V) { return V == QC_TV_L1 || (V >= kMix && (V & 4)); }
+// loss slots a CTA writes (the workspace stride of its partial sums)
+__host__ __device__ constexpr int slots_of(int V) { return V >= kMix ? kMixSlots : kAccSlots; }
+
 // ── per-variant arithmetic ───────────────────────────────────────────────
 
 __device__ __forceinline__ float sqrt_approx(float x) {
@@ -96,6 +111,7 @@ __device__ __forceinline__ float gsign(float g, float x) {
 struct Gains {
     float gmul;        // multiplies the divergence
     float gd, gh, gw;  // L1 per-axis gains folded into F
+    float gsq2, giso;  // mixed variants: 2·g of the squared term, g of the isotropic term
 };
 
 // Loss terms and flux at a voxel with value v and +1 neighbours (nd, nh, nw);
@@ -103,12 +119,50 @@ struct Gains {
 template <int V, bool LOSS, bool GRAD>
 __device__ __forceinline__ void voxel_flux(float v, float nd, float nh, float nw, bool vd, bool vh,
                                            bool vw, bool own, float eps, const Gains &gn,
-                                           float &Fd, float &Fh, float &Fw, float &l0, float &l1,
-                                           float &l2) {
+                                           float &Fd, float &Fh, float &Fw, float *l) {
+    float &l0 = l[0], &l1 = l[1], &l2 = l[2];
     const float dd = vd ? nd - v : 0.f;
     const float dh = vh ? nh - v : 0.f;
     const float dw = vw ? nw - v : 0.f;
-    if constexpr (V == QC_TV_SQ) {
+    if constexpr (is_mix(V)) {
+        float fd = 0.f, fh = 0.f, fw = 0.f;
+        if constexpr (has_sq(V)) {
+            if (LOSS && own) l[0] += __fmaf_rn(dw, dw, __fmaf_rn(dh, dh, dd * dd));
+            if (GRAD) {
+                fd = gn.gsq2 * dd;
+                fh = gn.gsq2 * dh;
+                fw = gn.gsq2 * dw;
+            }
+        }
+        if constexpr (has_iso(V)) {
+            const bool ok = vd && vh && vw;
+            const float x = iso_x(dd, dh, dw, eps);
+            if (LOSS) l[1] += (ok && own) ? sqrt_approx(x) : 0.f;
+            if (GRAD) {
+                const float inv = ok ? gn.giso * rsqrt_approx(x) : 0.f;
+                fd = __fmaf_rn(dd, inv, fd);
+                fh = __fmaf_rn(dh, inv, fh);
+                fw = __fmaf_rn(dw, inv, fw);
+            }
+        }
+        if constexpr (has_l1(V)) {
+            if (LOSS && own) {
+                l[2] += fabsf(dd);
+                l[3] += fabsf(dh);
+                l[4] += fabsf(dw);
+            }
+            if (GRAD) {
+                fd += gsign(gn.gd, dd);
+                fh += gsign(gn.gh, dh);
+                fw += gsign(gn.gw, dw);
+            }
+        }
+        if (GRAD) {
+            Fd = fd;
+            Fh = fh;
+            Fw = fw;
+        }
+    } else if constexpr (V == QC_TV_SQ) {
         if (LOSS) {
             const float s = __fmaf_rn(dw, dw, __fmaf_rn(dh, dh, dd * dd));
             l0 += own ? s : 0.f;
@@ -149,7 +203,18 @@ __device__ __forceinline__ float flux_from_up(float v, float up, float up_nd, fl
                                               bool has_up, bool vd, bool vw_up, float eps,
                                               const Gains &gn) {
     const float dh = has_up ? v - up : 0.f;
-    if constexpr (V == QC_TV_SQ) {
+    if constexpr (is_mix(V)) {
+        float f = 0.f;
+        if constexpr (has_sq(V)) f = gn.gsq2 * dh;
+        if constexpr (has_iso(V)) {
+            const bool ok = has_up && vd && vw_up;
+            const float dd = up_nd - up, dw = up_nw - up;
+            const float inv = ok ? gn.giso * rsqrt_approx(iso_x(dd, dh, dw, eps)) : 0.f;
+            f = __fmaf_rn(dh, inv, f);
+        }
+        if constexpr (has_l1(V)) f += gsign(gn.gh, dh);
+        return f;
+    } else if constexpr (V == QC_TV_SQ) {
         return dh;
     } else if constexpr (V == QC_TV_L1) {
         return gsign(gn.gh, dh);
@@ -168,7 +233,18 @@ __device__ __forceinline__ float flux_from_left(float v, float lf, float lf_nd, 
                                                 bool has_left, bool vd, bool vh, float eps,
                                                 const Gains &gn) {
     const float dw = has_left ? v - lf : 0.f;
-    if constexpr (V == QC_TV_SQ) {
+    if constexpr (is_mix(V)) {
+        float f = 0.f;
+        if constexpr (has_sq(V)) f = gn.gsq2 * dw;
+        if constexpr (has_iso(V)) {
+            const bool ok = has_left && vd && vh;
+            const float dd = lf_nd - lf, dh = lf_nh - lf;
+            const float inv = ok ? gn.giso * rsqrt_approx(iso_x(dd, dh, dw, eps)) : 0.f;
+            f = __fmaf_rn(dw, inv, f);
+        }
+        if constexpr (has_l1(V)) f += gsign(gn.gw, dw);
+        return f;
+    } else if constexpr (V == QC_TV_SQ) {
         return dw;
     } else if constexpr (V == QC_TV_L1) {
         return gsign(gn.gw, dw);
@@ -182,9 +258,16 @@ __device__ __forceinline__ float flux_from_left(float v, float lf, float lf_nd, 
 
 template <int V>
 __device__ __forceinline__ Gains load_gains(const float *g, float scale) {
-    Gains gn{1.f, 0.f, 0.f, 0.f};
+    Gains gn{1.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (g == nullptr) return gn;
-    if constexpr (V == QC_TV_SQ) {
+    if constexpr (is_mix(V)) {
+        // g = [g_sq, g_iso, g_d, g_h, g_w]; the divergence gain stays 1
+        gn.gsq2 = 2.0f * (__ldg(g) * scale);
+        gn.giso = __ldg(g + 1) * scale;
+        gn.gd = __ldg(g + 2) * scale;
+        gn.gh = __ldg(g + 3) * scale;
+        gn.gw = __ldg(g + 4) * scale;
+    } else if constexpr (V == QC_TV_SQ) {
         gn.gmul = 2.0f * (__ldg(g) * scale);
     } else if constexpr (V == QC_TV_ISO) {
         gn.gmul = __ldg(g) * scale;
@@ -213,7 +296,7 @@ struct Plan {
                              // atomics instead of writing a workspace partial
 };
 
-// A CTA's sum of loss slot `slot` (threadIdx.x < kAccSlots): into the
+// A CTA's sum of loss slot `slot` (threadIdx.x < slots_of(V)): into the
 // workspace for the fixed-order finalize, or (reference-signature entries,
 // which have no workspace) added to the caller's accumulator atomically, as
 // the reference's loss kernels do (tv_loss.cu:95, :273, :404-408).
@@ -222,7 +305,7 @@ __device__ __forceinline__ void store_cta_sum(const Plan &pl, double *partials, 
     if (pl.acc_atomic != nullptr) {
         if (slot < (V == QC_TV_L1 ? 3 : 1)) atomicAdd(pl.acc_atomic + slot, (float)(t * (double)pl.scale));
     } else {
-        partials[(size_t)blockIdx.x * kAccSlots + slot] = t;
+        partials[(size_t)blockIdx.x * slots_of(V) + slot] = t;
     }
 }
 
@@ -397,7 +480,7 @@ struct SweepSmem {
     float stage[G::S][G::StageFloats];
     uint64_t full[G::S];
     uint64_t empty[G::S];
-    double red[G::NW][kAccSlots];
+    double red[G::NW][kMaxSlots];
     int abort;
     int xgo;
 };
@@ -484,13 +567,83 @@ __device__ __forceinline__ void row_flux_pairs(const ulonglong2 &c, const ulongl
                                                const ulonglong2 &dn, float right, f2 eps01,
                                                f2 eps23, bool s3_ok, const Gains &gn,
                                                ulonglong2 &Fd, ulonglong2 &Fh, ulonglong2 &Fw,
-                                               f2 &acc01, f2 &acc23, float &r0, float &r1,
-                                               float &r2) {
+                                               f2 &acc01, f2 &acc23, f2 &bcc01, f2 &bcc23,
+                                               float &r0, float &r1, float &r2) {
     const f2 dd01 = sub2(n.x, c.x), dd23 = sub2(n.y, c.y);
     const f2 dh01 = sub2(dn.x, c.x), dh23 = sub2(dn.y, c.y);
     const f2 w01 = pk2(hi2(c.x), lo2(c.y)), w23 = pk2(hi2(c.y), right);
     const f2 dw01 = sub2(w01, c.x), dw23 = sub2(w23, c.y);
-    if constexpr (V == QC_TV_SQ) {
+    if constexpr (is_mix(V)) {
+        // squared loss pairs in acc, isotropic loss pairs in bcc, L1 sums in
+        // r0..r2; the flux is the gain-weighted sum of the terms' fluxes
+        f2 fd01 = 0ull, fd23 = 0ull, fh01 = 0ull, fh23 = 0ull, fw01 = 0ull, fw23 = 0ull;
+        if constexpr (has_sq(V)) {
+            if (LOSS) {
+                acc01 = fma2(dd01, dd01, acc01);
+                acc01 = fma2(dh01, dh01, acc01);
+                acc01 = fma2(dw01, dw01, acc01);
+                acc23 = fma2(dd23, dd23, acc23);
+                acc23 = fma2(dh23, dh23, acc23);
+                acc23 = fma2(dw23, dw23, acc23);
+            }
+            if (GRAD) {
+                const f2 g2 = pk2(gn.gsq2, gn.gsq2);
+                fd01 = mul2(dd01, g2);
+                fd23 = mul2(dd23, g2);
+                fh01 = mul2(dh01, g2);
+                fh23 = mul2(dh23, g2);
+                fw01 = mul2(dw01, g2);
+                fw23 = mul2(dw23, g2);
+            }
+        }
+        if constexpr (has_iso(V)) {
+            const f2 x01 = fma2(dw01, dw01, fma2(dh01, dh01, fma2(dd01, dd01, eps01)));
+            const f2 x23 = fma2(dw23, dw23, fma2(dh23, dh23, fma2(dd23, dd23, eps23)));
+            const f2 r01 = pk2(rsqrt_approx(lo2(x01)), rsqrt_approx(hi2(x01)));
+            const f2 r23 = pk2(rsqrt_approx(lo2(x23)), rsqrt_approx(hi2(x23)));
+            if (LOSS) {
+                const f2 s01 = mul2(x01, r01), s23 = mul2(x23, r23);
+                bcc01 = add2(bcc01, s01);
+                bcc23 = add2(bcc23, s3_ok ? s23 : pk2(lo2(s23), 0.f));
+            }
+            if (GRAD) {
+                const f2 gi = pk2(gn.giso, gn.giso);
+                const f2 q01 = mul2(r01, gi), q23 = mul2(r23, gi);
+                fd01 = fma2(dd01, q01, fd01);
+                fd23 = fma2(dd23, q23, fd23);
+                fh01 = fma2(dh01, q01, fh01);
+                fh23 = fma2(dh23, q23, fh23);
+                fw01 = fma2(dw01, q01, fw01);
+                fw23 = fma2(dw23, q23, fw23);
+            }
+        }
+        if constexpr (has_l1(V)) {
+            const float dd[4] = {lo2(dd01), hi2(dd01), lo2(dd23), hi2(dd23)};
+            const float dh[4] = {lo2(dh01), hi2(dh01), lo2(dh23), hi2(dh23)};
+            const float dw[4] = {lo2(dw01), hi2(dw01), lo2(dw23), hi2(dw23)};
+            if (LOSS) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    r0 += fabsf(dd[j]);
+                    r1 += fabsf(dh[j]);
+                    r2 += fabsf(dw[j]);
+                }
+            }
+            if (GRAD) {
+                fd01 = add2(fd01, pk2(gsign_fast(gn.gd, dd[0]), gsign_fast(gn.gd, dd[1])));
+                fd23 = add2(fd23, pk2(gsign_fast(gn.gd, dd[2]), gsign_fast(gn.gd, dd[3])));
+                fh01 = add2(fh01, pk2(gsign_fast(gn.gh, dh[0]), gsign_fast(gn.gh, dh[1])));
+                fh23 = add2(fh23, pk2(gsign_fast(gn.gh, dh[2]), gsign_fast(gn.gh, dh[3])));
+                fw01 = add2(fw01, pk2(gsign_fast(gn.gw, dw[0]), gsign_fast(gn.gw, dw[1])));
+                fw23 = add2(fw23, pk2(gsign_fast(gn.gw, dw[2]), gsign_fast(gn.gw, dw[3])));
+            }
+        }
+        if (GRAD) {
+            Fd = make_ulonglong2(fd01, fd23);
+            Fh = make_ulonglong2(fh01, fh23);
+            Fw = make_ulonglong2(fw01, fw23);
+        }
+    } else if constexpr (V == QC_TV_SQ) {
         if (LOSS) {
             acc01 = fma2(dd01, dd01, acc01);
             acc01 = fma2(dh01, dh01, acc01);
@@ -558,10 +711,34 @@ __device__ __forceinline__ void row_flux4(const float4 &c, const float4 &n, cons
     const float nv[4] = {n.x, n.y, n.z, n.w};
     const float hv[4] = {dn.x, dn.y, dn.z, dn.w};
     const float wv[4] = {c.y, c.z, c.w, right};
+    static_assert(!(is_mix(V) && LOSS), "row_flux4 gives the mixed variants' flux only");
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const float dd = nv[j] - cv[j], dh = hv[j] - cv[j], dw = wv[j] - cv[j];
-        if constexpr (V == QC_TV_SQ) {
+        if constexpr (is_mix(V)) {
+            if (GRAD) {
+                float fd = 0.f, fh = 0.f, fw = 0.f;
+                if constexpr (has_sq(V)) {
+                    fd = gn.gsq2 * dd;
+                    fh = gn.gsq2 * dh;
+                    fw = gn.gsq2 * dw;
+                }
+                if constexpr (has_iso(V)) {
+                    const float r = gn.giso * rsqrt_approx(iso_x(dd, dh, dw, j == 3 ? eps3 : eps_row));
+                    fd = __fmaf_rn(dd, r, fd);
+                    fh = __fmaf_rn(dh, r, fh);
+                    fw = __fmaf_rn(dw, r, fw);
+                }
+                if constexpr (has_l1(V)) {
+                    fd += gsign_fast(gn.gd, dd);
+                    fh += gsign_fast(gn.gh, dh);
+                    fw += gsign_fast(gn.gw, dw);
+                }
+                Fd[j] = fd;
+                Fh[j] = fh;
+                Fw[j] = fw;
+            }
+        } else if constexpr (V == QC_TV_SQ) {
             if (LOSS) r0 = __fmaf_rn(dw, dw, __fmaf_rn(dh, dh, __fmaf_rn(dd, dd, r0)));
             if (GRAD) {
                 Fd[j] = dd;
@@ -619,7 +796,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
     __syncthreads();
     if (xc.seq != 0) halo_push_prologue(xc, pl.B, pl.Dp, (long long)pl.H * pl.W, &sm.xgo);
 
-    double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0;
+    double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0, acc4 = 0.0;
 
     if (warp == NW) {
         // ── producer warp: one lane issues every TMA load ──
@@ -752,7 +929,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                         const float lf = lds1(Sc, hrow + 1, kHaloW - 1);
                         const float v0 = lds1(Sc, hrow + 1, kHaloW);
                         float lf_nd = 0.f, lf_nh = 0.f;
-                        if (V == QC_TV_ISO) {
+                        if (has_iso(V)) {
                             lf_nd = lds1(Sn, hrow + 1, kHaloW - 1);
                             lf_nh = lds1(Sc, hrow + 2, kHaloW - 1);
                         }
@@ -765,7 +942,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                     float Fh_up[4] = {0.f, 0.f, 0.f, 0.f};
                     if (GRAD) {
                         const float4 up = has_up ? lds4(Sc, r0, scol) : cur;
-                        if constexpr (V == QC_TV_ISO) {
+                        if constexpr (V == QC_TV_ISO || is_mix(V)) {
                             const float4 up_nd = has_nxt ? lds4(Sn, r0, scol) : up;
                             float up_right = __shfl_down_sync(0xffffffffu, up.x, 1);
                             if (lane == 31) up_right = lds1(Sc, r0, scol + 4);
@@ -790,6 +967,7 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
 
                     float *gp = gbase + (size_t)p * plane_elems;
                     f2 la01 = 0ull, la23 = 0ull;  // paired loss sums of this plane (+0.0f pairs)
+                    f2 lb01 = 0ull, lb23 = 0ull;  // mixed variants: the isotropic term's pairs
                     f2 up01 = pk2(Fh_up[0], Fh_up[1]), up23 = pk2(Fh_up[2], Fh_up[3]);
                     // The strip's rows, specialised on whether every row has its
                     // +H neighbour (all strips but the one holding row H-1): then
@@ -818,11 +996,22 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                             f2 e01 = e01_full, e23 = e23_full;
                             if (!FULL && !row_ok) e01 = e23 = pk2(kInf, kInf);
                             ulonglong2 Fd, Fh, Fw;
-                            f2 q01 = 0ull, q23 = 0ull;
+                            f2 q01 = 0ull, q23 = 0ull, b01 = 0ull, b23 = 0ull;
                             row_flux_pairs<V, LOSS, GRAD>(curp, nxt, dn, right, e01, e23, !last_quad, gn,
-                                                          Fd, Fh, Fw, q01, q23, l0, l1, l2);
+                                                          Fd, Fh, Fw, q01, q23, b01, b23, l0, l1, l2);
                             if (LOSS) {
-                                if constexpr (V == QC_TV_ISO) {
+                                if constexpr (is_mix(V)) {
+                                    if constexpr (has_sq(V)) {
+                                        la01 = add2(la01, q01);
+                                        la23 = add2(la23, q23);
+                                    }
+                                    if constexpr (has_iso(V)) {
+                                        if (loss_lane && row_ok) {
+                                            lb01 = add2(lb01, b01);
+                                            lb23 = add2(lb23, b23);
+                                        }
+                                    }
+                                } else if constexpr (V == QC_TV_ISO) {
                                     if (loss_lane && row_ok) {
                                         la01 = add2(la01, q01);
                                         la23 = add2(la23, q23);
@@ -866,13 +1055,31 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                         rows(std::true_type{});
                     else
                         rows(std::false_type{});
-                    if (LOSS) l0 += (lo2(la01) + hi2(la01)) + (lo2(la23) + hi2(la23));
+                    if (LOSS) {
+                        if constexpr (is_mix(V)) {
+                            // slots: sq, iso, then the L1 axes (l0..l2)
+                            if constexpr (has_sq(V))
+                                acc0 += (double)((lo2(la01) + hi2(la01)) + (lo2(la23) + hi2(la23)));
+                            if constexpr (has_iso(V))
+                                acc1 += (double)((lo2(lb01) + hi2(lb01)) + (lo2(lb23) + hi2(lb23)));
+                        } else {
+                            l0 += (lo2(la01) + hi2(la01)) + (lo2(la23) + hi2(la23));
+                        }
+                    }
                 }
                 if (LOSS) {
-                    acc0 += (double)l0;
-                    if (V == QC_TV_L1) {
-                        acc1 += (double)l1;
-                        acc2 += (double)l2;
+                    if constexpr (is_mix(V)) {
+                        if constexpr (has_l1(V)) {
+                            acc2 += (double)l0;
+                            acc3 += (double)l1;
+                            acc4 += (double)l2;
+                        }
+                    } else {
+                        acc0 += (double)l0;
+                        if (V == QC_TV_L1) {
+                            acc1 += (double)l1;
+                            acc2 += (double)l2;
+                        }
                     }
                 }
                 // Release plane p's stage.
@@ -899,15 +1106,23 @@ __global__ void __launch_bounds__(G::Threads, G::MinB) tv_sweep_tma_kernel(
                 acc0 += __shfl_xor_sync(0xffffffffu, acc0, off);
                 acc1 += __shfl_xor_sync(0xffffffffu, acc1, off);
                 acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
+                if constexpr (is_mix(V)) {
+                    acc3 += __shfl_xor_sync(0xffffffffu, acc3, off);
+                    acc4 += __shfl_xor_sync(0xffffffffu, acc4, off);
+                }
             }
             if (lane == 0) {
                 sm.red[warp][0] = acc0;
                 sm.red[warp][1] = acc1;
                 sm.red[warp][2] = acc2;
+                if constexpr (is_mix(V)) {
+                    sm.red[warp][3] = acc3;
+                    sm.red[warp][4] = acc4;
+                }
             }
         }
         __syncthreads();
-        if (threadIdx.x < kAccSlots) {
+        if (threadIdx.x < slots_of(V)) {
             double t = 0.0;
             for (int w = 0; w < NW; ++w) t += sm.red[w][threadIdx.x];
             store_cta_sum<V>(pl, partials, threadIdx.x, t);
@@ -927,7 +1142,7 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
     const Gains gn = load_gains<V>(g, pl.scale);
     const int tx = threadIdx.x % kGenTileW, ty = threadIdx.x / kGenTileW;
     const size_t plane = (size_t)pl.H * pl.W;
-    double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0;
+    double acc[kMaxSlots] = {0.0, 0.0, 0.0, 0.0, 0.0};
 
     for (long long u = blockIdx.x; u < pl.n_units; u += gridDim.x) {
         const Unit U = decode_unit<GRAD>(pl, u, kGenTileH, kGenTileW);
@@ -945,7 +1160,7 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
         for (int p = U.first; p < U.d_end; ++p) {
             const bool has_nxt = (p + 1) <= U.last;
             const bool owned = p >= U.d_start;
-            float l0 = 0.f, l1 = 0.f, l2 = 0.f;
+            float l[kMaxSlots] = {0.f, 0.f, 0.f, 0.f, 0.f};
             float Fd = 0.f, Fh = 0.f, Fw = 0.f;
             if (in) {
                 const float v = at(p, h, w);
@@ -953,19 +1168,19 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
                 const float nh = vh ? at(p, h + 1, w) : 0.f;
                 const float nw = vw ? at(p, h, w + 1) : 0.f;
                 voxel_flux<V, LOSS, GRAD>(v, nd, nh, nw, has_nxt, vh, vw, owned, pl.eps, gn, Fd,
-                                          Fh, Fw, l0, l1, l2);
+                                          Fh, Fw, l);
                 if (GRAD && owned) {
                     float Fh_up = 0.f, Fw_left = 0.f;
                     if (h >= 1) {
                         const float up = at(p, h - 1, w);
-                        const float up_nd = (V == QC_TV_ISO && has_nxt) ? at(p + 1, h - 1, w) : 0.f;
-                        const float up_nw = (V == QC_TV_ISO && vw) ? at(p, h - 1, w + 1) : 0.f;
+                        const float up_nd = (has_iso(V) && has_nxt) ? at(p + 1, h - 1, w) : 0.f;
+                        const float up_nw = (has_iso(V) && vw) ? at(p, h - 1, w + 1) : 0.f;
                         Fh_up = flux_from_up<V>(v, up, up_nd, up_nw, true, has_nxt, vw, pl.eps, gn);
                     }
                     if (w >= 1) {
                         const float lf = at(p, h, w - 1);
-                        const float lf_nd = (V == QC_TV_ISO && has_nxt) ? at(p + 1, h, w - 1) : 0.f;
-                        const float lf_nh = (V == QC_TV_ISO && vh) ? at(p, h + 1, w - 1) : 0.f;
+                        const float lf_nd = (has_iso(V) && has_nxt) ? at(p + 1, h, w - 1) : 0.f;
+                        const float lf_nh = (has_iso(V) && vh) ? at(p, h + 1, w - 1) : 0.f;
                         Fw_left = flux_from_left<V>(v, lf, lf_nd, lf_nh, true, has_nxt, vh, pl.eps, gn);
                     }
                     const float gv =
@@ -977,9 +1192,8 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
             }
             Fd_prev = Fd;
             if (LOSS) {
-                acc0 += (double)l0;
-                acc1 += (double)l1;
-                acc2 += (double)l2;
+#pragma unroll
+                for (int a = 0; a < slots_of(V); ++a) acc[a] += (double)l[a];
             }
         }
     }
@@ -987,21 +1201,16 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
     griddep_launch_dependents();
 
     if (LOSS) {
-        __shared__ double red[kGenThreads / 32][kAccSlots];
+        __shared__ double red[kGenThreads / 32][kMaxSlots];
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            acc0 += __shfl_xor_sync(0xffffffffu, acc0, off);
-            acc1 += __shfl_xor_sync(0xffffffffu, acc1, off);
-            acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
-        }
-        if (lane == 0) {
-            red[warp][0] = acc0;
-            red[warp][1] = acc1;
-            red[warp][2] = acc2;
+        for (int a = 0; a < slots_of(V); ++a) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) acc[a] += __shfl_xor_sync(0xffffffffu, acc[a], off);
+            if (lane == 0) red[warp][a] = acc[a];
         }
         __syncthreads();
-        if (threadIdx.x < kAccSlots) {
+        if (threadIdx.x < slots_of(V)) {
             double t = 0.0;
             for (int w = 0; w < kGenThreads / 32; ++w) t += red[w][threadIdx.x];
             store_cta_sum<V>(pl, partials, threadIdx.x, t);
@@ -1013,16 +1222,25 @@ __global__ void __launch_bounds__(kGenThreads) tv_sweep_generic_kernel(
 
 constexpr int kFinThreads = 256;
 
+// Per-slot multipliers of the finalized sums (the isotropic mean's 1/N).
+struct FinScales {
+    float s[kMaxSlots];
+};
+
 __global__ void __launch_bounds__(kFinThreads) tv_finalize_kernel(const double *__restrict__ partials,
                                                                   int n_partials, int n_acc,
+                                                                  int stride,
                                                                   float *__restrict__ acc,
-                                                                  float scale, int overwrite) {
+                                                                  const FinScales scales,
+                                                                  int overwrite) {
     griddep_wait();  // the sweep grid has completed and its writes are visible
-    __shared__ double red[kAccSlots][kFinThreads];
+    __shared__ double red[kMaxSlots][kFinThreads];
+    // CTA i's sums start at partials[i * stride] (stride: the sweep's slot
+    // count, 3 for a single term, 5 for a mixed sweep)
     for (int a = 0; a < n_acc; ++a) {
         double t = 0.0;
         for (int i = threadIdx.x; i < n_partials; i += kFinThreads)
-            t += partials[(size_t)i * kAccSlots + a];
+            t += partials[(size_t)i * stride + a];
         red[a][threadIdx.x] = t;
     }
     __syncthreads();
@@ -1032,7 +1250,7 @@ __global__ void __launch_bounds__(kFinThreads) tv_finalize_kernel(const double *
         __syncthreads();
     }
     if (threadIdx.x < n_acc) {
-        const float v = (float)(red[threadIdx.x][0] * (double)scale);
+        const float v = (float)(red[threadIdx.x][0] * (double)scales.s[threadIdx.x]);
         acc[threadIdx.x] = overwrite ? v : acc[threadIdx.x] + v;
     }
 }
@@ -1191,6 +1409,18 @@ struct FastGeomFor<QC_TV_L1> {
     using type = Geom<4, 4, 4, 4>;
 };
 #endif
+// Mixed sweeps carry several terms' fluxes and loss sums per voxel: 16-row
+// tiles with the register budget of 3 CTAs per SM.
+// QC_TV_MIX_R, QC_TV_MIX_NW, QC_TV_MIX_S and QC_TV_MIX_MINB override it at
+// build time.
+template <int V>
+struct MixGeom {
+#ifdef QC_TV_MIX_R
+    using type = Geom<QC_TV_MIX_R, QC_TV_MIX_NW, QC_TV_MIX_S, QC_TV_MIX_MINB>;
+#else
+    using type = Geom<4, 4, 4, 3>;
+#endif
+};
 
 template <int V, bool LOSS, bool GRAD>
 int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, double *partials,
@@ -1198,7 +1428,8 @@ int launch_variant(bool use_tma, const float *vol, const float *g, float *grad, 
     int sms = 0;
     if (int st = device_sm_count(&sms)) return st;
     if (use_tma) {
-        using G = typename FastGeomFor<V>::type;
+        using G = typename std::conditional<is_mix(V), typename MixGeom<V>::type,
+                                            typename FastGeomFor<V>::type>::type;
         EncodeTiledFn encode = nullptr;
         if (int st = get_encode_fn(&encode)) return st;
         // The tensor map is encoded through the driver API, which needs a
@@ -1288,7 +1519,17 @@ int dispatch_mode(int flags, bool use_tma, const float *vol, const float *g, flo
 int launch_halo_exchange(const qc_tv_peers *peers, unsigned long long seq, float *d_slab, int B,
                          int Dp, int H, int W, cudaStream_t stream);
 
-size_t workspace_bytes() { return (size_t)kMaxPartials * kAccSlots * sizeof(double); }
+// Scratch of the deterministic reduction: one slot row per CTA partial.
+size_t workspace_bytes_for(int variant) {
+    return (size_t)kMaxPartials * slots_of(variant) * sizeof(double);
+}
+size_t workspace_bytes() { return (size_t)kMaxPartials * kMaxSlots * sizeof(double); }
+
+// Mixed-term variants with a compiled sweep: sq+iso, sq+L1, iso+L1, all three.
+bool mix_supported(int variant) {
+    return variant == (kMix | 3) || variant == (kMix | 5) || variant == (kMix | 6) ||
+           variant == (kMix | 7);
+}
 
 int run(int variant, int flags, const float *vol, const float *g, float *acc, float *grad, int B,
         int Dp, int H, int W, int d_lo, int d_hi, int has_prev, int has_next, float eps,
@@ -1296,14 +1537,22 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
         const qc_tv_peers *peers = nullptr, unsigned long long seq = 0,
         unsigned long long halo_seq = 0, int *n_partials_out = nullptr,
         bool atomic_acc = false) {
-    QC_NVTX(variant == QC_TV_SQ ? "quantem::tv_sq" : variant == QC_TV_ISO ? "quantem::tv_iso" : "quantem::tv_l1");
+    QC_NVTX(variant == QC_TV_SQ    ? "quantem::tv_sq"
+            : variant == QC_TV_ISO ? "quantem::tv_iso"
+            : variant == QC_TV_L1  ? "quantem::tv_l1"
+                                   : "quantem::tv_mix");
     // n_partials_out != nullptr: launch the sweep only (its CTA partials stay
     // in ws, *n_partials_out of them) for a later tv_loss_3d_peer_finalize_cuda.
     const bool sweep_only = n_partials_out != nullptr;
     if (sweep_only) *n_partials_out = 0;
     const bool want_loss = flags & QC_TV_LOSS, want_grad = flags & QC_TV_GRAD;
-    QC_RETURN_IF(variant < QC_TV_SQ || variant > QC_TV_L1, QC_ERR_INVALID_ARGUMENT,
-                 "tv: unknown variant %d", variant);
+    const bool mixed = is_mix(variant);
+    QC_RETURN_IF((variant < QC_TV_SQ || variant > QC_TV_L1) && !mix_supported(variant),
+                 QC_ERR_INVALID_ARGUMENT, "tv: unknown variant %d", variant);
+    QC_RETURN_IF(mixed && (flags & (QC_TV_LOSS | QC_TV_GRAD)) != (QC_TV_LOSS | QC_TV_GRAD),
+                 QC_ERR_INVALID_ARGUMENT, "tv: a mixed sweep computes losses and gradient together");
+    QC_RETURN_IF(mixed && (peers != nullptr || n_partials_out != nullptr || atomic_acc),
+                 QC_ERR_INVALID_ARGUMENT, "tv: mixed sweeps are single-GPU, deterministic-workspace only");
     QC_RETURN_IF(!want_loss && !want_grad, QC_ERR_INVALID_ARGUMENT,
                  "tv: flags must request QC_TV_LOSS and/or QC_TV_GRAD");
     QC_RETURN_IF(B < 0 || Dp < 0 || H < 0 || W < 0, QC_ERR_INVALID_ARGUMENT,
@@ -1316,7 +1565,7 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
                  "tv: has_next needs a halo plane at d_hi");
     QC_RETURN_IF((long long)H * W >= (1LL << 31), QC_ERR_INVALID_ARGUMENT,
                  "tv: H*W must be < 2^31");
-    const int n_acc = variant == QC_TV_L1 ? 3 : 1;
+    const int n_acc = mixed ? kMixSlots : (variant == QC_TV_L1 ? 3 : 1);
     const bool empty = B == 0 || H == 0 || W == 0 || d_hi == d_lo;
     QC_RETURN_IF(atomic_acc && (peers != nullptr || sweep_only || (flags & QC_TV_ACC_OVERWRITE)),
                  QC_ERR_INVALID_ARGUMENT, "tv: atomic accumulation is for single-GPU acc += calls");
@@ -1324,9 +1573,10 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
         QC_RETURN_IF(acc == nullptr, QC_ERR_INVALID_ARGUMENT, "tv: null acc");
     }
     if (want_loss && !atomic_acc) {
-        QC_RETURN_IF(ws == nullptr || ws_bytes < workspace_bytes(), QC_ERR_WORKSPACE_TOO_SMALL,
+        QC_RETURN_IF(ws == nullptr || ws_bytes < workspace_bytes_for(variant),
+                     QC_ERR_WORKSPACE_TOO_SMALL,
                      "tv: workspace of %zu bytes is below the %zu required", ws_bytes,
-                     workspace_bytes());
+                     workspace_bytes_for(variant));
     }
     if (want_grad) {
         QC_RETURN_IF(grad == nullptr, QC_ERR_INVALID_ARGUMENT, "tv: null grad");
@@ -1350,7 +1600,9 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     pl.has_prev = has_prev ? 1 : 0;
     pl.has_next = has_next ? 1 : 0;
     pl.eps = eps;
-    pl.scale = acc_scale;
+    // a mixed sweep takes every gain from d_g; acc_scale multiplies its
+    // isotropic sum only (slot 1)
+    pl.scale = mixed ? 1.0f : acc_scale;
     pl.acc_atomic = (atomic_acc && want_loss) ? acc : nullptr;
 
     const bool aligned = (reinterpret_cast<uintptr_t>(vol) % 16 == 0) &&
@@ -1385,7 +1637,11 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     } else switch (variant) {
         case QC_TV_SQ: st = dispatch_mode<QC_TV_SQ>(flags, use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
         case QC_TV_ISO: st = dispatch_mode<QC_TV_ISO>(flags, use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
-        default: st = dispatch_mode<QC_TV_L1>(flags, use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
+        case QC_TV_L1: st = dispatch_mode<QC_TV_L1>(flags, use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
+        case kMix | 3: st = launch_variant<kMix | 3, true, true>(use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
+        case kMix | 5: st = launch_variant<kMix | 5, true, true>(use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
+        case kMix | 6: st = launch_variant<kMix | 6, true, true>(use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
+        default: st = launch_variant<kMix | 7, true, true>(use_tma, vol, g, grad, partials, pl, xc, &grid, stream); break;
     }
     if (st) return st;
 
@@ -1412,8 +1668,10 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
             QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_peer_kernel, terms, *peers, seq),
                         "tv_finalize_peer_kernel launch");
         } else {
+            FinScales sc;
+            for (int a = 0; a < kMaxSlots; ++a) sc.s[a] = mixed ? (a == 1 ? acc_scale : 1.0f) : acc_scale;
             QC_CUDA_TRY(cudaLaunchKernelEx(&cfg, tv_finalize_kernel, (const double *)partials, grid,
-                                           n_acc, acc, acc_scale,
+                                           n_acc, slots_of(variant), acc, sc,
                                            (flags & QC_TV_ACC_OVERWRITE) ? 1 : 0),
                         "tv_finalize_kernel launch");
         }
@@ -1516,6 +1774,24 @@ int tv_loss_l1_3d_fwd_grad_cuda(const float *d_vol, const float *d_g, float *d_a
                                 size_t workspace_bytes, cudaStream_t stream) {
     return qc::tv::run(QC_TV_L1, QC_TV_LOSS | QC_TV_GRAD, d_vol, d_g, d_acc, d_grad_vol, B, D, H,
                        W, 0, D, 0, 0, 0.f, 1.0f, d_workspace, workspace_bytes, stream);
+}
+
+int tv_loss_mix_3d_fwd_grad_cuda(int terms, int flags, const float *d_vol, const float *d_g,
+                                 float *d_acc, float *d_grad_vol, int B, int D, int H, int W,
+                                 float eps, float iso_scale, void *d_workspace,
+                                 size_t workspace_bytes, cudaStream_t stream) {
+    QC_RETURN_IF(terms != (QC_TV_TERM_SQ | QC_TV_TERM_ISO) && terms != (QC_TV_TERM_SQ | QC_TV_TERM_L1) &&
+                     terms != (QC_TV_TERM_ISO | QC_TV_TERM_L1) &&
+                     terms != (QC_TV_TERM_SQ | QC_TV_TERM_ISO | QC_TV_TERM_L1),
+                 QC_ERR_INVALID_ARGUMENT,
+                 "tv_loss_mix_3d_fwd_grad_cuda: terms 0x%x must name two or three of "
+                 "QC_TV_TERM_SQ, QC_TV_TERM_ISO, QC_TV_TERM_L1",
+                 (unsigned)terms);
+    QC_RETURN_IF(flags & ~QC_TV_ACC_OVERWRITE, QC_ERR_INVALID_ARGUMENT,
+                 "tv_loss_mix_3d_fwd_grad_cuda: flags may only hold QC_TV_ACC_OVERWRITE");
+    return qc::tv::run(qc::tv::kMix | terms, QC_TV_LOSS | QC_TV_GRAD | flags, d_vol, d_g, d_acc,
+                       d_grad_vol, B, D, H, W, 0, D, 0, 0, eps, iso_scale, d_workspace,
+                       workspace_bytes, stream);
 }
 
 int quantem_cuda_device_fault_word(int device, unsigned int *word, int clear) {

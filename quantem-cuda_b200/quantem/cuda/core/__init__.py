@@ -11,6 +11,7 @@ from quantem.cuda.core._ops import (
     tv_loss_iso_3d_fwd_grad as tv_loss_iso_3d_fwd_grad,
     tv_loss_l1_3d as tv_loss_l1_3d,
     tv_loss_l1_3d_fwd_grad as tv_loss_l1_3d_fwd_grad,
+    tv_loss_multi_3d_fwd_grad as tv_loss_multi_3d_fwd_grad,
     tv_loss_sq_3d as tv_loss_sq_3d,
     tv_loss_sq_3d_fwd_grad as tv_loss_sq_3d_fwd_grad,
     tv_vol_loss as tv_vol_loss,

@@ -264,6 +264,35 @@ def _(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
     return volume.new_empty((3,)), torch.empty_like(volume)
 
 
+# ── several terms in one sweep ────────────────────────────────────────────
+
+_TERM_SQ, _TERM_ISO, _TERM_L1 = _core.TV_TERM_SQ, _core.TV_TERM_ISO, _core.TV_TERM_L1
+
+
+@torch.library.custom_op("quantem_cuda::tv_loss_multi_3d_fwd_grad", mutates_args=())
+def _tv_loss_multi_3d_fwd_grad(volume: Tensor, weights: Tensor, terms: int, eps: float) -> tuple[Tensor, Tensor]:
+    """weights = [w_sq, w_iso, w_d, w_h, w_w]; returns ([sq sum, iso mean, l1_d,
+    l1_h, l1_w], Σ_term w·∂term/∂volume) for the terms in the bit mask."""
+    vol, b, d, h, w, stream = _launch_args(volume)
+    n = float(_iso_n_corners(vol.shape))
+    scale = torch.tensor([1.0, 1.0 / n, 1.0, 1.0, 1.0], dtype=torch.float32, device=vol.device)
+    g = (weights.detach().to(dtype=torch.float32, device=vol.device).reshape(5) * scale).contiguous()
+    acc = torch.empty(5, dtype=torch.float32, device=vol.device)
+    grad_vol = torch.empty_like(vol)
+    ws = _workspace(vol.device)
+    with torch.cuda.device(vol.device):
+        _core.tv_loss_mix_3d_fwd_grad_cuda(
+            int(terms), _OVERWRITE, vol.data_ptr(), g.data_ptr(), acc.data_ptr(), grad_vol.data_ptr(),
+            b, d, h, w, float(eps), 1.0 / n, ws.data_ptr(), ws.numel(), stream,
+        )
+    return acc, grad_vol
+
+
+@_tv_loss_multi_3d_fwd_grad.register_fake
+def _(volume: Tensor, weights: Tensor, terms: int, eps: float) -> tuple[Tensor, Tensor]:
+    return volume.new_empty((5,)), torch.empty_like(volume)
+
+
 # ── public wrappers ───────────────────────────────────────────────────────
 
 
@@ -363,6 +392,70 @@ def tv_loss_l1_3d_fwd_grad(
     g = _upstream(g, 3, vol.device)
     sums, grad = _tv_loss_l1_3d_fwd_grad(vol, g)
     return sums, grad.view(volume.shape)
+
+
+def _weight(x, n: int, device) -> Tensor:
+    if isinstance(x, Tensor):
+        t = x.detach().to(dtype=torch.float32, device=device).reshape(-1)
+        return t.expand(n) if t.numel() == 1 else t.reshape(n)
+    if isinstance(x, (tuple, list)):
+        if len(x) != n:
+            raise ValueError(f"expected {n} weights, got {len(x)}")
+        return torch.tensor([float(v) for v in x], dtype=torch.float32, device=device)
+    return torch.full((n,), float(x), dtype=torch.float32, device=device)
+
+
+def tv_loss_multi_3d_fwd_grad(
+    volume: Tensor,
+    *,
+    sq: Tensor | float | None = None,
+    iso: Tensor | float | None = None,
+    l1: Tensor | float | tuple[float, float, float] | None = None,
+    eps: float = 1e-8,
+) -> tuple[dict[str, Tensor], Tensor]:
+    """Several TV terms of one volume and the gradient of their weighted sum,
+    reading the volume once.
+
+    ``sq`` and ``iso`` weight :func:`tv_loss_sq_3d` and :func:`tv_loss_iso_3d`
+    (the mean over corners, ``eps`` inside the square root); ``l1`` weights
+    the three per-axis sums of :func:`tv_loss_l1_3d` (one value for all axes
+    or three). A term left as ``None`` is not computed. Returns
+    ``(losses, grad)``: ``losses`` maps "sq", "iso", "l1" (for the terms
+    given) to what the single-term ops return, and ``grad`` is
+    ``Σ weight · ∂term/∂volume``. With two or three terms one sweep computes
+    everything (8 B of HBM traffic per voxel instead of 8 B per term); with
+    one term this is that term's single sweep. Not differentiable itself.
+    """
+    vol = _as_batched(volume, "tv_loss_multi_3d_fwd_grad")
+    dev = vol.device
+    terms = (_TERM_SQ if sq is not None else 0) | (_TERM_ISO if iso is not None else 0) | (
+        _TERM_L1 if l1 is not None else 0)
+    if terms == 0:
+        raise ValueError("tv_loss_multi_3d_fwd_grad needs at least one of sq, iso, l1")
+    if terms in (_TERM_SQ, _TERM_ISO, _TERM_L1):
+        if terms == _TERM_SQ:
+            loss, grad = _tv_loss_sq_3d_fwd_grad(vol, _weight(sq, 1, dev))
+            return {"sq": loss}, grad.view(volume.shape)
+        if terms == _TERM_ISO:
+            loss, grad = _tv_loss_iso_3d_fwd_grad(vol, _weight(iso, 1, dev), float(eps))
+            return {"iso": loss}, grad.view(volume.shape)
+        sums, grad = _tv_loss_l1_3d_fwd_grad(vol, _weight(l1, 3, dev))
+        return {"l1": sums}, grad.view(volume.shape)
+    zero1 = torch.zeros(1, dtype=torch.float32, device=dev)
+    weights = torch.cat([
+        _weight(sq, 1, dev) if sq is not None else zero1,
+        _weight(iso, 1, dev) if iso is not None else zero1,
+        _weight(l1, 3, dev) if l1 is not None else zero1.expand(3),
+    ])
+    acc, grad = _tv_loss_multi_3d_fwd_grad(vol, weights, terms, float(eps))
+    losses = {}
+    if sq is not None:
+        losses["sq"] = acc[0]
+    if iso is not None:
+        losses["iso"] = acc[1]
+    if l1 is not None:
+        losses["l1"] = acc[2:5]
+    return losses, grad.view(volume.shape)
 
 
 def ptycho_tv_loss(array: Tensor, weight: tuple[float, float]) -> Tensor:

@@ -78,6 +78,12 @@ def test_argument_errors_need_no_device():
     r.restype = ctypes.c_int
     r.argtypes = [vp, vp, i, i, i, i, vp]
     assert r(vp(16), vp(16), -1, 4, 4, 4, None) == 10001
+    # a mixed sweep needs two or three terms
+    mx = lib.tv_loss_mix_3d_fwd_grad_cuda
+    mx.restype = ctypes.c_int
+    mx.argtypes = [i, i, vp, vp, vp, vp, i, i, i, i, fl, fl, vp, ctypes.c_size_t, vp]
+    assert mx(2, 0, vp(16), vp(16), vp(16), vp(16), 1, 4, 4, 4, 1e-8, 1.0, vp(16), 1 << 20, None) == 10001
+    assert b"two or three" in lib.quantem_cuda_last_error()
     # the allocation-free entry refuses shapes beyond the largest volume before any CUDA call
     na = lib.tv_loss_iso_3d_fwd_grad_noalloc_cuda
     na.restype = ctypes.c_int

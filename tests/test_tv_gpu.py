@@ -23,6 +23,7 @@ if torch.cuda.is_available():
         tv_loss_iso_3d_fwd_grad,
         tv_loss_l1_3d,
         tv_loss_l1_3d_fwd_grad,
+        tv_loss_multi_3d_fwd_grad,
         tv_loss_sq_3d,
         tv_loss_sq_3d_fwd_grad,
     )
@@ -380,6 +381,99 @@ def test_tomography_scale_blob_volume():
     assert rel <= FWD_RTOL, rel
     print(f"iso loss rel err on the blob volume: {rel:.3e} (tolerance {FWD_RTOL:g})")
     _compare_grad_chunked(grad, oracle.tv_iso_grad(x, 1.0 / n_corners(x.shape), 1e-8))
+
+
+MIX_WEIGHTS = {"sq": 0.3, "iso": 1.7, "l1": (0.7, 1.3, 0.2)}
+MIX_COMBOS = [("sq", "iso"), ("iso", "l1"), ("sq", "l1"), ("sq", "iso", "l1")]
+
+
+def _single_terms(v, combo):
+    """Losses and the weighted gradient sum from the single-term sweeps."""
+    losses, grad = {}, torch.zeros_like(v)
+    if "sq" in combo:
+        losses["sq"], g = tv_loss_sq_3d_fwd_grad(v, MIX_WEIGHTS["sq"])
+        grad += g
+    if "iso" in combo:
+        losses["iso"], g = tv_loss_iso_3d_fwd_grad(v, MIX_WEIGHTS["iso"], eps=1e-8)
+        grad += g
+    if "l1" in combo:
+        losses["l1"], g = tv_loss_l1_3d_fwd_grad(v, MIX_WEIGHTS["l1"])
+        grad += g
+    return losses, grad
+
+
+@pytest.mark.parametrize("combo", MIX_COMBOS, ids=["+".join(c) for c in MIX_COMBOS])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_multi_term_sweep_matches_single_terms_and_oracle(shape, combo):
+    """Two or three terms in one sweep: each loss equals its single-term
+    sweep's and the oracle's; the gradient equals the weighted sum of the
+    single-term gradients and of the oracle's."""
+    vol = rand_vol(shape, 31)
+    v = vol.cuda()
+    losses, grad = tv_loss_multi_3d_fwd_grad(v, eps=1e-8, **{k: MIX_WEIGHTS[k] for k in combo})
+    ref_losses, ref_grad = _single_terms(v, combo)
+    assert set(losses) == set(combo)
+    for k in combo:
+        torch.testing.assert_close(losses[k], ref_losses[k], rtol=1e-6, atol=0)
+    assert_same_up_to_rounding(grad, ref_grad)
+    x = vol.numpy()
+    oracle_grad = np.zeros_like(x.reshape(-1, *x.shape[-3:]))
+    if "sq" in combo:
+        np.testing.assert_allclose(losses["sq"].item(), oracle.tv_sq_loss(x), rtol=FWD_RTOL)
+        oracle_grad += oracle.tv_sq_grad(x, MIX_WEIGHTS["sq"]).reshape(oracle_grad.shape)
+    if "iso" in combo:
+        np.testing.assert_allclose(losses["iso"].item(), oracle.tv_iso_loss(x, 1e-8), rtol=FWD_RTOL, atol=1e-12)
+        oracle_grad += oracle.tv_iso_grad(x, MIX_WEIGHTS["iso"] / n_corners(shape), 1e-8).reshape(oracle_grad.shape)
+    if "l1" in combo:
+        np.testing.assert_allclose(losses["l1"].cpu().numpy(), oracle.tv_l1_loss(x), rtol=FWD_RTOL)
+        oracle_grad += oracle.tv_l1_grad(x, np.array(MIX_WEIGHTS["l1"], np.float32)).reshape(oracle_grad.shape)
+    assert_grad_close(grad, oracle_grad)
+
+
+def test_multi_term_sweep_on_the_benchmark_volume():
+    """iso + L1 in one sweep on the [4, 256^3] volume with 1% plateaus (the
+    benchmark step done as one sweep instead of two), against the two single
+    sweeps and the oracle."""
+    import bench
+
+    vol = bench.tv_iso_l1_volume(1)
+    v = vol.cuda()
+    losses, grad = tv_loss_multi_3d_fwd_grad(v, iso=1.0, l1=1.0, eps=1e-8)
+    li, gi = tv_loss_iso_3d_fwd_grad(v, 1.0, eps=1e-8)
+    ll, gl = tv_loss_l1_3d_fwd_grad(v, 1.0)
+    torch.testing.assert_close(losses["iso"], li, rtol=1e-6, atol=0)
+    torch.testing.assert_close(losses["l1"], ll, rtol=1e-6, atol=0)
+    assert_same_up_to_rounding(grad, gi + gl)
+    x = vol.numpy()
+    np.testing.assert_allclose(losses["iso"].item(), oracle.tv_iso_loss(x, 1e-8), rtol=FWD_RTOL)
+    np.testing.assert_allclose(losses["l1"].cpu().numpy(), oracle.tv_l1_loss(x), rtol=FWD_RTOL)
+
+
+def test_multi_term_c_abi_accumulates_and_rejects_one_term():
+    lib = ctypes.CDLL(str(Path(_core.__file__).parent / "libquantem_cuda_b200.so"))
+    vp, i, f, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+    fn = lib.tv_loss_mix_3d_fwd_grad_cuda
+    fn.argtypes = [i, i, vp, vp, vp, vp, i, i, i, i, f, f, vp, sz, vp]
+    vol = rand_vol((2, 24, 20, 68), 32)
+    v = vol.cuda()
+    ws = torch.empty(lib.tv_loss_3d_workspace_bytes(0, 0, 0, 0), dtype=torch.uint8, device="cuda")
+    g = torch.tensor([0.5, 2.0, 1.0, 1.0, 1.0], device="cuda")
+    acc = torch.zeros(5, device="cuda")
+    grad = torch.empty_like(v)
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):  # acc += ...
+        assert fn(7, 0, v.data_ptr(), g.data_ptr(), acc.data_ptr(), grad.data_ptr(), 2, 24, 20, 68, 1e-8, 1.0,
+                  ws.data_ptr(), ws.numel(), st) == 0
+    x = vol.numpy()
+    np.testing.assert_allclose(acc[0].item(), 2 * oracle.tv_sq_loss(x), rtol=FWD_RTOL)
+    np.testing.assert_allclose(acc[1].item(), 2 * oracle.tv_iso_sum(x, 1e-8), rtol=FWD_RTOL)
+    np.testing.assert_allclose(acc[2:].cpu().numpy(), 2 * oracle.tv_l1_loss(x), rtol=FWD_RTOL)
+    expected = (oracle.tv_sq_grad(x, 0.5) + oracle.tv_iso_grad(x, 2.0, 1e-8)
+                + oracle.tv_l1_grad(x, np.ones(3, np.float32)))
+    assert_grad_close(grad, expected)
+    for terms in (0, 1, 2, 4, 8):
+        assert fn(terms, 0, v.data_ptr(), g.data_ptr(), acc.data_ptr(), grad.data_ptr(), 2, 24, 20, 68, 1e-8, 1.0,
+                  ws.data_ptr(), ws.numel(), st) == 10001
 
 
 def test_no_kernel_gave_up_waiting():
