@@ -1101,6 +1101,7 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
     # pinned host buffers, as the CPU computation leaves them in host memory.
     e2e = None
     ref_cuda = None
+    l2_ceiling = None
     if ctx.world == 1:
         hp, hr, hg, hu = (t.pin_memory() for t in (pts, rot, plane, up))
         out_host = torch.empty((N, T * C), pin_memory=True)
@@ -1125,6 +1126,7 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
                "what": "points, rotations, planes and upstream gradient copied in; output and the point, "
                        "rotation and plane gradients copied back to pinned host memory"}
         ref_cuda = ref_cuda_kplanes(ctx, p, r, g, u, steps, warmup)
+        l2_ceiling = kplanes_l2_ceiling(p, r, g, u)
     else:
         # each rank brings its points and upstream gradient in from pinned host
         # memory (planes and rotations are parameters resident on the device)
@@ -1185,8 +1187,68 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         "clocks": sampler.summary(),
         "e2e": e2e,
         "ref_cuda": ref_cuda,
+        "l2_ceiling": l2_ceiling,
         "breakdown": breakdown,
         "dtype": "f32",
+    }
+
+
+def kplanes_l2_ceiling(p, r, g, u, reps: int = 10) -> dict:
+    """The forward and backward kernels (C ABI, no op-layer work) against
+    kplanes_l2_probe_cuda, which replays their memory traffic at C = 32
+    without arithmetic: 12 corner rows of 128 B gathered per (point,
+    rotation), plus a vector reduction per corner in the backward. The
+    probe's time is the L2-side ceiling of the access pattern."""
+    from quantem.cuda import _core
+
+    N, T = p.shape[0], r.shape[0]
+    C, H, W = g.shape[1:]
+    if C != 32:
+        return {"unavailable": "the probe replays C = 32"}
+    dev = p.device
+    st = torch.cuda.current_stream(dev).cuda_stream
+    pairs = N * T
+    planes = torch.rand((3, H, W, C), device=dev)
+    pgrad = torch.zeros_like(planes)
+    out = torch.empty((N, T * C), device=dev)
+    gpts = torch.zeros((N, 3), device=dev)
+    sink = torch.empty(int(_core.kplanes_l2_probe_sink_floats()), device=dev)
+    grid_cl = g.permute(0, 2, 3, 1).contiguous()
+    gg, gr = torch.zeros_like(grid_cl), torch.zeros_like(r)
+
+    def timed(fn) -> float:
+        for _ in range(3):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    def probe(mode):
+        return lambda: _core.kplanes_l2_probe_cuda(mode, planes.data_ptr(), pgrad.data_ptr(), u.data_ptr(),
+                                                   out.data_ptr(), gpts.data_ptr(), sink.data_ptr(), pairs, N,
+                                                   H, W, st)
+
+    res = {m: timed(probe(getattr(_core, f"KP_PROBE_{m.upper()}"))) for m in ("gather", "reduce", "backward",
+                                                                             "forward")}
+    fwd_ms = timed(lambda: _core.kplanes_tilted_fuse_cuda(p.data_ptr(), r.data_ptr(), grid_cl.data_ptr(),
+                                                          out.data_ptr(), N, T, C, H, W, st))
+    bwd_ms = timed(lambda: _core.kplanes_tilted_fuse_grad_cuda(p.data_ptr(), r.data_ptr(), grid_cl.data_ptr(),
+                                                               u.data_ptr(), gg.data_ptr(), gr.data_ptr(),
+                                                               gpts.data_ptr(), N, T, C, H, W, st))
+    lines = 12.0 * pairs * 128
+    return {
+        "what": "kernels (C ABI) against kplanes_l2_probe_cuda, their memory traffic without arithmetic "
+                "(hashed cells, 8 lanes x float4 per pair); traffic_ms / kernel_ms = fraction of the ceiling",
+        "fwd_kernel_ms": fwd_ms, "fwd_traffic_ms": res["forward"], "fwd_frac": res["forward"] / fwd_ms,
+        "bwd_kernel_ms": bwd_ms, "bwd_traffic_ms": res["backward"], "bwd_frac": res["backward"] / bwd_ms,
+        "gather_only_ms": res["gather"], "reduce_only_ms": res["reduce"],
+        "l2_gather_GBps": lines / (res["gather"] / 1e3) / 1e9,
+        "l2_reduce_GBps": lines / (res["reduce"] / 1e3) / 1e9,
     }
 
 
@@ -1281,6 +1343,11 @@ def main() -> None:
         return
 
     if ctx.world > 1:
+        # NCCL's communicator set-up log on stderr (the JSON line keeps stdout):
+        # it names every rank and its GPU, although the data plane of the
+        # default transports is peer memory
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(ctx.local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", ctx.local_rank))

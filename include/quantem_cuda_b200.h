@@ -379,6 +379,26 @@ int kplanes_tilted_tv_fuse_grad_cuda(const float *d_pts, const float *d_R, const
                                      float *d_gpts, long B, int T, int C, int H, int W, float h,
                                      cudaStream_t stream);
 
+/* Diagnostic, no counterpart in the reference: the memory traffic of the
+ * K-Planes kernels at C = 32 without their arithmetic, to measure the L2-side
+ * ceiling of their access pattern. `pairs` (point, rotation) pairs each touch
+ * 12 channel rows of 128 B at hashed cells of three [H, W, 32] planes:
+ *   QC_KP_PROBE_GATHER    gathers them;
+ *   QC_KP_PROBE_REDUCE    adds a red.global.add.v4.f32 per 16 B into d_grad;
+ *   QC_KP_PROBE_BACKWARD  gathers, reduces, reads a 128-B row of d_gout and adds
+ *                         3 floats to d_gpts (the backward's traffic);
+ *   QC_KP_PROBE_FORWARD   gathers and writes a 128-B row of d_out (the forward's).
+ * Buffers: d_planes and d_grad 3*H*W*32 floats, d_gout and d_out pairs*32,
+ * d_gpts npts*3, d_sink kplanes_l2_probe_sink_floats() floats. */
+#define QC_KP_PROBE_GATHER 0
+#define QC_KP_PROBE_REDUCE 1
+#define QC_KP_PROBE_BACKWARD 2
+#define QC_KP_PROBE_FORWARD 3
+int kplanes_l2_probe_cuda(int mode, const float *d_planes, float *d_grad, const float *d_gout,
+                          float *d_out, float *d_gpts, float *d_sink, long long pairs,
+                          long long npts, int H, int W, cudaStream_t stream);
+size_t kplanes_l2_probe_sink_floats(void);
+
 /* Plane layout conversion [P, C, H, W] -> [P, H, W, C] and back. Replaces the
  * torch permute+contiguous of the reference's op layer
  * (src/quantem/cuda/core/ml/_ops.py:21-25, :82). src and dst must not overlap. */

@@ -43,7 +43,7 @@ NVCC_FLAGS = [
     f"-I{CSRC}",
 ]
 
-CU_SOURCES = ["status.cu", "tv_sweep.cu", "kplanes_tilted.cu", "peer_mem.cu", "peer_reduce.cu"]
+CU_SOURCES = ["status.cu", "tv_sweep.cu", "kplanes_tilted.cu", "kplanes_probe.cu", "peer_mem.cu", "peer_reduce.cu"]
 HEADERS = [INCLUDE / "quantem_cuda_b200.h", CSRC / "qc_common.cuh"]
 
 LIB = PKG / "libquantem_cuda_b200.so"

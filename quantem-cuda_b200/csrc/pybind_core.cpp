@@ -315,6 +315,24 @@ PYBIND11_MODULE(_core, m) {
         py::arg("W"), py::arg("stream_ptr"));
 
     m.def(
+        "kplanes_l2_probe_cuda",
+        [](int mode, uintptr_t planes, uintptr_t grad, uintptr_t gout, uintptr_t out, uintptr_t gpts,
+           uintptr_t sink, long long pairs, long long npts, int H, int W, uintptr_t stream) {
+            check(kplanes_l2_probe_cuda(mode, ptr<const float>(planes), ptr<float>(grad),
+                                        ptr<const float>(gout), ptr<float>(out), ptr<float>(gpts),
+                                        ptr<float>(sink), pairs, npts, H, W, stream_of(stream)));
+        },
+        "Diagnostic: the K-Planes kernels' memory traffic (C = 32) without their arithmetic.",
+        py::arg("mode"), py::arg("planes_ptr"), py::arg("grad_ptr"), py::arg("gout_ptr"),
+        py::arg("out_ptr"), py::arg("gpts_ptr"), py::arg("sink_ptr"), py::arg("pairs"),
+        py::arg("npts"), py::arg("H"), py::arg("W"), py::arg("stream_ptr"));
+    m.def("kplanes_l2_probe_sink_floats", &kplanes_l2_probe_sink_floats);
+    m.attr("KP_PROBE_GATHER") = QC_KP_PROBE_GATHER;
+    m.attr("KP_PROBE_REDUCE") = QC_KP_PROBE_REDUCE;
+    m.attr("KP_PROBE_BACKWARD") = QC_KP_PROBE_BACKWARD;
+    m.attr("KP_PROBE_FORWARD") = QC_KP_PROBE_FORWARD;
+
+    m.def(
         "device_fault_word",
         [](int device, bool clear) {
             unsigned int w = 0;
