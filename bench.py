@@ -290,6 +290,28 @@ def time_steps(ctx: Ctx, step, steps: int, warmup: int, sampler: ClockSampler | 
     return ctx.max_over_ranks(ms)
 
 
+def time_pipelined(ctx: Ctx, step, steps: int, warmup: int, side_streams) -> float:
+    """time_steps for steps whose copies run on side streams: the end event
+    is recorded once the compute stream has waited for every side stream, so
+    the timed region holds all K steps' copies and kernels."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(cur)
+    for _ in range(steps):
+        step()
+    for s_ in side_streams:
+        cur.wait_stream(s_)
+    end.record(cur)
+    torch.cuda.synchronize()
+    ctx.barrier()
+    return ctx.max_over_ranks(start.elapsed_time(end))
+
+
 class KernelTimer:
     """CUDA-event durations of one launch site inside the timed loop."""
 
@@ -529,6 +551,7 @@ def cpu_kplanes_ms(sample_n: int = 2048, min_seconds: float = 10.0, reps: int | 
 
 CPU_BASELINES = {
     "tv_iso_l1": cpu_tv_iso_l1,
+    "tv_multi": cpu_tv_iso_l1,
     "tv_sq_128": cpu_tv_sq_128,
     "tv_1024": cpu_tv_1024,
     "kplanes": cpu_kplanes,
@@ -537,6 +560,7 @@ CPU_BASELINES = {
 
 TORCH_CPU_BASELINES = {
     "tv_iso_l1": torch_cpu_tv_iso_l1,
+    "tv_multi": torch_cpu_tv_iso_l1,
     "tv_sq_128": torch_cpu_tv_sq_128,
     "kplanes": torch_cpu_kplanes,
 }
@@ -769,6 +793,54 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
 
     e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
     e2e_losses_ms = time_steps(ctx, lambda: e2e_step(False), steps, min(warmup, 3))
+    piped = None
+    if ctx.world == 1:
+        # The same public ops with the steps pipelined the way a caller that
+        # streams volumes through the GPU would run them: step k+1's volume
+        # comes in on one copy stream and step k's gradients go out on another
+        # while step k computes (two device slots; every copy of every step is
+        # still inside the timed region).
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        comp = torch.cuda.current_stream(dev)
+        slots = [torch.empty_like(vol) for _ in range(2)]
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_comp = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+        out_host = [[torch.empty(4, pin_memory=True)] + [torch.empty(vol_cpu.shape, pin_memory=True)
+                                                         for _ in range(2)] for _ in range(2)]
+        used = [False, False]
+        k_ = [0]
+
+        def piped_step():
+            i = k_[0] % 2
+            if used[i]:
+                s_in.wait_event(ev_comp[i])  # the slot's previous volume has been read
+            with torch.cuda.stream(s_in):
+                slots[i].copy_(host, non_blocking=True)
+                ev_in[i].record(s_in)
+            comp.wait_event(ev_in[i])
+            if used[i]:
+                comp.wait_event(ev_out[i])  # the slot's previous results have left
+            li, gi = tv_loss_iso_3d_fwd_grad(slots[i], g1, eps=1e-8)
+            ls, gl = tv_loss_l1_3d_fwd_grad(slots[i], g3)
+            ev_comp[i].record(comp)
+            s_out.wait_event(ev_comp[i])
+            with torch.cuda.stream(s_out):
+                res, hg_i, hg_l = out_host[i]
+                res[:1].copy_(li.reshape(1), non_blocking=True)
+                res[1:].copy_(ls, non_blocking=True)
+                hg_i.copy_(gi, non_blocking=True)
+                hg_l.copy_(gl, non_blocking=True)
+                ev_out[i].record(s_out)
+            for t_ in (li, ls, gi, gl):
+                t_.record_stream(s_out)
+            used[i] = True
+            k_[0] += 1
+
+        piped_ms = time_pipelined(ctx, piped_step, steps, min(warmup, 3), (s_in, s_out))
+        piped = {"value": voxels_local / (piped_ms / steps / 1e3), "ms_per_step": piped_ms / steps,
+                 "what": "the same copies and public ops, step k+1's volume in and step k's losses and "
+                         "gradients out on two copy streams while step k computes"}
     ref_cuda = None
     one_sweep = None
     if ctx.world == 1:
@@ -793,10 +865,12 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
         "unit": "voxels/s",
         "h2d_bytes_per_step": host.numel() * 4 * ctx.world,
         "d2h_bytes_per_step": (16 + 2 * host.numel() * 4) * ctx.world,
-        "what": "volume copied in, both losses and both gradients copied back to pinned host memory",
+        "what": "volume copied in, both losses and both gradients copied back to pinned host memory, "
+                "one step after the other",
         "losses_only": {"value": voxels_local * ctx.world / (e2e_losses_ms / steps / 1e3),
                         "d2h_bytes_per_step": 16 * ctx.world,
                         "what": "gradients left on the device, losses read back"},
+        "pipelined": piped,
     }
 
     peak, peak_kind = measured_hbm_peak()
@@ -833,6 +907,43 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
         "ref_cuda": ref_cuda,
         "one_sweep": one_sweep,
         "breakdown": breakdown,
+        "dtype": "f32",
+    }
+
+
+def run_tv_multi(ctx: Ctx, steps: int, warmup: int) -> dict:
+    """The tv_iso_l1 volume with both losses and their summed gradient from
+    one sweep (tv_loss_multi_3d_fwd_grad): one GPU, one JSON line."""
+    from quantem.cuda.core import tv_loss_multi_3d_fwd_grad
+
+    if ctx.world > 1:
+        raise SystemExit("tv_multi runs on one GPU")
+    dev = ctx.device
+    vol_cpu = tv_iso_l1_volume(1)
+    vol = vol_cpu.to(dev)
+    g1 = torch.ones(1, device=dev)
+    g3 = torch.ones(3, device=dev)
+    t = KernelTimer()
+    both = t.wrap(lambda: tv_loss_multi_3d_fwd_grad(vol, iso=g1, l1=g3, eps=1e-8))
+    sampler = ClockSampler(ctx.local_rank)
+    ms = time_steps(ctx, both, steps, warmup, sampler)
+    op_ms = t.mean_ms(steps)
+    algo = 8.0 * vol.numel()
+    peak, peak_kind = measured_hbm_peak()
+    return {
+        "metric": "TV fwd+grad voxels/sec",
+        "value": vol.numel() / (ms / steps / 1e3),
+        "unit": "voxels/s",
+        "ms_per_step": ms / steps,
+        "gpu_launches": 2 * steps,
+        "config": {"workload": DESCRIPTIONS["tv_multi"], "shape_per_gpu": list(vol.shape),
+                   "l2": "inputs larger than L2 (268 MB volume, 268 MB gradient per step)"},
+        "roofline": {"bound": "hbm", "kernel": "tv iso + L1 mixed sweep (with its finalize)",
+                     "achieved": algo / (op_ms / 1e3) / 1e9, "peak": peak,
+                     "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
+                     "frac": algo / (op_ms / 1e3) / 1e9 / peak, "traffic": None, "algorithmic_bytes": algo},
+        "clocks": sampler.summary(),
+        "e2e": None,
         "dtype": "f32",
     }
 
@@ -1120,11 +1231,56 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
             torch.cuda.current_stream().synchronize()
 
         e2e_ms = time_steps(ctx, e2e_step, steps, min(warmup, 3))
+
+        # the same steps pipelined: step k+1's inputs in on one copy stream and
+        # step k's output and gradients out on another while step k computes
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        comp = torch.cuda.current_stream(dev)
+        slots = [[torch.empty(t.shape, device=dev) for t in (pts, rot, plane, up)] for _ in range(2)]
+        hosts = [[torch.empty((N, T * C), pin_memory=True)] + [torch.empty(t.shape, pin_memory=True)
+                                                              for t in (pts, rot, plane)] for _ in range(2)]
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_comp = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+        used = [False, False]
+        k_ = [0]
+
+        def piped_step():
+            i = k_[0] % 2
+            if used[i]:
+                s_in.wait_event(ev_comp[i])
+            with torch.cuda.stream(s_in):
+                for d_, h_ in zip(slots[i], (hp, hr, hg, hu)):
+                    d_.copy_(h_, non_blocking=True)
+                ev_in[i].record(s_in)
+            comp.wait_event(ev_in[i])
+            if used[i]:
+                comp.wait_event(ev_out[i])
+            pp, rr, gg = (t.detach().requires_grad_(True) for t in slots[i][:3])
+            out = kplanes_tilted_fuse(pp, rr, gg)
+            out.backward(slots[i][3])
+            ev_comp[i].record(comp)
+            s_out.wait_event(ev_comp[i])
+            results = (out.detach(), pp.grad, rr.grad, gg.grad)
+            with torch.cuda.stream(s_out):
+                for h_, t_ in zip(hosts[i], results):
+                    h_.copy_(t_, non_blocking=True)
+                ev_out[i].record(s_out)
+            for t_ in results:
+                t_.record_stream(s_out)
+            used[i] = True
+            k_[0] += 1
+
+        piped_ms = time_pipelined(ctx, piped_step, steps, min(warmup, 3), (s_in, s_out))
         e2e = {"value": N / (e2e_ms / steps / 1e3), "unit": "points/s",
                "h2d_bytes_per_step": sum(t.numel() * 4 for t in (hp, hr, hg, hu)),
                "d2h_bytes_per_step": (out_host.numel() + sum(t.numel() for t in gh)) * 4,
                "what": "points, rotations, planes and upstream gradient copied in; output and the point, "
-                       "rotation and plane gradients copied back to pinned host memory"}
+                       "rotation and plane gradients copied back to pinned host memory, one step after "
+                       "the other",
+               "pipelined": {"value": N / (piped_ms / steps / 1e3), "ms_per_step": piped_ms / steps,
+                             "what": "the same copies and public ops, step k+1's inputs in and step k's "
+                                     "results out on two copy streams while step k computes"}}
         ref_cuda = ref_cuda_kplanes(ctx, p, r, g, u, steps, warmup)
         l2_ceiling = kplanes_l2_ceiling(p, r, g, u)
     else:
@@ -1255,6 +1411,8 @@ def kplanes_l2_ceiling(p, r, g, u, reps: int = 10) -> dict:
 DESCRIPTIONS = {
     "tv_iso_l1": "tv_iso_l1: tv_loss_iso_3d (eps 1e-8) + tv_loss_l1_3d single-sweep fwd+grad",
     "tv_sq_128": "tv_sq_128: tv_loss_sq_3d single-sweep fwd+grad on [128,128,128]",
+    "tv_multi": "tv_multi: tv_loss_iso_3d (eps 1e-8) + tv_loss_l1_3d losses and summed gradient in one sweep "
+                "(tv_loss_multi_3d_fwd_grad) on the tv_iso_l1 volume",
     "tv_1024": "tv_1024: tv_loss_sq_3d + tv_loss_iso_3d single-sweep fwd+grad on [1024]^3 blobs",
     "kplanes": "kplanes: kplanes_tilted_fuse fwd + bwd ops, N=2^20, T=4, C=32, 256^2",
     "kplanes_ms": "kplanes_ms: multiscale kplanes_tilted_fuse fwd + bwd, 4 levels 64/128/256/512, N=2^24, T=8, C=32",
@@ -1263,6 +1421,7 @@ DESCRIPTIONS = {
 WORKLOADS = {
     "tv_iso_l1": run_tv_iso_l1,
     "tv_sq_128": run_tv_sq_128,
+    "tv_multi": run_tv_multi,
     "tv_1024": run_tv_1024,
     "kplanes": run_kplanes,
     "kplanes_ms": run_kplanes_ms,
