@@ -147,11 +147,12 @@ int tv_loss_l1_3d_fwd_grad_cuda(const float *d_vol, const float *d_g, float *d_a
  * reads the volume once instead of once per term.
  *   terms: two or three of QC_TV_TERM_SQ, QC_TV_TERM_ISO, QC_TV_TERM_L1
  *   flags: 0 (acc += ...) or QC_TV_ACC_OVERWRITE (acc = ...)
- *   d_g:   5 device floats [g_sq, g_iso, g_d, g_h, g_w]: the gradient written
- *          is g_sq·∇Σsq + g_iso·∇Σiso + Σ_axis g_axis·∇Σ|Δ_axis| (the raw
- *          sums; for the mean isotropic loss pass g_iso = upstream / N)
- *   d_acc: 5 device floats [Σsq, iso_scale·Σiso, Σ|Δd|, Σ|Δh|, Σ|Δw|]; slots
- *          of terms not requested receive 0 (or are left as they were)
+ *   d_acc: 5 device floats, the losses [Σsq, iso_scale·Σiso, Σ|Δd|, Σ|Δh|,
+ *          Σ|Δw|] (iso_scale = 1/N gives the isotropic mean); slots of terms
+ *          not requested receive 0 (or are left as they were)
+ *   d_g:   5 device floats, the upstream gradient of each of those losses:
+ *          the gradient written is g_sq·∇Σsq + g_iso·iso_scale·∇Σiso +
+ *          Σ_axis g_axis·∇Σ|Δ_axis|
  * Deterministic (fixed-order reduction through the workspace, at least
  * tv_loss_3d_workspace_bytes() bytes). */
 #define QC_TV_TERM_SQ 1

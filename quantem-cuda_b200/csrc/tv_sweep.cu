@@ -261,12 +261,14 @@ __device__ __forceinline__ Gains load_gains(const float *g, float scale) {
     Gains gn{1.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (g == nullptr) return gn;
     if constexpr (is_mix(V)) {
-        // g = [g_sq, g_iso, g_d, g_h, g_w]; the divergence gain stays 1
-        gn.gsq2 = 2.0f * (__ldg(g) * scale);
+        // g = [g_sq, g_iso, g_d, g_h, g_w], the upstream gradients of the
+        // reported losses; `scale` is the isotropic loss's own factor (1/N
+        // for the mean), so only g_iso takes it. The divergence gain stays 1.
+        gn.gsq2 = 2.0f * __ldg(g);
         gn.giso = __ldg(g + 1) * scale;
-        gn.gd = __ldg(g + 2) * scale;
-        gn.gh = __ldg(g + 3) * scale;
-        gn.gw = __ldg(g + 4) * scale;
+        gn.gd = __ldg(g + 2);
+        gn.gh = __ldg(g + 3);
+        gn.gw = __ldg(g + 4);
     } else if constexpr (V == QC_TV_SQ) {
         gn.gmul = 2.0f * (__ldg(g) * scale);
     } else if constexpr (V == QC_TV_ISO) {
@@ -1600,9 +1602,9 @@ int run(int variant, int flags, const float *vol, const float *g, float *acc, fl
     pl.has_prev = has_prev ? 1 : 0;
     pl.has_next = has_next ? 1 : 0;
     pl.eps = eps;
-    // a mixed sweep takes every gain from d_g; acc_scale multiplies its
-    // isotropic sum only (slot 1)
-    pl.scale = mixed ? 1.0f : acc_scale;
+    // a mixed sweep: acc_scale multiplies its isotropic sum (slot 1) and the
+    // isotropic gradient term, the other gains come from d_g unscaled
+    pl.scale = acc_scale;
     pl.acc_atomic = (atomic_acc && want_loss) ? acc : nullptr;
 
     const bool aligned = (reinterpret_cast<uintptr_t>(vol) % 16 == 0) &&

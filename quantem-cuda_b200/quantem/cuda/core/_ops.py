@@ -275,8 +275,7 @@ def _tv_loss_multi_3d_fwd_grad(volume: Tensor, weights: Tensor, terms: int, eps:
     l1_h, l1_w], Σ_term w·∂term/∂volume) for the terms in the bit mask."""
     vol, b, d, h, w, stream = _launch_args(volume)
     n = float(_iso_n_corners(vol.shape))
-    scale = torch.tensor([1.0, 1.0 / n, 1.0, 1.0, 1.0], dtype=torch.float32, device=vol.device)
-    g = (weights.detach().to(dtype=torch.float32, device=vol.device).reshape(5) * scale).contiguous()
+    g = weights.detach().to(dtype=torch.float32, device=vol.device).reshape(5).contiguous()
     acc = torch.empty(5, dtype=torch.float32, device=vol.device)
     grad_vol = torch.empty_like(vol)
     ws = _workspace(vol.device)
@@ -383,7 +382,7 @@ def tv_loss_l1_3d_fwd_grad(
     in one HBM sweep. ``grad_out`` is a 3-vector (or a scalar for all axes)."""
     vol = _as_batched(volume, "tv_loss_l1_3d_fwd_grad")
     if isinstance(grad_out, (tuple, list)):
-        g = torch.tensor(grad_out, dtype=torch.float32, device=vol.device)
+        g = _host_values(grad_out, vol.device)
     elif isinstance(grad_out, Tensor):
         g = grad_out.detach().to(dtype=torch.float32, device=vol.device)
         g = g.expand(3) if g.numel() == 1 else g.reshape(3)
@@ -401,8 +400,16 @@ def _weight(x, n: int, device) -> Tensor:
     if isinstance(x, (tuple, list)):
         if len(x) != n:
             raise ValueError(f"expected {n} weights, got {len(x)}")
-        return torch.tensor([float(v) for v in x], dtype=torch.float32, device=device)
+        return _host_values(x, device)
     return torch.full((n,), float(x), dtype=torch.float32, device=device)
+
+
+def _host_values(values, device) -> Tensor:
+    """A few host floats on the device through pinned memory: the copy is
+    queued on the current stream without waiting for it (a copy from pageable
+    memory would first synchronise with the stream)."""
+    host = torch.tensor([float(v) for v in values], dtype=torch.float32).pin_memory()
+    return host.to(device, non_blocking=True)
 
 
 def tv_loss_multi_3d_fwd_grad(

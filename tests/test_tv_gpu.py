@@ -461,14 +461,15 @@ def test_multi_term_c_abi_accumulates_and_rejects_one_term():
     acc = torch.zeros(5, device="cuda")
     grad = torch.empty_like(v)
     st = torch.cuda.current_stream().cuda_stream
+    iso_scale = 0.25  # acc[1] = 0.25 * iso sum; gradient term 2.0 * 0.25 * grad(iso sum)
     for _ in range(2):  # acc += ...
-        assert fn(7, 0, v.data_ptr(), g.data_ptr(), acc.data_ptr(), grad.data_ptr(), 2, 24, 20, 68, 1e-8, 1.0,
-                  ws.data_ptr(), ws.numel(), st) == 0
+        assert fn(7, 0, v.data_ptr(), g.data_ptr(), acc.data_ptr(), grad.data_ptr(), 2, 24, 20, 68, 1e-8,
+                  iso_scale, ws.data_ptr(), ws.numel(), st) == 0
     x = vol.numpy()
     np.testing.assert_allclose(acc[0].item(), 2 * oracle.tv_sq_loss(x), rtol=FWD_RTOL)
-    np.testing.assert_allclose(acc[1].item(), 2 * oracle.tv_iso_sum(x, 1e-8), rtol=FWD_RTOL)
+    np.testing.assert_allclose(acc[1].item(), 2 * iso_scale * oracle.tv_iso_sum(x, 1e-8), rtol=FWD_RTOL)
     np.testing.assert_allclose(acc[2:].cpu().numpy(), 2 * oracle.tv_l1_loss(x), rtol=FWD_RTOL)
-    expected = (oracle.tv_sq_grad(x, 0.5) + oracle.tv_iso_grad(x, 2.0, 1e-8)
+    expected = (oracle.tv_sq_grad(x, 0.5) + oracle.tv_iso_grad(x, 2.0 * iso_scale, 1e-8)
                 + oracle.tv_l1_grad(x, np.ones(3, np.float32)))
     assert_grad_close(grad, expected)
     for terms in (0, 1, 2, 4, 8):
