@@ -1117,6 +1117,25 @@ def run_kplanes_ms(ctx: Ctx, steps: int, warmup: int) -> dict:
     if reducers is not None:
         for red in reducers:
             red.close()
+    one_launch = None
+    if ctx.world == 1:
+        # all four levels in one launch per pass (kplanes_tilted_fuse_levels),
+        # the same work as the per-level loop above
+        torch.cuda.empty_cache()
+
+        def levels_step():
+            outs = torch.ops.quantem_cuda.kplanes_tilted_fuse_levels(p, r, planes)
+            grads = torch.ops.quantem_cuda.kplanes_tilted_fuse_levels_bwd(p, r, planes, ups)
+            return outs, grads
+
+        try:
+            lv_ms = time_steps(ctx, lambda: levels_step() and None, steps, min(warmup, 3)) / steps
+            one_launch = {"value": n_total / (lv_ms / 1e3), "ms_per_step": lv_ms,
+                          "what": "kplanes_tilted_fuse_levels forward + backward: all four levels in one launch "
+                                  "per pass (all four outputs alive at once)"}
+        except torch.OutOfMemoryError as e:  # four 17 GB outputs at once
+            one_launch = {"unavailable": f"out of device memory: {str(e).splitlines()[0]}"}
+        torch.cuda.empty_cache()
     n_local = p.shape[0]
     P = [g.numel() * 4 for g in planes]
     # per rank: out + upstream (2·4·N·R·C) + points (12 N fwd, 12 N bwd, 12 N gpts)
@@ -1135,7 +1154,8 @@ def run_kplanes_ms(ctx: Ctx, steps: int, warmup: int) -> dict:
                    "points_per_gpu": n_local,
                    "parallelism": f"points{ctx.world} (gradient sum: peer)" if ctx.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (17 GB output + 17 GB upstream gradient per level at 1 GPU)",
-                   "level_ms": dict(zip(("64", "128", "256", "512"), lvl_ms))},
+                   "level_ms": dict(zip(("64", "128", "256", "512"), lvl_ms)),
+                   "one_launch_all_levels": one_launch},
         "roofline": {"bound": "hbm", "kernel": "all four levels' fwd+bwd (per rank, step)",
                      "achieved": algo / (ms_step / 1e3) / 1e9, "peak": peak,
                      "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
@@ -1505,8 +1525,9 @@ def main() -> None:
         # NCCL's communicator set-up log on stderr (the JSON line keeps stdout):
         # it names every rank and its GPU, although the data plane of the
         # default transports is peer memory
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
         torch.cuda.set_device(ctx.local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", ctx.local_rank))

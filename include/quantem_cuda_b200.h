@@ -361,6 +361,27 @@ int kplanes_tilted_fuse_grad_rotations_cuda(const float *d_pts, const float *d_R
                                             int T, int C, int H, int W, int t_begin, int t_end,
                                             cudaStream_t stream);
 
+/* Several levels of one multiscale tilted K-Planes encoding (the caller's
+ * loop over resolutions: one rotation set, one point set, the planes of each
+ * level at their own H x W, all with C channels) in one launch each way.
+ * `grids`, `outs`, `gouts`, `ggrids`, `H` and `W` are HOST arrays of
+ * n_levels entries (1 <= n_levels <= QC_KP_MAX_LEVELS) holding device
+ * pointers and sizes; level l is exactly kplanes_tilted_fuse_cuda /
+ * kplanes_tilted_fuse_grad_cuda on grids[l] (channels-last [3T, H[l], W[l], C],
+ * outs[l] and gouts[l] [N, T*C]). The backward accumulates each level's plane
+ * gradient into ggrids[l] and the sum over levels into gR and gpts. No
+ * counterpart in the reference (its caller, quantem's multiscale K-Planes
+ * encoder, calls the single-level op once per level). */
+#define QC_KP_MAX_LEVELS 8
+int kplanes_tilted_fuse_levels_cuda(const float *d_pts, const float *d_R, int n_levels,
+                                    const float *const *grids, float *const *outs, const int *H,
+                                    const int *W, long B, int T, int C, cudaStream_t stream);
+int kplanes_tilted_fuse_levels_grad_cuda(const float *d_pts, const float *d_R, int n_levels,
+                                         const float *const *grids, const float *const *gouts,
+                                         float *const *ggrids, const int *H, const int *W,
+                                         float *d_gR, float *d_gpts, long B, int T, int C,
+                                         cudaStream_t stream);
+
 /* Tilted K-Planes at four taps for finite-difference TV regularisation:
  * out[k, b, t*C + c] samples at R_t·p (k = 0, bit-identical to
  * kplanes_tilted_fuse_cuda) and at R_t·p + h·R_t[:, k-1] (k = 1, 2, 3); out is

@@ -166,11 +166,11 @@ constexpr int kFwdMinBlocks = QC_KP_FWD_MINB;
 // interpolation at R_t·p and at the three offsets R_t·p + h·R_t[:, k-1], written
 // to out[k] of a [4, B, T*C] output (tap 0 is bit-identical to NT = 1).
 template <int L, int NT>
-__global__ void __launch_bounds__(kThreads, NT == 1 ? kFwdMinBlocks : 4) kpt_fwd_v4_kernel(const float *__restrict__ pts,
-                                                              const float *__restrict__ R,
-                                                              const float *__restrict__ grid,
-                                                              float *__restrict__ out, long long B,
-                                                              int T, int H, int W, float h) {
+__device__ __forceinline__ void kpt_fwd_v4_body(const float *__restrict__ pts,
+                                                const float *__restrict__ R,
+                                                const float *__restrict__ grid,
+                                                float *__restrict__ out, long long B, int T, int H,
+                                                int W, float h) {
     constexpr int C = 4 * L;
     constexpr int G = 32 / L;  // points per warp tile
     const int t = blockIdx.y;
@@ -229,6 +229,34 @@ __global__ void __launch_bounds__(kThreads, NT == 1 ? kFwdMinBlocks : 4) kpt_fwd
     }
 }
 
+template <int L, int NT>
+__global__ void __launch_bounds__(kThreads, NT == 1 ? kFwdMinBlocks : 4) kpt_fwd_v4_kernel(
+    const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
+    float *__restrict__ out, long long B, int T, int H, int W, float h) {
+    kpt_fwd_v4_body<L, NT>(pts, R, grid, out, B, T, H, W, h);
+}
+
+// Several levels of one multiscale encoding (planes of their own resolution,
+// one rotation set) in one launch: blockIdx.z is the level. Blocks are
+// dispatched level by level, so each level keeps the per-rotation L2
+// residency of its own launch.
+struct LevelTable {
+    const float *grid[QC_KP_MAX_LEVELS];
+    float *out[QC_KP_MAX_LEVELS];
+    const float *gout[QC_KP_MAX_LEVELS];
+    float *ggrid[QC_KP_MAX_LEVELS];
+    int H[QC_KP_MAX_LEVELS], W[QC_KP_MAX_LEVELS];
+};
+
+template <int L>
+__global__ void __launch_bounds__(kThreads, kFwdMinBlocks) kpt_fwd_levels_kernel(
+    const float *__restrict__ pts, const float *__restrict__ R, const LevelTable tab, long long B,
+    int T) {
+    const int lv = blockIdx.z;
+    kpt_fwd_v4_body<L, 1>(pts, R, tab.grid[lv], tab.out[lv], B, T, tab.H[lv], tab.W[lv], 0.f);
+}
+
+
 template <int L>
 __device__ __forceinline__ float group_sum(float v) {
 #pragma unroll
@@ -262,7 +290,7 @@ __device__ __forceinline__ void sample_with_slopes(const float *pc, const Tap &t
 // offset h·R_t[:, k-1] (h·dr_k into column k-1) — and reaches p through
 // R_t^T dr_k; the taps' dr are summed before the point and R_t·p terms.
 template <int L, int NT>
-__global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
+__device__ __forceinline__ void kpt_bwd_v4_body(
     const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
     const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
     float *__restrict__ gpts, long long B, int T, int H, int W, int t0, float h) {
@@ -394,6 +422,26 @@ __global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
         if (v != 0.f) atomicAdd(gR + 9 * t + threadIdx.x, v);
     }
 }
+
+template <int L, int NT>
+__global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_v4_kernel(
+    const float *__restrict__ pts, const float *__restrict__ R, const float *__restrict__ grid,
+    const float *__restrict__ gout, float *__restrict__ ggrid, float *__restrict__ gR,
+    float *__restrict__ gpts, long long B, int T, int H, int W, int t0, float h) {
+    kpt_bwd_v4_body<L, NT>(pts, R, grid, gout, ggrid, gR, gpts, B, T, H, W, t0, h);
+}
+
+// Backward of kpt_fwd_levels_kernel: blockIdx.z is the level; gR and gpts
+// take the sum over the levels (they share the points and the rotations).
+template <int L>
+__global__ void __launch_bounds__(kThreads, kBwdMinBlocks) kpt_bwd_levels_kernel(
+    const float *__restrict__ pts, const float *__restrict__ R, const LevelTable tab,
+    float *__restrict__ gR, float *__restrict__ gpts, long long B, int T) {
+    const int lv = blockIdx.z;
+    kpt_bwd_v4_body<L, 1>(pts, R, tab.grid[lv], tab.gout[lv], tab.ggrid[lv], gR, gpts, B, T,
+                          tab.H[lv], tab.W[lv], 0, 0.f);
+}
+
 
 // ── generic path: any C (scalar channels, one warp per point) ─────────────
 
@@ -727,6 +775,30 @@ int bwd_v4(const float *pts, const float *R, const float *grid, const float *gou
     return 0;
 }
 
+template <int L>
+int fwd_levels(const float *pts, const float *R, const LevelTable &tab, int n, long long B, int T,
+               cudaStream_t stream) {
+    constexpr int G = 32 / L;
+    int gx = 0;
+    if (int st = rotation_grid_x((B + G - 1) / G, 8, &gx)) return st;
+    QC_RETURN_IF(T > 65535, QC_ERR_INVALID_ARGUMENT, "kplanes: T=%d exceeds 65535", T);
+    kpt_fwd_levels_kernel<L><<<dim3(gx, T, n), kThreads, 0, stream>>>(pts, R, tab, B, T);
+    QC_CHECK_LAUNCH("kpt_fwd_levels_kernel launch");
+    return 0;
+}
+
+template <int L>
+int bwd_levels(const float *pts, const float *R, const LevelTable &tab, int n, float *gR,
+               float *gpts, long long B, int T, cudaStream_t stream) {
+    constexpr int G = 32 / L;
+    int gx = 0;
+    if (int st = rotation_grid_x((B + G - 1) / G, kBwdMinBlocks, &gx)) return st;
+    QC_RETURN_IF(T > 65535, QC_ERR_INVALID_ARGUMENT, "kplanes: T=%d exceeds 65535", T);
+    kpt_bwd_levels_kernel<L><<<dim3(gx, T, n), kThreads, 0, stream>>>(pts, R, tab, gR, gpts, B, T);
+    QC_CHECK_LAUNCH("kpt_bwd_levels_kernel launch");
+    return 0;
+}
+
 template <int NT>
 int forward(const char *who, const float *d_pts, const float *d_R, const float *d_grid,
             float *d_out, long B, int T, int C, int H, int W, float h, cudaStream_t stream) {
@@ -790,6 +862,103 @@ int backward(const char *who, const float *d_pts, const float *d_R, const float 
     return 0;
 }
 
+// Checks of the level tables (host arrays of device pointers and sizes).
+int check_levels(const char *who, int n, const void *a, const void *b, const int *H, const int *W,
+                 long B, int T, int C) {
+    QC_RETURN_IF(n < 1 || n > QC_KP_MAX_LEVELS, QC_ERR_INVALID_ARGUMENT,
+                 "%s: %d levels, need 1..%d", who, n, QC_KP_MAX_LEVELS);
+    QC_RETURN_IF(a == nullptr || b == nullptr || H == nullptr || W == nullptr,
+                 QC_ERR_INVALID_ARGUMENT, "%s: null level table", who);
+    for (int l = 0; l < n; ++l)
+        if (int st = check_shapes(who, B, T, C, H[l], W[l])) return st;
+    return 0;
+}
+
+int forward_levels(const float *d_pts, const float *d_R, int n, const float *const *grids,
+                   float *const *outs, const int *H, const int *W, long B, int T, int C,
+                   cudaStream_t stream) {
+    QC_NVTX("quantem::kplanes_fwd_levels");
+    const char *who = "kplanes_tilted_fuse_levels_cuda";
+    if (int st = check_levels(who, n, grids, outs, H, W, B, T, C)) return st;
+    if (B == 0 || T == 0 || C == 0) return 0;
+    bool vec = (C % 4 == 0) && C <= 128;
+    for (int l = 0; l < n; ++l) {
+        QC_RETURN_IF(H[l] == 0 || W[l] == 0, QC_ERR_INVALID_ARGUMENT, "%s: empty plane at level %d", who, l);
+        QC_RETURN_IF(!grids[l] || !outs[l], QC_ERR_INVALID_ARGUMENT, "%s: null pointer at level %d", who, l);
+        vec = vec && aligned16(grids[l]) && aligned16(outs[l]);
+    }
+    QC_RETURN_IF(!d_pts || !d_R, QC_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+    if (!vec) {  // per-level launches of the general kernels
+        for (int l = 0; l < n; ++l)
+            if (int st = forward<1>(who, d_pts, d_R, grids[l], outs[l], B, T, C, H[l], W[l], 0.f, stream))
+                return st;
+        return 0;
+    }
+    LevelTable tab{};
+    for (int l = 0; l < n; ++l) {
+        tab.grid[l] = grids[l];
+        tab.out[l] = outs[l];
+        tab.H[l] = H[l];
+        tab.W[l] = W[l];
+    }
+    switch (C / 4) {
+        case 1: return fwd_levels<1>(d_pts, d_R, tab, n, B, T, stream);
+        case 2: return fwd_levels<2>(d_pts, d_R, tab, n, B, T, stream);
+        case 4: return fwd_levels<4>(d_pts, d_R, tab, n, B, T, stream);
+        case 8: return fwd_levels<8>(d_pts, d_R, tab, n, B, T, stream);
+        case 16: return fwd_levels<16>(d_pts, d_R, tab, n, B, T, stream);
+        case 32: return fwd_levels<32>(d_pts, d_R, tab, n, B, T, stream);
+        default: break;
+    }
+    for (int l = 0; l < n; ++l)
+        if (int st = forward<1>(who, d_pts, d_R, grids[l], outs[l], B, T, C, H[l], W[l], 0.f, stream))
+            return st;
+    return 0;
+}
+
+int backward_levels(const float *d_pts, const float *d_R, int n, const float *const *grids,
+                    const float *const *gouts, float *const *ggrids, const int *H, const int *W,
+                    float *d_gR, float *d_gpts, long B, int T, int C, cudaStream_t stream) {
+    QC_NVTX("quantem::kplanes_bwd_levels");
+    const char *who = "kplanes_tilted_fuse_levels_grad_cuda";
+    if (int st = check_levels(who, n, grids, gouts, H, W, B, T, C)) return st;
+    QC_RETURN_IF(ggrids == nullptr, QC_ERR_INVALID_ARGUMENT, "%s: null level table", who);
+    if (B == 0 || T == 0 || C == 0) return 0;
+    bool vec = (C % 4 == 0) && C <= 128;
+    for (int l = 0; l < n; ++l) {
+        QC_RETURN_IF(H[l] == 0 || W[l] == 0, QC_ERR_INVALID_ARGUMENT, "%s: empty plane at level %d", who, l);
+        QC_RETURN_IF(!grids[l] || !gouts[l] || !ggrids[l], QC_ERR_INVALID_ARGUMENT,
+                     "%s: null pointer at level %d", who, l);
+        vec = vec && aligned16(grids[l]) && aligned16(gouts[l]) && aligned16(ggrids[l]);
+    }
+    QC_RETURN_IF(!d_pts || !d_R || !d_gR || !d_gpts, QC_ERR_INVALID_ARGUMENT, "%s: null pointer", who);
+    const bool fast = vec && (C / 4 == 1 || C / 4 == 2 || C / 4 == 4 || C / 4 == 8 || C / 4 == 16 ||
+                              C / 4 == 32);
+    if (!fast) {
+        for (int l = 0; l < n; ++l)
+            if (int st = backward<1>(who, d_pts, d_R, grids[l], gouts[l], ggrids[l], d_gR, d_gpts, B, T, C,
+                                     H[l], W[l], 0, T, 0.f, stream))
+                return st;
+        return 0;
+    }
+    LevelTable tab{};
+    for (int l = 0; l < n; ++l) {
+        tab.grid[l] = grids[l];
+        tab.gout[l] = gouts[l];
+        tab.ggrid[l] = ggrids[l];
+        tab.H[l] = H[l];
+        tab.W[l] = W[l];
+    }
+    switch (C / 4) {
+        case 1: return bwd_levels<1>(d_pts, d_R, tab, n, d_gR, d_gpts, B, T, stream);
+        case 2: return bwd_levels<2>(d_pts, d_R, tab, n, d_gR, d_gpts, B, T, stream);
+        case 4: return bwd_levels<4>(d_pts, d_R, tab, n, d_gR, d_gpts, B, T, stream);
+        case 8: return bwd_levels<8>(d_pts, d_R, tab, n, d_gR, d_gpts, B, T, stream);
+        case 16: return bwd_levels<16>(d_pts, d_R, tab, n, d_gR, d_gpts, B, T, stream);
+        default: return bwd_levels<32>(d_pts, d_R, tab, n, d_gR, d_gpts, B, T, stream);
+    }
+}
+
 }  // namespace kp
 
 int kp_fault_word(unsigned int *word, int clear) {
@@ -846,6 +1015,21 @@ int kplanes_tilted_fuse_grad_cuda(const float *d_pts, const float *d_R, const fl
     return kplanes_tilted_fuse_grad_rotations_cuda(d_pts, d_R, d_grid, d_gout, d_ggrid, d_gR,
                                                    d_gpts, B, T, C, H, W, 0, T < 0 ? 0 : T,
                                                    stream);
+}
+
+int kplanes_tilted_fuse_levels_cuda(const float *d_pts, const float *d_R, int n_levels,
+                                    const float *const *grids, float *const *outs, const int *H,
+                                    const int *W, long B, int T, int C, cudaStream_t stream) {
+    return qc::kp::forward_levels(d_pts, d_R, n_levels, grids, outs, H, W, B, T, C, stream);
+}
+
+int kplanes_tilted_fuse_levels_grad_cuda(const float *d_pts, const float *d_R, int n_levels,
+                                         const float *const *grids, const float *const *gouts,
+                                         float *const *ggrids, const int *H, const int *W,
+                                         float *d_gR, float *d_gpts, long B, int T, int C,
+                                         cudaStream_t stream) {
+    return qc::kp::backward_levels(d_pts, d_R, n_levels, grids, gouts, ggrids, H, W, d_gR, d_gpts,
+                                   B, T, C, stream);
 }
 
 int kplanes_planes_to_channels_last_cuda(const float *d_src, float *d_dst, int P, int C, int H,

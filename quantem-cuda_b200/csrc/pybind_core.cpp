@@ -281,6 +281,58 @@ PYBIND11_MODULE(_core, m) {
         py::arg("C"), py::arg("H"), py::arg("W"), py::arg("h"), py::arg("stream_ptr"));
 
     m.def(
+        "kplanes_tilted_fuse_levels_cuda",
+        [](uintptr_t pts, uintptr_t r, const std::vector<uintptr_t> &grids,
+           const std::vector<uintptr_t> &outs, const std::vector<int> &H, const std::vector<int> &W,
+           long B, int T, int C, uintptr_t stream) {
+            const size_t n = grids.size();
+            if (outs.size() != n || H.size() != n || W.size() != n)
+                throw std::invalid_argument("kplanes_tilted_fuse_levels_cuda: one grid, output, H and W per level");
+            std::vector<const float *> g(n);
+            std::vector<float *> o(n);
+            for (size_t l = 0; l < n; ++l) {
+                g[l] = ptr<const float>(grids[l]);
+                o[l] = ptr<float>(outs[l]);
+            }
+            check(kplanes_tilted_fuse_levels_cuda(ptr<const float>(pts), ptr<const float>(r), (int)n,
+                                                  g.data(), o.data(), H.data(), W.data(), B, T, C,
+                                                  stream_of(stream)));
+        },
+        "Several levels of a multiscale tilted K-Planes encoding in one launch.",
+        py::arg("pts_ptr"), py::arg("r_ptr"), py::arg("grid_ptrs"), py::arg("out_ptrs"), py::arg("H"),
+        py::arg("W"), py::arg("B"), py::arg("T"), py::arg("C"), py::arg("stream_ptr"));
+
+    m.def(
+        "kplanes_tilted_fuse_levels_grad_cuda",
+        [](uintptr_t pts, uintptr_t r, const std::vector<uintptr_t> &grids,
+           const std::vector<uintptr_t> &gouts, const std::vector<uintptr_t> &ggrids,
+           const std::vector<int> &H, const std::vector<int> &W, uintptr_t gr, uintptr_t gpts, long B,
+           int T, int C, uintptr_t stream) {
+            const size_t n = grids.size();
+            if (gouts.size() != n || ggrids.size() != n || H.size() != n || W.size() != n)
+                throw std::invalid_argument(
+                    "kplanes_tilted_fuse_levels_grad_cuda: one grid, upstream gradient, plane gradient, "
+                    "H and W per level");
+            std::vector<const float *> g(n), go(n);
+            std::vector<float *> gg(n);
+            for (size_t l = 0; l < n; ++l) {
+                g[l] = ptr<const float>(grids[l]);
+                go[l] = ptr<const float>(gouts[l]);
+                gg[l] = ptr<float>(ggrids[l]);
+            }
+            check(kplanes_tilted_fuse_levels_grad_cuda(ptr<const float>(pts), ptr<const float>(r), (int)n,
+                                                       g.data(), go.data(), gg.data(), H.data(), W.data(),
+                                                       ptr<float>(gr), ptr<float>(gpts), B, T, C,
+                                                       stream_of(stream)));
+        },
+        "Backward of kplanes_tilted_fuse_levels_cuda: ggrids per level, gr and gpts summed over levels "
+        "(all accumulated into).",
+        py::arg("pts_ptr"), py::arg("r_ptr"), py::arg("grid_ptrs"), py::arg("gout_ptrs"),
+        py::arg("ggrid_ptrs"), py::arg("H"), py::arg("W"), py::arg("gr_ptr"), py::arg("gpts_ptr"),
+        py::arg("B"), py::arg("T"), py::arg("C"), py::arg("stream_ptr"));
+    m.attr("KP_MAX_LEVELS") = QC_KP_MAX_LEVELS;
+
+    m.def(
         "kplanes_tilted_fuse_grad_rotations_cuda",
         [](uintptr_t pts, uintptr_t r, uintptr_t grid, uintptr_t gout, uintptr_t ggrid,
            uintptr_t gr, uintptr_t gpts, long B, int T, int C, int H, int W, int t_begin,

@@ -158,6 +158,102 @@ def _kpt_backward(ctx, grad_out):
 _kplanes_tilted_fuse.register_autograd(_kpt_backward, setup_context=_kpt_setup_context)
 
 
+# ── several levels in one launch ──────────────────────────────────────────
+#
+# A multiscale encoder samples the same points under the same rotations at
+# every level (each level's planes at their own resolution). One launch per
+# pass covers all levels: level l's output is kplanes_tilted_fuse(pts,
+# rotations, planes[l]) bit for bit, and the backward adds every level's
+# point and rotation gradients into one sum.
+
+
+def _check_levels(fn: str, pts: Tensor, rotations: Tensor, planes: list[Tensor],
+                  grad_outs: list[Tensor] | None = None) -> None:
+    if not 1 <= len(planes) <= _core.KP_MAX_LEVELS:
+        raise ValueError(f"{fn}: 1 to {_core.KP_MAX_LEVELS} levels, got {len(planes)}")
+    c = planes[0].shape[1] if planes[0].ndim == 4 else -1
+    for lv, plane in enumerate(planes):
+        _check_kernel_inputs(fn, pts, rotations, plane,
+                             None if grad_outs is None else grad_outs[lv])
+        if plane.shape[1] != c:
+            raise ValueError(f"{fn}: every level needs the same channel count C, got {c} and "
+                             f"{plane.shape[1]} (level {lv})")
+    if grad_outs is not None and len(grad_outs) != len(planes):
+        raise ValueError(f"{fn}: one grad_out per level, got {len(grad_outs)} for {len(planes)} levels")
+
+
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse_levels", mutates_args=())
+def _kplanes_tilted_fuse_levels(pts: Tensor, rotations: Tensor, planes: list[Tensor]) -> list[Tensor]:
+    _check_levels("kplanes_tilted_fuse_levels", pts, rotations, planes)
+    p = pts.contiguous()
+    r = rotations.contiguous()
+    b, t = p.shape[0], r.shape[0]
+    c = planes[0].shape[1]
+    stream = _stream(p.device)
+    with torch.cuda.device(p.device):
+        grids = [_channels_last(plane, stream) for plane in planes]
+        outs = [torch.empty((b, t * c), dtype=torch.float32, device=p.device) for _ in planes]
+        _core.kplanes_tilted_fuse_levels_cuda(
+            p.data_ptr(), r.data_ptr(), [g.data_ptr() for g in grids], [o.data_ptr() for o in outs],
+            [pl.shape[2] for pl in planes], [pl.shape[3] for pl in planes], b, t, c, stream,
+        )
+    return outs
+
+
+@_kplanes_tilted_fuse_levels.register_fake
+def _(pts: Tensor, rotations: Tensor, planes: list[Tensor]) -> list[Tensor]:
+    return [pts.new_empty((pts.shape[0], rotations.shape[0] * pl.shape[1])) for pl in planes]
+
+
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse_levels_bwd", mutates_args=())
+def _kplanes_tilted_fuse_levels_bwd(
+    pts: Tensor, rotations: Tensor, planes: list[Tensor], grad_outs: list[Tensor]
+) -> list[Tensor]:
+    """[grad_pts, grad_rotations, grad_plane_0, ..., grad_plane_{L-1}]"""
+    _check_levels("kplanes_tilted_fuse_levels_bwd", pts, rotations, planes, grad_outs)
+    p = pts.contiguous()
+    r = rotations.contiguous()
+    b, t = p.shape[0], r.shape[0]
+    c = planes[0].shape[1]
+    stream = _stream(p.device)
+    with torch.cuda.device(p.device):
+        grids = [_channels_last(plane, stream) for plane in planes]
+        gouts = [go.detach().to(dtype=torch.float32, device=p.device).contiguous() for go in grad_outs]
+        grad_pts = torch.zeros_like(p)
+        grad_r = torch.zeros_like(r)
+        grads_cl = [torch.zeros(g.shape, dtype=torch.float32, device=p.device) for g in grids]
+        _core.kplanes_tilted_fuse_levels_grad_cuda(
+            p.data_ptr(), r.data_ptr(), [g.data_ptr() for g in grids], [go.data_ptr() for go in gouts],
+            [gc.data_ptr() for gc in grads_cl], [pl.shape[2] for pl in planes], [pl.shape[3] for pl in planes],
+            grad_r.data_ptr(), grad_pts.data_ptr(), b, t, c, stream,
+        )
+        grad_planes = [_from_channels_last(gc, pl, stream) for gc, pl in zip(grads_cl, planes)]
+    return [grad_pts, grad_r, *grad_planes]
+
+
+@_kplanes_tilted_fuse_levels_bwd.register_fake
+def _(pts: Tensor, rotations: Tensor, planes: list[Tensor], grad_outs: list[Tensor]) -> list[Tensor]:
+    return [torch.empty_like(pts), torch.empty_like(rotations), *[torch.empty_like(pl) for pl in planes]]
+
+
+def _kpl_setup_context(ctx, inputs, output) -> None:
+    pts, rotations, planes = inputs
+    ctx.n_levels = len(planes)
+    ctx.save_for_backward(pts, rotations, *planes)
+
+
+def _kpl_backward(ctx, grad_outs):
+    pts, rotations, *planes = ctx.saved_tensors
+    gouts = [go if go is not None else torch.zeros((pts.shape[0], rotations.shape[0] * pl.shape[1]),
+                                                   dtype=torch.float32, device=pts.device)
+             for go, pl in zip(grad_outs, planes)]
+    grad_pts, grad_r, *grad_planes = _kplanes_tilted_fuse_levels_bwd(pts, rotations, planes, gouts)
+    return grad_pts, grad_r, grad_planes
+
+
+_kplanes_tilted_fuse_levels.register_autograd(_kpl_backward, setup_context=_kpl_setup_context)
+
+
 # ── four-tap variant for finite-difference TV regularisation ──────────────
 #
 # The reference's kplanes_tilted_tv_fuse (core/ml/_ops.py:103-204): tap 0 at
@@ -285,6 +381,22 @@ def kplanes_tilted_fuse(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor
     """
     _validate("kplanes_tilted_fuse", pts, rotations, plane)
     return _kplanes_tilted_fuse(pts, rotations, plane)
+
+
+def kplanes_tilted_fuse_levels(pts: Tensor, rotations: Tensor, planes: list[Tensor]) -> list[Tensor]:
+    """:func:`kplanes_tilted_fuse` for every level of a multiscale encoding in
+    one launch per pass: ``planes[l]`` is level ``l``'s ``[3*T, C, H_l, W_l]``
+    plane tensor (same ``T`` and ``C`` at every level, any resolution), and
+    the result is the list of the levels' ``[B, T*C]`` features, each equal
+    bit for bit to ``kplanes_tilted_fuse(pts, rotations, planes[l])``.
+    Differentiable w.r.t. ``pts``, ``rotations`` and every plane tensor; the
+    backward is one launch for all levels as well. At most 8 levels."""
+    planes = list(planes)
+    if not planes:
+        raise ValueError("kplanes_tilted_fuse_levels expects at least one level")
+    for plane in planes:
+        _validate("kplanes_tilted_fuse_levels", pts, rotations, plane)
+    return _kplanes_tilted_fuse_levels(pts, rotations, planes)
 
 
 def kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:

@@ -554,3 +554,67 @@ def test_raw_ops_refuse_mismatched_buffers_before_launch():
     with pytest.raises(ValueError, match="all inputs must be on"):
         torch.ops.quantem_cuda.kplanes_tilted_fuse(p, r, g.cpu())
     torch.cuda.synchronize()
+
+
+# ── several levels in one launch (kplanes_tilted_fuse_levels) ────────────────
+
+# (N, T, C, resolutions): fast path at C = 32 and 8 with levels of different
+# (also non-square) sizes, and C = 5 (general per-level fallback)
+LEVEL_CONFIGS = [
+    (3000, 4, 32, [(16, 16), (32, 32), (64, 48)]),
+    (1500, 2, 8, [(9, 13), (33, 17)]),
+    (700, 3, 5, [(7, 9), (12, 12)]),
+]
+
+
+def _level_inputs(N, T, C, res, seed):
+    gen = torch.Generator().manual_seed(seed)
+    pts = torch.empty((N, 3)).uniform_(-1.1, 1.1, generator=gen)
+    rot = torch.empty((T, 3, 3)).uniform_(-1.0, 1.0, generator=gen)
+    planes = [torch.empty((3 * T, C, h, w)).uniform_(0.1, 0.5, generator=gen) for h, w in res]
+    ups = [torch.randn((N, T * C), generator=gen) for _ in res]
+    return pts, rot, planes, ups
+
+
+@pytest.mark.parametrize("cfg", LEVEL_CONFIGS, ids=["c32x3", "c8x2", "c5x2"])
+def test_levels_in_one_launch_match_single_level_ops_and_oracle(cfg):
+    from quantem.cuda.core.ml import kplanes_tilted_fuse_levels
+
+    N, T, C, res = cfg
+    pts, rot, planes, ups = _level_inputs(N, T, C, res, seed=71)
+    p = pts.cuda().requires_grad_(True)
+    r = rot.cuda().requires_grad_(True)
+    pls = [pl.cuda().requires_grad_(True) for pl in planes]
+    outs = kplanes_tilted_fuse_levels(p, r, pls)
+    sum(((o * u.cuda()).sum() for o, u in zip(outs, ups))).backward()
+    o_gp = np.zeros_like(pts.numpy(), dtype=np.float64)
+    o_gr = np.zeros_like(rot.numpy(), dtype=np.float64)
+    for lv, (out, pl, up) in enumerate(zip(outs, planes, ups)):
+        single = kplanes_tilted_fuse(pts.cuda(), rot.cuda(), pl.cuda())
+        assert torch.equal(out.detach(), single), f"level {lv} differs from the single-level op"
+        ref = oracle.kplanes_fwd(pts.numpy(), rot.numpy(), pl.numpy())
+        assert np.array_equal(out.detach().cpu().numpy(), ref), f"level {lv} differs from the oracle"
+        gp, gr, gg = oracle.kplanes_bwd(pts.numpy(), rot.numpy(), pl.numpy(), up.numpy())
+        assert_rel_max(pls[lv].grad, gg, 1e-4, f"grad_plane level {lv}")
+        assert_rel_elementwise(pls[lv].grad, gg, f"grad_plane level {lv}")
+        o_gp += gp
+        o_gr += gr
+    assert_rel_max(p.grad, o_gp, 1e-4, "grad_pts (sum over levels)")
+    assert_rel_elementwise(p.grad, o_gp, "grad_pts (sum over levels)")
+    assert_rel_max(r.grad, o_gr, 1e-4, "grad_rotations (sum over levels)")
+
+
+def test_levels_validation():
+    from quantem.cuda.core.ml import kplanes_tilted_fuse_levels
+
+    pts, rot, planes, ups = _level_inputs(64, 2, 8, [(9, 9), (5, 7)], seed=72)
+    p, r = pts.cuda(), rot.cuda()
+    g = [pl.cuda() for pl in planes]
+    with pytest.raises(ValueError, match="same channel count"):
+        kplanes_tilted_fuse_levels(p, r, [g[0], g[1][:, :4].contiguous()])
+    with pytest.raises(ValueError, match="1 to 8 levels"):
+        torch.ops.quantem_cuda.kplanes_tilted_fuse_levels(p, r, g * 5)
+    with pytest.raises(ValueError, match="3\\*T"):
+        kplanes_tilted_fuse_levels(p, r, [g[0], g[1][:3]])
+    with pytest.raises(ValueError, match="grad_out must have shape"):
+        torch.ops.quantem_cuda.kplanes_tilted_fuse_levels_bwd(p, r, g, [u.cuda()[:, :3] for u in ups])
