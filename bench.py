@@ -290,6 +290,19 @@ def time_steps(ctx: Ctx, step, steps: int, warmup: int, sampler: ClockSampler | 
     return ctx.max_over_ranks(ms)
 
 
+def time_with_op_events(ctx: Ctx, step, steps: int, warmup: int, timers, sampler=None) -> float:
+    """The timed pass (K steps, no events between the ops; its duration is
+    returned), then a second pass of K steps with each timer's events around
+    its op, which is where the per-op durations of the line come from."""
+    for t in timers:
+        t.enabled = False
+    ms = time_steps(ctx, step, steps, warmup, sampler)
+    for t in timers:
+        t.enabled = True
+    time_steps(ctx, step, steps, 0)
+    return ms
+
+
 def time_pipelined(ctx: Ctx, step, steps: int, warmup: int, side_streams) -> float:
     """time_steps for steps whose copies run on side streams: the end event
     is recorded once the compute stream has waited for every side stream, so
@@ -313,13 +326,20 @@ def time_pipelined(ctx: Ctx, step, steps: int, warmup: int, side_streams) -> flo
 
 
 class KernelTimer:
-    """CUDA-event durations of one launch site inside the timed loop."""
+    """CUDA-event durations of one launch site (an op) of the step. Disabled
+    timers call straight through: events recorded between two ops would
+    separate a sweep from the kernel before it, which costs it the
+    programmatic-dependent-launch overlap, so the timed pass runs without them
+    and time_with_op_events() measures the ops in a second pass."""
 
     def __init__(self):
         self.pairs = []
+        self.enabled = True
 
     def wrap(self, fn):
         def run(*a, **k):
+            if not self.enabled:
+                return fn(*a, **k)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             r = fn(*a, **k)
@@ -702,7 +722,7 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
             l1()
 
     sampler = ClockSampler(ctx.local_rank)
-    ms = time_steps(ctx, step, steps, warmup, sampler)
+    ms = time_with_op_events(ctx, step, steps, warmup, (t_iso, t_l1), sampler)
     ms_step = ms / steps
     iso_ms = t_iso.mean_ms(steps)
     l1_ms = t_l1.mean_ms(steps) if t_l1.pairs else None
@@ -851,7 +871,7 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
 
         t_one = KernelTimer()
         both = t_one.wrap(lambda: tv_loss_multi_3d_fwd_grad(vol, iso=g1, l1=g3, eps=1e-8))
-        one_ms = time_steps(ctx, both, steps, warmup) / steps
+        one_ms = time_with_op_events(ctx, both, steps, warmup, (t_one,)) / steps
         peak_, _ = measured_hbm_peak()
         one_sweep = {"value": voxels_local / (one_ms / 1e3), "unit": "voxels/s", "ms_per_step": one_ms,
                      "op_ms": t_one.mean_ms(steps),
@@ -890,6 +910,9 @@ def run_tv_iso_l1(ctx: Ctx, steps: int, warmup: int) -> dict:
             "parallelism": f"d-slab{ctx.world} ({ctx.args.tv_transport})" if ctx.world > 1 else "single GPU",
             "l2": "inputs larger than L2 (268 MB volume per GPU, 2 x 268 MB of gradients written per step)",
             "per_loss_ms": {"iso": iso_ms, "l1": l1_ms} if l1_ms is not None else {"iso_plus_l1": iso_ms},
+            "per_loss_ms_how": "CUDA events around each op in a second pass of the K steps (events between "
+                               "the ops of the timed pass would cost each sweep its overlap with the kernel "
+                               "before it)",
         },
         "roofline": {
             "bound": "hbm",
@@ -1032,7 +1055,7 @@ def run_tv_1024(ctx: Ctx, steps: int, warmup: int) -> dict:
         local_voxels = (ps.d_hi - ps.d_lo) * n * n
         launches = 3
     sampler = ClockSampler(ctx.local_rank)
-    ms = time_steps(ctx, step, steps, warmup, sampler)
+    ms = time_with_op_events(ctx, step, steps, warmup, (t_sq, t_iso), sampler)
     ms_step = ms / steps
     peak, peak_kind = measured_hbm_peak()
     if ctx.world == 1:
@@ -1112,7 +1135,7 @@ def run_kplanes_ms(ctx: Ctx, steps: int, warmup: int) -> dict:
             run()  # each level's output and gradients are released before the next
 
     sampler = ClockSampler(ctx.local_rank)
-    ms = time_steps(ctx, step, steps, warmup, sampler)
+    ms = time_with_op_events(ctx, step, steps, warmup, timers, sampler)
     ms_step = ms / steps
     if reducers is not None:
         for red in reducers:
@@ -1199,7 +1222,7 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
             fb()
 
     sampler = ClockSampler(ctx.local_rank)
-    ms = time_steps(ctx, step, steps, warmup, sampler)
+    ms = time_with_op_events(ctx, step, steps, warmup, (t_f, t_b), sampler)
     ms_step = ms / steps
     f_ms, b_ms = t_f.mean_ms(steps), t_b.mean_ms(steps)
     if ctx.world > 1:

@@ -53,7 +53,7 @@ def _run(
 ) -> None:
     b, d, h, w = vol.shape
     ws = _workspace(vol.device) if flags & _LOSS else None
-    with torch.cuda.device(vol.device):
+    with _on_device(vol.device):
         _core.tv_loss_3d_slab_cuda(
             variant,
             flags,
@@ -77,7 +77,39 @@ def _run(
         )
 
 
+class _NoContext:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_CONTEXT = _NoContext()
+
+
+def _on_device(device: torch.device):
+    """torch.cuda.device(device), or nothing when it is already current (the
+    context manager costs host time on every call)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return _NO_CONTEXT
+    return torch.cuda.device(device)
+
+
+def _eager(x: Tensor) -> bool:
+    """True for a plain tensor outside torch.compile: the public wrappers of
+    the single-sweep ops then call their implementation directly instead of
+    through the torch.library dispatcher, whose Python-side cost per call
+    (about 60 us) is comparable to a sweep's device time on small volumes.
+    Under compilation, and for tensor subclasses (fake tensors), the
+    registered op is used."""
+    return type(x) is torch.Tensor and not torch.compiler.is_compiling()
+
+
 def _upstream(grad_out: Tensor | float, n: int, device: torch.device) -> Tensor:
+    if (isinstance(grad_out, Tensor) and grad_out.dtype == torch.float32 and grad_out.device == device
+            and grad_out.numel() == n and grad_out.is_contiguous()):
+        return grad_out.detach().view(n)
     if isinstance(grad_out, Tensor):
         return grad_out.detach().to(dtype=torch.float32, device=device).reshape(n).contiguous()
     return torch.full((n,), float(grad_out), dtype=torch.float32, device=device)
@@ -218,8 +250,7 @@ _tv_loss_l1_3d.register_autograd(_l1_backward, setup_context=_l1_setup_context)
 # ── single-sweep forward + gradient ───────────────────────────────────────
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_iso_3d_fwd_grad", mutates_args=())
-def _tv_loss_iso_3d_fwd_grad(volume: Tensor, grad_out: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+def _iso_fwd_grad_impl(volume: Tensor, grad_out: Tensor, eps: float) -> tuple[Tensor, Tensor]:
     vol, b, d, h, w, stream = _launch_args(volume)
     g = _upstream(grad_out, 1, vol.device)
     acc = torch.empty(1, dtype=torch.float32, device=vol.device)
@@ -229,13 +260,17 @@ def _tv_loss_iso_3d_fwd_grad(volume: Tensor, grad_out: Tensor, eps: float) -> tu
     return acc.squeeze(0), grad_vol
 
 
+@torch.library.custom_op("quantem_cuda::tv_loss_iso_3d_fwd_grad", mutates_args=())
+def _tv_loss_iso_3d_fwd_grad(volume: Tensor, grad_out: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    return _iso_fwd_grad_impl(volume, grad_out, eps)
+
+
 @_tv_loss_iso_3d_fwd_grad.register_fake
 def _(volume: Tensor, grad_out: Tensor, eps: float) -> tuple[Tensor, Tensor]:
     return volume.new_empty(()), torch.empty_like(volume)
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_sq_3d_fwd_grad", mutates_args=())
-def _tv_loss_sq_3d_fwd_grad(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
+def _sq_fwd_grad_impl(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
     vol, b, d, h, w, stream = _launch_args(volume)
     g = _upstream(grad_out, 1, vol.device)
     acc = torch.empty(1, dtype=torch.float32, device=vol.device)
@@ -244,19 +279,28 @@ def _tv_loss_sq_3d_fwd_grad(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, T
     return acc.squeeze(0), grad_vol
 
 
+@torch.library.custom_op("quantem_cuda::tv_loss_sq_3d_fwd_grad", mutates_args=())
+def _tv_loss_sq_3d_fwd_grad(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
+    return _sq_fwd_grad_impl(volume, grad_out)
+
+
 @_tv_loss_sq_3d_fwd_grad.register_fake
 def _(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
     return volume.new_empty(()), torch.empty_like(volume)
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_l1_3d_fwd_grad", mutates_args=())
-def _tv_loss_l1_3d_fwd_grad(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
+def _l1_fwd_grad_impl(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
     vol, b, d, h, w, stream = _launch_args(volume)
     g = _upstream(grad_out, 3, vol.device)
     acc = torch.empty(3, dtype=torch.float32, device=vol.device)
     grad_vol = torch.empty_like(vol)
     _run(_L1, _LOSS | _GRAD | _OVERWRITE, vol, g, acc, grad_vol, 0.0, 1.0, stream)
     return acc, grad_vol
+
+
+@torch.library.custom_op("quantem_cuda::tv_loss_l1_3d_fwd_grad", mutates_args=())
+def _tv_loss_l1_3d_fwd_grad(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
+    return _l1_fwd_grad_impl(volume, grad_out)
 
 
 @_tv_loss_l1_3d_fwd_grad.register_fake
@@ -269,8 +313,7 @@ def _(volume: Tensor, grad_out: Tensor) -> tuple[Tensor, Tensor]:
 _TERM_SQ, _TERM_ISO, _TERM_L1 = _core.TV_TERM_SQ, _core.TV_TERM_ISO, _core.TV_TERM_L1
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_multi_3d_fwd_grad", mutates_args=())
-def _tv_loss_multi_3d_fwd_grad(volume: Tensor, weights: Tensor, terms: int, eps: float) -> tuple[Tensor, Tensor]:
+def _multi_fwd_grad_impl(volume: Tensor, weights: Tensor, terms: int, eps: float) -> tuple[Tensor, Tensor]:
     """weights = [w_sq, w_iso, w_d, w_h, w_w]; returns ([sq sum, iso mean, l1_d,
     l1_h, l1_w], Σ_term w·∂term/∂volume) for the terms in the bit mask."""
     vol, b, d, h, w, stream = _launch_args(volume)
@@ -279,12 +322,17 @@ def _tv_loss_multi_3d_fwd_grad(volume: Tensor, weights: Tensor, terms: int, eps:
     acc = torch.empty(5, dtype=torch.float32, device=vol.device)
     grad_vol = torch.empty_like(vol)
     ws = _workspace(vol.device)
-    with torch.cuda.device(vol.device):
+    with _on_device(vol.device):
         _core.tv_loss_mix_3d_fwd_grad_cuda(
             int(terms), _OVERWRITE, vol.data_ptr(), g.data_ptr(), acc.data_ptr(), grad_vol.data_ptr(),
             b, d, h, w, float(eps), 1.0 / n, ws.data_ptr(), ws.numel(), stream,
         )
     return acc, grad_vol
+
+
+@torch.library.custom_op("quantem_cuda::tv_loss_multi_3d_fwd_grad", mutates_args=())
+def _tv_loss_multi_3d_fwd_grad(volume: Tensor, weights: Tensor, terms: int, eps: float) -> tuple[Tensor, Tensor]:
+    return _multi_fwd_grad_impl(volume, weights, terms, eps)
 
 
 @_tv_loss_multi_3d_fwd_grad.register_fake
@@ -364,14 +412,16 @@ def tv_loss_iso_3d_fwd_grad(
     ``grad`` shaped like ``volume``. Not differentiable itself.
     """
     vol = _as_batched(volume, "tv_loss_iso_3d_fwd_grad")
-    loss, grad = _tv_loss_iso_3d_fwd_grad(vol, _upstream(grad_out, 1, vol.device), float(eps))
+    op = _iso_fwd_grad_impl if _eager(vol) else _tv_loss_iso_3d_fwd_grad
+    loss, grad = op(vol, _upstream(grad_out, 1, vol.device), float(eps))
     return loss, grad.view(volume.shape)
 
 
 def tv_loss_sq_3d_fwd_grad(volume: Tensor, grad_out: Tensor | float = 1.0) -> tuple[Tensor, Tensor]:
     """Squared TV sum and ``grad_out · ∂sum/∂volume`` in one HBM sweep."""
     vol = _as_batched(volume, "tv_loss_sq_3d_fwd_grad")
-    loss, grad = _tv_loss_sq_3d_fwd_grad(vol, _upstream(grad_out, 1, vol.device))
+    op = _sq_fwd_grad_impl if _eager(vol) else _tv_loss_sq_3d_fwd_grad
+    loss, grad = op(vol, _upstream(grad_out, 1, vol.device))
     return loss, grad.view(volume.shape)
 
 
@@ -389,7 +439,8 @@ def tv_loss_l1_3d_fwd_grad(
     else:
         g = float(grad_out)
     g = _upstream(g, 3, vol.device)
-    sums, grad = _tv_loss_l1_3d_fwd_grad(vol, g)
+    op = _l1_fwd_grad_impl if _eager(vol) else _tv_loss_l1_3d_fwd_grad
+    sums, grad = op(vol, g)
     return sums, grad.view(volume.shape)
 
 
@@ -440,13 +491,17 @@ def tv_loss_multi_3d_fwd_grad(
     if terms == 0:
         raise ValueError("tv_loss_multi_3d_fwd_grad needs at least one of sq, iso, l1")
     if terms in (_TERM_SQ, _TERM_ISO, _TERM_L1):
+        eager = _eager(vol)
         if terms == _TERM_SQ:
-            loss, grad = _tv_loss_sq_3d_fwd_grad(vol, _weight(sq, 1, dev))
+            op = _sq_fwd_grad_impl if eager else _tv_loss_sq_3d_fwd_grad
+            loss, grad = op(vol, _weight(sq, 1, dev))
             return {"sq": loss}, grad.view(volume.shape)
         if terms == _TERM_ISO:
-            loss, grad = _tv_loss_iso_3d_fwd_grad(vol, _weight(iso, 1, dev), float(eps))
+            op = _iso_fwd_grad_impl if eager else _tv_loss_iso_3d_fwd_grad
+            loss, grad = op(vol, _weight(iso, 1, dev), float(eps))
             return {"iso": loss}, grad.view(volume.shape)
-        sums, grad = _tv_loss_l1_3d_fwd_grad(vol, _weight(l1, 3, dev))
+        op = _l1_fwd_grad_impl if eager else _tv_loss_l1_3d_fwd_grad
+        sums, grad = op(vol, _weight(l1, 3, dev))
         return {"l1": sums}, grad.view(volume.shape)
     zero1 = torch.zeros(1, dtype=torch.float32, device=dev)
     weights = torch.cat([
@@ -454,7 +509,8 @@ def tv_loss_multi_3d_fwd_grad(
         _weight(iso, 1, dev) if iso is not None else zero1,
         _weight(l1, 3, dev) if l1 is not None else zero1.expand(3),
     ])
-    acc, grad = _tv_loss_multi_3d_fwd_grad(vol, weights, terms, float(eps))
+    op = _multi_fwd_grad_impl if _eager(vol) else _tv_loss_multi_3d_fwd_grad
+    acc, grad = op(vol, weights, terms, float(eps))
     losses = {}
     if sq is not None:
         losses["sq"] = acc[0]
