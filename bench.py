@@ -1058,10 +1058,19 @@ def run_tv_1024(ctx: Ctx, steps: int, warmup: int) -> dict:
     ms = time_with_op_events(ctx, step, steps, warmup, (t_sq, t_iso), sampler)
     ms_step = ms / steps
     peak, peak_kind = measured_hbm_peak()
+    one_sweep = None
     if ctx.world == 1:
         per_loss = {"sq": t_sq.mean_ms(steps), "iso": t_iso.mean_ms(steps)}
         dom_ms = max(per_loss.values())
         kernel = "tv single sweep (the slower of sq and iso)"
+        # both terms and their summed gradient from one sweep
+        from quantem.cuda.core import tv_loss_multi_3d_fwd_grad
+
+        one_ms = time_steps(ctx, lambda: tv_loss_multi_3d_fwd_grad(vol, sq=g1, iso=g1, eps=1e-8), steps,
+                            min(warmup, 3)) / steps
+        one_sweep = {"value": n ** 3 / (one_ms / 1e3), "unit": "voxels/s", "ms_per_step": one_ms,
+                     "roofline_frac": 8.0 * local_voxels / (one_ms / 1e3) / 1e9 / peak,
+                     "what": "sq + iso losses and their summed gradient in one sweep (tv_loss_multi_3d_fwd_grad)"}
     else:
         per_loss = {"sq_plus_iso": t_sq.mean_ms(steps)}
         dom_ms = per_loss["sq_plus_iso"] / 2
@@ -1079,7 +1088,8 @@ def run_tv_1024(ctx: Ctx, steps: int, warmup: int) -> dict:
                    "global_shape": [n, n, n],
                    "parallelism": f"d-slab{ctx.world} (peer)" if ctx.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (4 GiB volume)",
-                   "per_loss_ms": per_loss},
+                   "per_loss_ms": per_loss,
+                   "one_sweep": one_sweep},
         "roofline": {"bound": "hbm", "kernel": kernel, "achieved": algo / (dom_ms / 1e3) / 1e9,
                      "peak": peak, "peak_kind": f"{peak_kind} HBM copy bandwidth", "unit": "GB/s",
                      "frac": algo / (dom_ms / 1e3) / 1e9 / peak, "traffic": None, "algorithmic_bytes": algo},
