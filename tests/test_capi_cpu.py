@@ -78,6 +78,19 @@ def test_argument_errors_need_no_device():
     r.restype = ctypes.c_int
     r.argtypes = [vp, vp, i, i, i, i, vp]
     assert r(vp(16), vp(16), -1, 4, 4, 4, None) == 10001
+    # the multi-level K-Planes entries check their level tables before any CUDA call
+    lv = lib.kplanes_tilted_fuse_levels_cuda
+    lv.restype = ctypes.c_int
+    lv.argtypes = [vp, vp, i, ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.POINTER(i), ctypes.POINTER(i),
+                   ctypes.c_long, i, i, vp]
+    grids = (vp * 9)(*([16] * 9))
+    hs = (i * 9)(*([8] * 9))
+    assert lv(vp(16), vp(16), 0, grids, grids, hs, hs, 4, 2, 8, None) == 10001
+    assert lv(vp(16), vp(16), 9, grids, grids, hs, hs, 4, 2, 8, None) == 10001
+    assert b"levels" in lib.quantem_cuda_last_error()
+    assert lv(vp(16), vp(16), 2, None, grids, hs, hs, 4, 2, 8, None) == 10001
+    big = (i * 2)(1 << 16, 1 << 16)
+    assert lv(vp(16), vp(16), 2, grids, grids, big, big, 4, 2, 8, None) == 10001  # C*H*W >= 2^31
     # a mixed sweep needs two or three terms
     mx = lib.tv_loss_mix_3d_fwd_grad_cuda
     mx.restype = ctypes.c_int
