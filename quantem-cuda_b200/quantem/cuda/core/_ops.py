@@ -118,8 +118,7 @@ def _upstream(grad_out: Tensor | float, n: int, device: torch.device) -> Tensor:
 # ── isotropic 3-D TV ──────────────────────────────────────────────────────
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_iso_3d", mutates_args=())
-def _tv_loss_iso_3d(volume: Tensor, eps: float) -> Tensor:
+def _iso_fwd_impl(volume: Tensor, eps: float) -> Tensor:
     vol, b, d, h, w, stream = _launch_args(volume)
     acc = torch.empty(1, dtype=torch.float32, device=vol.device)
     scale = 1.0 / float(_iso_n_corners(vol.shape))
@@ -127,19 +126,28 @@ def _tv_loss_iso_3d(volume: Tensor, eps: float) -> Tensor:
     return acc.squeeze(0)
 
 
+@torch.library.custom_op("quantem_cuda::tv_loss_iso_3d", mutates_args=())
+def _tv_loss_iso_3d(volume: Tensor, eps: float) -> Tensor:
+    return _iso_fwd_impl(volume, eps)
+
+
 @_tv_loss_iso_3d.register_fake
 def _(volume: Tensor, eps: float) -> Tensor:
     return volume.new_empty(())
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_iso_3d_bwd", mutates_args=())
-def _tv_loss_iso_3d_bwd(volume: Tensor, grad_out: Tensor, eps: float) -> Tensor:
+def _iso_bwd_impl(volume: Tensor, grad_out: Tensor, eps: float) -> Tensor:
     vol, b, d, h, w, stream = _launch_args(volume)
     g = _upstream(grad_out, 1, vol.device)
     grad_vol = torch.empty_like(vol)
     scale = 1.0 / float(_iso_n_corners(vol.shape))
     _run(_ISO, _GRAD, vol, g, None, grad_vol, eps, scale, stream)
     return grad_vol
+
+
+@torch.library.custom_op("quantem_cuda::tv_loss_iso_3d_bwd", mutates_args=())
+def _tv_loss_iso_3d_bwd(volume: Tensor, grad_out: Tensor, eps: float) -> Tensor:
+    return _iso_bwd_impl(volume, grad_out, eps)
 
 
 @_tv_loss_iso_3d_bwd.register_fake
@@ -164,12 +172,16 @@ _tv_loss_iso_3d.register_autograd(_iso_backward, setup_context=_iso_setup_contex
 # ── squared-anisotropic 3-D TV (quantem tv_vol parity) ────────────────────
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_sq_3d", mutates_args=())
-def _tv_loss_sq_3d(volume: Tensor) -> Tensor:
+def _sq_fwd_impl(volume: Tensor) -> Tensor:
     vol, b, d, h, w, stream = _launch_args(volume)
     acc = torch.empty(1, dtype=torch.float32, device=vol.device)
     _run(_SQ, _LOSS | _OVERWRITE, vol, None, acc, None, 0.0, 1.0, stream)
     return acc.squeeze(0)
+
+
+@torch.library.custom_op("quantem_cuda::tv_loss_sq_3d", mutates_args=())
+def _tv_loss_sq_3d(volume: Tensor) -> Tensor:
+    return _sq_fwd_impl(volume)
 
 
 @_tv_loss_sq_3d.register_fake
@@ -177,13 +189,17 @@ def _(volume: Tensor) -> Tensor:
     return volume.new_empty(())
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_sq_3d_bwd", mutates_args=())
-def _tv_loss_sq_3d_bwd(volume: Tensor, grad_out: Tensor) -> Tensor:
+def _sq_bwd_impl(volume: Tensor, grad_out: Tensor) -> Tensor:
     vol, b, d, h, w, stream = _launch_args(volume)
     g = _upstream(grad_out, 1, vol.device)
     grad_vol = torch.empty_like(vol)
     _run(_SQ, _GRAD, vol, g, None, grad_vol, 0.0, 1.0, stream)
     return grad_vol
+
+
+@torch.library.custom_op("quantem_cuda::tv_loss_sq_3d_bwd", mutates_args=())
+def _tv_loss_sq_3d_bwd(volume: Tensor, grad_out: Tensor) -> Tensor:
+    return _sq_bwd_impl(volume, grad_out)
 
 
 @_tv_loss_sq_3d_bwd.register_fake
@@ -207,12 +223,16 @@ _tv_loss_sq_3d.register_autograd(_sq_backward, setup_context=_sq_setup_context)
 # ── L1-anisotropic 3-D TV (per-axis sums) ─────────────────────────────────
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_l1_3d", mutates_args=())
-def _tv_loss_l1_3d(volume: Tensor) -> Tensor:
+def _l1_fwd_impl(volume: Tensor) -> Tensor:
     vol, b, d, h, w, stream = _launch_args(volume)
     acc = torch.empty(3, dtype=torch.float32, device=vol.device)
     _run(_L1, _LOSS | _OVERWRITE, vol, None, acc, None, 0.0, 1.0, stream)
     return acc
+
+
+@torch.library.custom_op("quantem_cuda::tv_loss_l1_3d", mutates_args=())
+def _tv_loss_l1_3d(volume: Tensor) -> Tensor:
+    return _l1_fwd_impl(volume)
 
 
 @_tv_loss_l1_3d.register_fake
@@ -220,13 +240,17 @@ def _(volume: Tensor) -> Tensor:
     return volume.new_empty((3,))
 
 
-@torch.library.custom_op("quantem_cuda::tv_loss_l1_3d_bwd", mutates_args=())
-def _tv_loss_l1_3d_bwd(volume: Tensor, grad_out: Tensor) -> Tensor:
+def _l1_bwd_impl(volume: Tensor, grad_out: Tensor) -> Tensor:
     vol, b, d, h, w, stream = _launch_args(volume)
     g = _upstream(grad_out, 3, vol.device)
     grad_vol = torch.empty_like(vol)
     _run(_L1, _GRAD, vol, g, None, grad_vol, 0.0, 1.0, stream)
     return grad_vol
+
+
+@torch.library.custom_op("quantem_cuda::tv_loss_l1_3d_bwd", mutates_args=())
+def _tv_loss_l1_3d_bwd(volume: Tensor, grad_out: Tensor) -> Tensor:
+    return _l1_bwd_impl(volume, grad_out)
 
 
 @_tv_loss_l1_3d_bwd.register_fake
@@ -340,6 +364,56 @@ def _(volume: Tensor, weights: Tensor, terms: int, eps: float) -> tuple[Tensor, 
     return volume.new_empty((5,)), torch.empty_like(volume)
 
 
+# ── eager autograd ────────────────────────────────────────────────────────
+#
+# The same implementations under torch.autograd.Function, used by the public
+# wrappers for plain tensors outside torch.compile: the registered ops above
+# stay what torch.compile and torch.ops.quantem_cuda.* see, while an eager
+# call skips the torch.library dispatcher's host cost. Backward is
+# once-differentiable, as the registered ops' backward is not differentiable
+# either.
+
+
+class _IsoTV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, volume: Tensor, eps: float) -> Tensor:
+        ctx.save_for_backward(volume)
+        ctx.eps = eps
+        return _iso_fwd_impl(volume, eps)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad_out):
+        (volume,) = ctx.saved_tensors
+        return _iso_bwd_impl(volume, grad_out, ctx.eps), None
+
+
+class _SqTV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, volume: Tensor) -> Tensor:
+        ctx.save_for_backward(volume)
+        return _sq_fwd_impl(volume)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad_out):
+        (volume,) = ctx.saved_tensors
+        return _sq_bwd_impl(volume, grad_out)
+
+
+class _L1TV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, volume: Tensor) -> Tensor:
+        ctx.save_for_backward(volume)
+        return _l1_fwd_impl(volume)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad_out):
+        (volume,) = ctx.saved_tensors
+        return _l1_bwd_impl(volume, grad_out)
+
+
 # ── public wrappers ───────────────────────────────────────────────────────
 
 
@@ -360,7 +434,8 @@ def tv_loss_iso_3d(volume: Tensor, eps: float = 1e-8) -> Tensor:
     Returns:
         0-dim fp32 tensor on the same device as ``volume``; differentiable.
     """
-    return _tv_loss_iso_3d(_as_batched(volume, "tv_loss_iso_3d"), eps)
+    vol = _as_batched(volume, "tv_loss_iso_3d")
+    return _IsoTV.apply(vol, float(eps)) if _eager(vol) else _tv_loss_iso_3d(vol, eps)
 
 
 def tv_loss_sq_3d(volume: Tensor) -> Tensor:
@@ -379,7 +454,8 @@ def tv_loss_sq_3d(volume: Tensor) -> Tensor:
     Returns:
         0-dim fp32 tensor on the same device as ``volume``; differentiable.
     """
-    return _tv_loss_sq_3d(_as_batched(volume, "tv_loss_sq_3d"))
+    vol = _as_batched(volume, "tv_loss_sq_3d")
+    return _SqTV.apply(vol) if _eager(vol) else _tv_loss_sq_3d(vol)
 
 
 def tv_loss_l1_3d(volume: Tensor) -> Tensor:
@@ -400,7 +476,8 @@ def tv_loss_l1_3d(volume: Tensor) -> Tensor:
     Returns:
         Shape-``(3,)`` fp32 tensor on the same device; differentiable.
     """
-    return _tv_loss_l1_3d(_as_batched(volume, "tv_loss_l1_3d"))
+    vol = _as_batched(volume, "tv_loss_l1_3d")
+    return _L1TV.apply(vol) if _eager(vol) else _tv_loss_l1_3d(vol)
 
 
 def tv_loss_iso_3d_fwd_grad(
