@@ -571,6 +571,7 @@ def cpu_kplanes_ms(sample_n: int = 2048, min_seconds: float = 10.0, reps: int | 
 
 CPU_BASELINES = {
     "tv_iso_l1": cpu_tv_iso_l1,
+    "reference_suite": cpu_tv_iso_l1,
     "tv_multi": cpu_tv_iso_l1,
     "tv_sq_128": cpu_tv_sq_128,
     "tv_1024": cpu_tv_1024,
@@ -1461,9 +1462,199 @@ def kplanes_l2_ceiling(p, r, g, u, reps: int = 10) -> dict:
     }
 
 
+# ── the reference's own benchmark configurations ──────────────────────────
+
+
+def _ref_suite_time(fn, iters: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def _ray_points(n: int, dev, gen, samples_per_ray: int = 200) -> torch.Tensor:
+    """Points laid out like a tomography ray sampler: consecutive entries are
+    consecutive samples along one ray (a random (x, y), z from -1 to 1)."""
+    n_rays = n // samples_per_ray
+    xy = (torch.rand((n_rays, 1, 2), generator=gen) * 2 - 1).to(dev)
+    z = torch.linspace(-1, 1, samples_per_ray, device=dev).view(1, -1, 1)
+    return torch.cat([xy.expand(-1, samples_per_ray, -1), z.expand(n_rays, -1, -1)], dim=-1).reshape(-1, 3)
+
+
+def run_reference_suite(ctx: Ctx, steps: int, warmup: int) -> dict:
+    """The configurations of the reference's own benchmarks
+    (benchmarks/core/bench_tv_loss.py: 4 shapes x iso/sq/L1 x fwd, fwd+bwd
+    through the public ops and autograd; benchmarks/core/ml/bench_kplanes_tilted.py:
+    3 point sets, two of them ray-structured, x fwd, fwd+bwd), timed for this
+    build's public ops, for the reference's own sm_100a kernels driven with its
+    op layer's calls (no autograd around them), and for the pure-torch chains
+    the reference benchmarks compare against. Seeded synthetic inputs."""
+    from quantem.cuda.core import tv_loss_iso_3d, tv_loss_l1_3d, tv_loss_sq_3d
+    from quantem.cuda.core.ml import kplanes_tilted_fuse
+    from oracle import torch_ref
+
+    if ctx.world > 1:
+        raise SystemExit("reference_suite runs on one GPU")
+    dev = ctx.device
+    core, why = reference_core()
+    iters = max(steps, 5)
+    gen = torch.Generator().manual_seed(5)
+    rows = []
+
+    def l1_mean(sums, shape):
+        d, h, w = shape[-3:]
+        n = int(np.prod(shape)) // (d * h * w)
+        counts = sums.new_tensor([n * (d - 1) * h * w, n * d * (h - 1) * w, n * d * h * (w - 1)])
+        return (sums / counts).sum() / 3
+
+    def torch_l1(v):
+        v4 = v.reshape(-1, *v.shape[-3:])
+        return sum(torch.mean(torch.abs(v4.diff(dim=d))) for d in (1, 2, 3)) / 3
+
+    for shape in ((16, 1024, 1024), (256, 256, 256), (4, 256, 256, 256), (512, 512, 512)):
+        vol = torch.rand(shape, generator=gen).to(dev)
+        v4 = vol.reshape(-1, *shape[-3:])
+        b, d, h, w = v4.shape
+        n_iso = float(max(1, b * (d - 1) * (h - 1) * (w - 1)))
+        ours = {"iso": lambda v: tv_loss_iso_3d(v, 1e-8), "squared": tv_loss_sq_3d,
+                "L1": lambda v: l1_mean(tv_loss_l1_3d(v), shape)}
+        torchs = {"iso": lambda v: torch_ref.tv_iso(v, 1e-8), "squared": torch_ref.tv_sq, "L1": torch_l1}
+        for name in ("iso", "squared", "L1"):
+            for backward in (False, True):
+                def mk(fn):
+                    def run():
+                        v = vol.detach().requires_grad_(backward)
+                        loss = fn(v)
+                        if backward:
+                            loss.backward()
+                    return run
+
+                t_ours = _ref_suite_time(mk(ours[name]), iters, warmup)
+                t_torch = _ref_suite_time(mk(torchs[name]), iters, warmup)
+                t_ref = None
+                if core is not None:
+                    st = torch.cuda.current_stream(dev).cuda_stream
+
+                    def ref_run():
+                        if name == "iso":
+                            acc = torch.zeros(1, device=dev)
+                            core.tv_loss_iso_3d_cuda(v4.data_ptr(), acc.data_ptr(), b, d, h, w, 1e-8, st)
+                            _ = acc.squeeze(0) / n_iso
+                            if backward:
+                                g = (torch.ones(1, device=dev) / n_iso).contiguous()
+                                gv = torch.zeros_like(v4)
+                                core.tv_loss_iso_3d_grad_cuda(v4.data_ptr(), g.data_ptr(), gv.data_ptr(), b, d, h, w,
+                                                              1e-8, st)
+                        elif name == "squared":
+                            acc = torch.zeros(1, device=dev)
+                            core.tv_loss_sq_3d_cuda(v4.data_ptr(), acc.data_ptr(), b, d, h, w, st)
+                            if backward:
+                                g = torch.ones(1, device=dev)
+                                gv = torch.empty_like(v4)
+                                core.tv_loss_sq_3d_grad_cuda(v4.data_ptr(), g.data_ptr(), gv.data_ptr(), b, d, h, w,
+                                                             st)
+                        else:
+                            acc = torch.zeros(3, device=dev)
+                            core.tv_loss_l1_3d_cuda(v4.data_ptr(), acc.data_ptr(), b, d, h, w, st)
+                            _ = l1_mean(acc, shape)
+                            if backward:
+                                g = torch.ones(3, device=dev)
+                                gv = torch.empty_like(v4)
+                                core.tv_loss_l1_3d_grad_cuda(v4.data_ptr(), g.data_ptr(), gv.data_ptr(), b, d, h, w,
+                                                             st)
+
+                    t_ref = _ref_suite_time(ref_run, iters, warmup)
+                rows.append({"bench": "tv", "config": str(shape), "op": name,
+                             "pass": "fwd+bwd" if backward else "fwd", "ours_ms": t_ours,
+                             "reference_kernels_ms": t_ref, "torch_ms": t_torch})
+        del vol, v4
+
+    kp_configs = (("light (8192x200 rays, T=4, C=8, 200^2)", 8192 * 200, 4, 8, 200, True),
+                  ("heavy (8192x200 rays, T=8, C=32, 200^2)", 8192 * 200, 8, 32, 200, True),
+                  ("decode (5*200^2 pts, T=4, C=8, 200^2)", 5 * 200 * 200, 4, 8, 200, False))
+    for label, n, t, c, res, rays in kp_configs:
+        pts = _ray_points(n, dev, gen) if rays else (torch.rand((n, 3), generator=gen) * 2 - 1).to(dev)
+        rot = torch.randn((t, 3, 3), generator=gen).to(dev)
+        plane = torch.empty((3 * t, c, res, res)).uniform_(0.1, 0.5, generator=gen).to(dev)
+        up = torch.randn((n, t * c), generator=gen).to(dev)
+        leaves = [x.detach().requires_grad_(True) for x in (pts, rot, plane)]
+        for backward in (False, True):
+            def mk(fn):
+                def run():
+                    out = fn(*leaves)
+                    if backward:
+                        (out * up).sum().backward()
+                        for x in leaves:
+                            x.grad = None
+                return run
+
+            t_ours = _ref_suite_time(mk(kplanes_tilted_fuse), iters, warmup)
+            t_torch = _ref_suite_time(mk(torch_ref.kplanes_tilted), max(3, iters // 4), 2)
+            t_ref = None
+            if core is not None:
+                st = torch.cuda.current_stream(dev).cuda_stream
+
+                def ref_run():
+                    gc = plane.permute(0, 2, 3, 1).contiguous()
+                    out = torch.empty((n, t * c), device=dev)
+                    core.kplanes_tilted_fuse_cuda(pts.data_ptr(), rot.data_ptr(), gc.data_ptr(), out.data_ptr(),
+                                                  n, t, c, res, res, st)
+                    if backward:
+                        # the benchmark's loss (out * upstream).sum() and the
+                        # gradient autograd hands the op's backward
+                        _ = (out * up).sum()
+                        gout = (up * 1.0).contiguous()
+                        gc2 = plane.permute(0, 2, 3, 1).contiguous()
+                        gp, gr, gg = torch.zeros_like(pts), torch.zeros_like(rot), torch.zeros_like(gc2)
+                        core.kplanes_tilted_fuse_grad_cuda(pts.data_ptr(), rot.data_ptr(), gc2.data_ptr(),
+                                                           gout.data_ptr(), gg.data_ptr(), gr.data_ptr(),
+                                                           gp.data_ptr(), n, t, c, res, res, st)
+                        _ = gg.permute(0, 3, 1, 2).contiguous()
+
+                t_ref = _ref_suite_time(ref_run, iters, warmup)
+            rows.append({"bench": "kplanes", "config": label, "op": "kplanes_tilted_fuse",
+                         "pass": "fwd+bwd" if backward else "fwd", "ours_ms": t_ours,
+                         "reference_kernels_ms": t_ref, "torch_ms": t_torch})
+
+    def gmean(xs):
+        xs = [x for x in xs if x]
+        return float(np.exp(np.mean(np.log(xs)))) if xs else None
+
+    for r in rows:
+        r["ours_over_reference"] = None if r["reference_kernels_ms"] is None else r["reference_kernels_ms"] / r["ours_ms"]
+        r["ours_over_torch"] = r["torch_ms"] / r["ours_ms"]
+    vs_ref = gmean([r["ours_over_reference"] for r in rows])
+    return {
+        "metric": "speed-up over the reference's own kernels on its benchmark configurations (geometric mean)",
+        "value": vs_ref,
+        "unit": "x",
+        "ms_per_step": sum(r["ours_ms"] for r in rows),
+        "gpu_launches": None,
+        "config": {"workload": DESCRIPTIONS["reference_suite"],
+                   "reference_kernels": "oracle/_ref/_core" if core is not None else why,
+                   "geomean_over_torch": gmean([r["ours_over_torch"] for r in rows]),
+                   "geomean_over_reference_tv": gmean([r["ours_over_reference"] for r in rows if r["bench"] == "tv"]),
+                   "geomean_over_reference_kplanes": gmean([r["ours_over_reference"] for r in rows
+                                                            if r["bench"] == "kplanes"])},
+        "rows": rows,
+        "roofline": None,
+        "clocks": None,
+        "e2e": None,
+        "dtype": "f32",
+    }
+
+
 DESCRIPTIONS = {
     "tv_iso_l1": "tv_iso_l1: tv_loss_iso_3d (eps 1e-8) + tv_loss_l1_3d single-sweep fwd+grad",
     "tv_sq_128": "tv_sq_128: tv_loss_sq_3d single-sweep fwd+grad on [128,128,128]",
+    "reference_suite": "reference_suite: the reference's benchmark configurations (bench_tv_loss.py, "
+                       "bench_kplanes_tilted.py) for this build, the reference's kernels and pure torch",
     "tv_multi": "tv_multi: tv_loss_iso_3d (eps 1e-8) + tv_loss_l1_3d losses and summed gradient in one sweep "
                 "(tv_loss_multi_3d_fwd_grad) on the tv_iso_l1 volume",
     "tv_1024": "tv_1024: tv_loss_sq_3d + tv_loss_iso_3d single-sweep fwd+grad on [1024]^3 blobs",
@@ -1475,6 +1666,7 @@ WORKLOADS = {
     "tv_iso_l1": run_tv_iso_l1,
     "tv_sq_128": run_tv_sq_128,
     "tv_multi": run_tv_multi,
+    "reference_suite": run_reference_suite,
     "tv_1024": run_tv_1024,
     "kplanes": run_kplanes,
     "kplanes_ms": run_kplanes_ms,
