@@ -107,6 +107,57 @@ def test_gradients_match_oracle(cfg):
         assert_rel_elementwise(mine, theirs, what)
 
 
+def ray_points(n_rays: int, samples: int, seed: int, scale: float = 1.1) -> torch.Tensor:
+    """Points in runs along rays, laid out as a tomography ray sampler lays
+    them out: neighbouring entries share plane cells."""
+    gen = torch.Generator().manual_seed(seed)
+    xy = torch.empty((n_rays, 1, 2)).uniform_(-scale, scale, generator=gen)
+    z = torch.linspace(-scale, scale, samples).view(1, -1, 1)
+    return torch.cat([xy.expand(-1, samples, -1), z.expand(n_rays, -1, -1)], dim=-1).reshape(-1, 3).contiguous()
+
+
+@pytest.mark.parametrize("C", [4, 8, 32])
+def test_ray_points_gradients_match_oracle(C):
+    """Runs of points that share plane cells, which the backward adds up in
+    registers before reducing (at C <= 8): one level, four taps and two levels
+    in one launch, against the oracle."""
+    from quantem.cuda.core.ml import kplanes_tilted_fuse_levels
+
+    T, H, W = 3, 40, 40
+    pts = ray_points(48, 64, seed=81)
+    N = pts.shape[0]
+    gen = torch.Generator().manual_seed(82)
+    rot = torch.empty((T, 3, 3)).uniform_(-1.0, 1.0, generator=gen)
+    plane = torch.empty((3 * T, C, H, W)).uniform_(0.1, 0.5, generator=gen)
+    up = torch.randn((N, T * C), generator=gen)
+    _, (gp, gr, gg) = grads(pts, rot, plane, up)
+    o_gp, o_gr, o_gg = oracle.kplanes_bwd(pts.numpy(), rot.numpy(), plane.numpy(), up.numpy())
+    for mine, theirs, what in ((gg, o_gg, "grad_plane"), (gp, o_gp, "grad_pts"), (gr, o_gr, "grad_rotations")):
+        assert_rel_max(mine, theirs, 1e-4, what)
+        assert_rel_elementwise(mine, theirs, what)
+
+    up4 = torch.randn((4, N, T * C), generator=gen)
+    _, (gp, gr, gg) = tv_grads(pts, rot, plane, up4, 0.02)
+    o_gp, o_gr, o_gg = oracle.kplanes_tv_bwd(pts.numpy(), rot.numpy(), plane.numpy(), up4.numpy(), 0.02)
+    for mine, theirs, what in ((gg, o_gg, "four-tap grad_plane"), (gp, o_gp, "four-tap grad_pts"),
+                               (gr, o_gr, "four-tap grad_rotations")):
+        assert_rel_max(mine, theirs, 1e-4, what)
+
+    planes = [plane, torch.empty((3 * T, C, 24, 24)).uniform_(0.1, 0.5, generator=gen)]
+    ups = [up, torch.randn((N, T * C), generator=gen)]
+    p = pts.cuda().requires_grad_(True)
+    pls = [pl.cuda().requires_grad_(True) for pl in planes]
+    outs = kplanes_tilted_fuse_levels(p, rot.cuda(), pls)
+    sum(((o * u.cuda()).sum() for o, u in zip(outs, ups))).backward()
+    o_gp = np.zeros(pts.shape, dtype=np.float64)
+    for lv, (pl, u) in enumerate(zip(planes, ups)):
+        g_p, _, g_g = oracle.kplanes_bwd(pts.numpy(), rot.numpy(), pl.numpy(), u.numpy())
+        assert_rel_max(pls[lv].grad, g_g, 1e-4, f"grad_plane level {lv}")
+        assert_rel_elementwise(pls[lv].grad, g_g, f"grad_plane level {lv}")
+        o_gp += g_p
+    assert_rel_max(p.grad, o_gp, 1e-4, "grad_pts (sum over levels)")
+
+
 def test_golden_fixtures_fp64_anchored(kp_golden):
     """test_kplanes_tilted.py:71-95 on the committed fixtures: the kernel's
     error against fp64 torch is no worse than 2x torch's own fp32 error."""
