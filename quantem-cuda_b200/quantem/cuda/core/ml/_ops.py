@@ -15,6 +15,12 @@ library's own transpose kernels, and skips the copy entirely when ``plane`` is
 already stored channels-last (``plane.permute(0, 2, 3, 1).is_contiguous()``,
 e.g. a parameter created with ``memory_format=torch.channels_last``); the
 plane gradient is then returned with the parameter's own strides.
+
+The public wrappers call the ops' implementations through
+``torch.autograd.Function`` classes when they run eagerly on plain tensors
+(``_eager``): the torch.library dispatcher costs tens of microseconds of host
+time per call, as much as a small point set's kernels. Under
+``torch.compile`` and for tensor subclasses the registered ops run unchanged.
 """
 
 from __future__ import annotations
@@ -23,6 +29,7 @@ import torch
 from torch import Tensor
 
 from quantem.cuda import _core
+from quantem.cuda.core._ops import _eager, _on_device
 
 
 def _stream(device: torch.device) -> int:
@@ -80,8 +87,7 @@ def _from_channels_last(grad_cl: Tensor, like: Tensor, stream: int) -> Tensor:
 # ── fused TILTED K-Planes interpolation ───────────────────────────────────
 
 
-@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse", mutates_args=())
-def _kplanes_tilted_fuse(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor:
+def _kpt_fwd_impl(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor:
     _check_kernel_inputs("kplanes_tilted_fuse", pts, rotations, plane)
     p = pts.contiguous()
     r = rotations.contiguous()
@@ -89,7 +95,7 @@ def _kplanes_tilted_fuse(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tenso
     b = p.shape[0]
     t = r.shape[0]
     stream = _stream(p.device)
-    with torch.cuda.device(p.device):
+    with _on_device(p.device):
         g = _channels_last(plane, stream)
         out = torch.empty((b, t * c), dtype=torch.float32, device=p.device)
         _core.kplanes_tilted_fuse_cuda(
@@ -98,15 +104,17 @@ def _kplanes_tilted_fuse(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tenso
     return out
 
 
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse", mutates_args=())
+def _kplanes_tilted_fuse(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor:
+    return _kpt_fwd_impl(pts, rotations, plane)
+
+
 @_kplanes_tilted_fuse.register_fake
 def _(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor:
     return pts.new_empty((pts.shape[0], rotations.shape[0] * plane.shape[1]))
 
 
-@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse_bwd", mutates_args=())
-def _kplanes_tilted_fuse_bwd(
-    pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor
-) -> list[Tensor]:
+def _kpt_bwd_impl(pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor) -> list[Tensor]:
     _check_kernel_inputs("kplanes_tilted_fuse_bwd", pts, rotations, plane, grad_out)
     p = pts.contiguous()
     r = rotations.contiguous()
@@ -114,7 +122,7 @@ def _kplanes_tilted_fuse_bwd(
     b = p.shape[0]
     t = r.shape[0]
     stream = _stream(p.device)
-    with torch.cuda.device(p.device):
+    with _on_device(p.device):
         g = _channels_last(plane, stream)
         gout = grad_out.detach().to(dtype=torch.float32, device=p.device).contiguous()
         grad_pts = torch.zeros_like(p)
@@ -139,6 +147,13 @@ def _kplanes_tilted_fuse_bwd(
     return [grad_pts, grad_r, grad_plane]
 
 
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse_bwd", mutates_args=())
+def _kplanes_tilted_fuse_bwd(
+    pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor
+) -> list[Tensor]:
+    return _kpt_bwd_impl(pts, rotations, plane, grad_out)
+
+
 @_kplanes_tilted_fuse_bwd.register_fake
 def _(pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor) -> list[Tensor]:
     return [torch.empty_like(pts), torch.empty_like(rotations), torch.empty_like(plane)]
@@ -156,6 +171,23 @@ def _kpt_backward(ctx, grad_out):
 
 
 _kplanes_tilted_fuse.register_autograd(_kpt_backward, setup_context=_kpt_setup_context)
+
+
+class _KPlanesTilted(torch.autograd.Function):
+    """The same forward and backward as the registered op, for eager calls on
+    plain tensors: no torch.library dispatch on the way (see ``_eager``)."""
+
+    @staticmethod
+    def forward(ctx, pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor:
+        ctx.save_for_backward(pts, rotations, plane)
+        return _kpt_fwd_impl(pts, rotations, plane)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad_out):
+        pts, rotations, plane = ctx.saved_tensors
+        grad_pts, grad_r, grad_plane = _kpt_bwd_impl(pts, rotations, plane, grad_out)
+        return grad_pts, grad_r, grad_plane
 
 
 # ── several levels in one launch ──────────────────────────────────────────
@@ -182,15 +214,14 @@ def _check_levels(fn: str, pts: Tensor, rotations: Tensor, planes: list[Tensor],
         raise ValueError(f"{fn}: one grad_out per level, got {len(grad_outs)} for {len(planes)} levels")
 
 
-@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse_levels", mutates_args=())
-def _kplanes_tilted_fuse_levels(pts: Tensor, rotations: Tensor, planes: list[Tensor]) -> list[Tensor]:
+def _kpl_fwd_impl(pts: Tensor, rotations: Tensor, planes: list[Tensor]) -> list[Tensor]:
     _check_levels("kplanes_tilted_fuse_levels", pts, rotations, planes)
     p = pts.contiguous()
     r = rotations.contiguous()
     b, t = p.shape[0], r.shape[0]
     c = planes[0].shape[1]
     stream = _stream(p.device)
-    with torch.cuda.device(p.device):
+    with _on_device(p.device):
         grids = [_channels_last(plane, stream) for plane in planes]
         outs = [torch.empty((b, t * c), dtype=torch.float32, device=p.device) for _ in planes]
         _core.kplanes_tilted_fuse_levels_cuda(
@@ -200,15 +231,17 @@ def _kplanes_tilted_fuse_levels(pts: Tensor, rotations: Tensor, planes: list[Ten
     return outs
 
 
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse_levels", mutates_args=())
+def _kplanes_tilted_fuse_levels(pts: Tensor, rotations: Tensor, planes: list[Tensor]) -> list[Tensor]:
+    return _kpl_fwd_impl(pts, rotations, planes)
+
+
 @_kplanes_tilted_fuse_levels.register_fake
 def _(pts: Tensor, rotations: Tensor, planes: list[Tensor]) -> list[Tensor]:
     return [pts.new_empty((pts.shape[0], rotations.shape[0] * pl.shape[1])) for pl in planes]
 
 
-@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse_levels_bwd", mutates_args=())
-def _kplanes_tilted_fuse_levels_bwd(
-    pts: Tensor, rotations: Tensor, planes: list[Tensor], grad_outs: list[Tensor]
-) -> list[Tensor]:
+def _kpl_bwd_impl(pts: Tensor, rotations: Tensor, planes: list[Tensor], grad_outs: list[Tensor]) -> list[Tensor]:
     """[grad_pts, grad_rotations, grad_plane_0, ..., grad_plane_{L-1}]"""
     _check_levels("kplanes_tilted_fuse_levels_bwd", pts, rotations, planes, grad_outs)
     p = pts.contiguous()
@@ -216,7 +249,7 @@ def _kplanes_tilted_fuse_levels_bwd(
     b, t = p.shape[0], r.shape[0]
     c = planes[0].shape[1]
     stream = _stream(p.device)
-    with torch.cuda.device(p.device):
+    with _on_device(p.device):
         grids = [_channels_last(plane, stream) for plane in planes]
         gouts = [go.detach().to(dtype=torch.float32, device=p.device).contiguous() for go in grad_outs]
         grad_pts = torch.zeros_like(p)
@@ -229,6 +262,14 @@ def _kplanes_tilted_fuse_levels_bwd(
         )
         grad_planes = [_from_channels_last(gc, pl, stream) for gc, pl in zip(grads_cl, planes)]
     return [grad_pts, grad_r, *grad_planes]
+
+
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_fuse_levels_bwd", mutates_args=())
+def _kplanes_tilted_fuse_levels_bwd(
+    pts: Tensor, rotations: Tensor, planes: list[Tensor], grad_outs: list[Tensor]
+) -> list[Tensor]:
+    """[grad_pts, grad_rotations, grad_plane_0, ..., grad_plane_{L-1}]"""
+    return _kpl_bwd_impl(pts, rotations, planes, grad_outs)
 
 
 @_kplanes_tilted_fuse_levels_bwd.register_fake
@@ -254,6 +295,24 @@ def _kpl_backward(ctx, grad_outs):
 _kplanes_tilted_fuse_levels.register_autograd(_kpl_backward, setup_context=_kpl_setup_context)
 
 
+class _KPlanesTiltedLevels(torch.autograd.Function):
+    """Eager counterpart of the registered multi-level op (see
+    ``_KPlanesTilted``); the planes come as separate arguments. A level whose
+    output takes no part in the loss gets a zero upstream gradient."""
+
+    @staticmethod
+    def forward(ctx, pts: Tensor, rotations: Tensor, *planes: Tensor):
+        ctx.save_for_backward(pts, rotations, *planes)
+        return tuple(_kpl_fwd_impl(pts, rotations, list(planes)))
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, *grad_outs):
+        pts, rotations, *planes = ctx.saved_tensors
+        grad_pts, grad_r, *grad_planes = _kpl_bwd_impl(pts, rotations, planes, list(grad_outs))
+        return (grad_pts, grad_r, *grad_planes)
+
+
 # ── four-tap variant for finite-difference TV regularisation ──────────────
 #
 # The reference's kplanes_tilted_tv_fuse (core/ml/_ops.py:103-204): tap 0 at
@@ -261,8 +320,7 @@ _kplanes_tilted_fuse_levels.register_autograd(_kpl_backward, setup_context=_kpl_
 # output [4, B, T*C] with the tap outermost; h carries no gradient.
 
 
-@torch.library.custom_op("quantem_cuda::kplanes_tilted_tv_fuse", mutates_args=())
-def _kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
+def _kpt_tv_fwd_impl(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
     _check_kernel_inputs("kplanes_tilted_tv_fuse", pts, rotations, plane)
     p = pts.contiguous()
     r = rotations.contiguous()
@@ -270,7 +328,7 @@ def _kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: fl
     b = p.shape[0]
     t = r.shape[0]
     stream = _stream(p.device)
-    with torch.cuda.device(p.device):
+    with _on_device(p.device):
         g = _channels_last(plane, stream)
         out = torch.empty((4, b, t * c), dtype=torch.float32, device=p.device)
         _core.kplanes_tilted_tv_fuse_cuda(
@@ -279,15 +337,17 @@ def _kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: fl
     return out
 
 
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_tv_fuse", mutates_args=())
+def _kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
+    return _kpt_tv_fwd_impl(pts, rotations, plane, h)
+
+
 @_kplanes_tilted_tv_fuse.register_fake
 def _(pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
     return pts.new_empty((4, pts.shape[0], rotations.shape[0] * plane.shape[1]))
 
 
-@torch.library.custom_op("quantem_cuda::kplanes_tilted_tv_fuse_bwd", mutates_args=())
-def _kplanes_tilted_tv_fuse_bwd(
-    pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor, h: float
-) -> list[Tensor]:
+def _kpt_tv_bwd_impl(pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor, h: float) -> list[Tensor]:
     _check_kernel_inputs("kplanes_tilted_tv_fuse_bwd", pts, rotations, plane, grad_out, taps=4)
     p = pts.contiguous()
     r = rotations.contiguous()
@@ -295,7 +355,7 @@ def _kplanes_tilted_tv_fuse_bwd(
     b = p.shape[0]
     t = r.shape[0]
     stream = _stream(p.device)
-    with torch.cuda.device(p.device):
+    with _on_device(p.device):
         g = _channels_last(plane, stream)
         gout = grad_out.detach().to(dtype=torch.float32, device=p.device).contiguous()
         grad_pts = torch.zeros_like(p)
@@ -307,6 +367,13 @@ def _kplanes_tilted_tv_fuse_bwd(
         )
         grad_plane = _from_channels_last(grad_plane_cl, plane, stream)
     return [grad_pts, grad_r, grad_plane]
+
+
+@torch.library.custom_op("quantem_cuda::kplanes_tilted_tv_fuse_bwd", mutates_args=())
+def _kplanes_tilted_tv_fuse_bwd(
+    pts: Tensor, rotations: Tensor, plane: Tensor, grad_out: Tensor, h: float
+) -> list[Tensor]:
+    return _kpt_tv_bwd_impl(pts, rotations, plane, grad_out, h)
 
 
 @_kplanes_tilted_tv_fuse_bwd.register_fake
@@ -327,6 +394,23 @@ def _kpt_tv_backward(ctx, grad_out):
 
 
 _kplanes_tilted_tv_fuse.register_autograd(_kpt_tv_backward, setup_context=_kpt_tv_setup_context)
+
+
+class _KPlanesTiltedTV(torch.autograd.Function):
+    """Eager counterpart of the registered four-tap op (see ``_KPlanesTilted``)."""
+
+    @staticmethod
+    def forward(ctx, pts: Tensor, rotations: Tensor, plane: Tensor, h: float) -> Tensor:
+        ctx.save_for_backward(pts, rotations, plane)
+        ctx.h = h
+        return _kpt_tv_fwd_impl(pts, rotations, plane, h)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad_out):
+        pts, rotations, plane = ctx.saved_tensors
+        grad_pts, grad_r, grad_plane = _kpt_tv_bwd_impl(pts, rotations, plane, grad_out, ctx.h)
+        return grad_pts, grad_r, grad_plane, None
 
 
 # ── public wrapper ────────────────────────────────────────────────────────
@@ -380,6 +464,8 @@ def kplanes_tilted_fuse(pts: Tensor, rotations: Tensor, plane: Tensor) -> Tensor
         fp32 tensor ``[B, T*C]`` (``out[b, t*C + c]``), differentiable.
     """
     _validate("kplanes_tilted_fuse", pts, rotations, plane)
+    if _eager(pts) and _eager(rotations) and _eager(plane):
+        return _KPlanesTilted.apply(pts, rotations, plane)
     return _kplanes_tilted_fuse(pts, rotations, plane)
 
 
@@ -396,6 +482,8 @@ def kplanes_tilted_fuse_levels(pts: Tensor, rotations: Tensor, planes: list[Tens
         raise ValueError("kplanes_tilted_fuse_levels expects at least one level")
     for plane in planes:
         _validate("kplanes_tilted_fuse_levels", pts, rotations, plane)
+    if _eager(pts) and _eager(rotations) and all(_eager(pl) for pl in planes):
+        return list(_KPlanesTiltedLevels.apply(pts, rotations, *planes))
     return _kplanes_tilted_fuse_levels(pts, rotations, planes)
 
 
@@ -424,4 +512,6 @@ def kplanes_tilted_tv_fuse(pts: Tensor, rotations: Tensor, plane: Tensor, h: flo
         pts, rotations and plane.
     """
     _validate("kplanes_tilted_tv_fuse", pts, rotations, plane)
+    if _eager(pts) and _eager(rotations) and _eager(plane):
+        return _KPlanesTiltedTV.apply(pts, rotations, plane, float(h))
     return _kplanes_tilted_tv_fuse(pts, rotations, plane, float(h))

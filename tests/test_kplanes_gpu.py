@@ -231,6 +231,41 @@ def test_compile_fullgraph():
     assert p.grad is not None and r.grad is not None and g.grad is not None
 
 
+def test_eager_path_matches_registered_ops():
+    """The public wrappers' eager path (autograd.Function) and the registered
+    torch.library ops give the same outputs bit for bit and the same
+    gradients (to the reordering of atomic sums), for the single-level,
+    four-tap and multi-level ops."""
+    from quantem.cuda.core.ml import kplanes_tilted_fuse_levels, kplanes_tilted_tv_fuse
+
+    pts, rot, plane, up = make_inputs(3000, 3, 8, 30, 26, seed=17)
+    plane2 = torch.empty((9, 8, 12, 15)).uniform_(0.1, 0.5, generator=torch.Generator().manual_seed(18))
+    up4 = torch.randn((4, *up.shape), generator=torch.Generator().manual_seed(19))
+    ops = torch.ops.quantem_cuda
+    cases = [
+        ("one level", lambda a, b, c, d: [kplanes_tilted_fuse(a, b, c)],
+         lambda a, b, c, d: [ops.kplanes_tilted_fuse(a, b, c)], [up]),
+        ("four taps", lambda a, b, c, d: [kplanes_tilted_tv_fuse(a, b, c, 0.03)],
+         lambda a, b, c, d: [ops.kplanes_tilted_tv_fuse(a, b, c, 0.03)], [up4]),
+        ("two levels", lambda a, b, c, d: kplanes_tilted_fuse_levels(a, b, [c, d]),
+         lambda a, b, c, d: ops.kplanes_tilted_fuse_levels(a, b, [c, d]), [up, up]),
+    ]
+    for what, eager, registered, ups in cases:
+        results = []
+        for fn in (eager, registered):
+            leaves = [t.cuda().requires_grad_(True) for t in (pts, rot, plane, plane2)]
+            outs = fn(*leaves)
+            sum((o * u.cuda()).sum() for o, u in zip(outs, ups)).backward()
+            results.append(([o.detach() for o in outs], [x.grad for x in leaves]))
+        (outs_e, grads_e), (outs_r, grads_r) = results
+        for a, b in zip(outs_e, outs_r):
+            assert torch.equal(a, b), what
+        for name, a, b in zip(("pts", "rotations", "plane", "plane2"), grads_e, grads_r):
+            assert (a is None) == (b is None), (what, name)
+            if a is not None:
+                torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-5 * b.abs().max().item(), msg=f"{what} {name}")
+
+
 def test_input_validation_on_device():
     pts, rot, plane, _ = make_inputs(16, 2, 4, 9, 9, seed=6)
     pts, rot, plane = pts.cuda(), rot.cuda(), plane.cuda()
