@@ -1221,11 +1221,14 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         # one channels-last copy of the planes for both passes, one backward
         # launch, then the plane- and rotation-gradient sum over the ranks:
         # by default one kernel over peer memory (deterministic, rank order);
-        # --kp-reduce nccl uses NCCL all_reduce (--kp-buckets > 1 overlaps
-        # per-bucket all_reduces with the backward)
+        # --kp-reduce nccl uses NCCL all_reduce; --kp-buckets > 1 overlaps
+        # each bucket's gradient sum (peer kernel of at most --kp-reduce-ctas
+        # CTAs on a second stream, or NCCL) with the next bucket's backward
         if ctx.args.kp_reduce == "peer":
             reducer = sharded.kplanes_gradient_reducer(g, r)
-            fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u, reducer=reducer))
+            fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u, reducer=reducer,
+                                                                  buckets=ctx.args.kp_buckets,
+                                                                  reduce_ctas=ctx.args.kp_reduce_ctas))
         else:
             fb = t_b.wrap(lambda: sharded.kplanes_fwd_bwd_sharded(p, r, g, u, buckets=ctx.args.kp_buckets))
 
@@ -1352,7 +1355,9 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
             pp = hp.to(dev, non_blocking=True)
             uu = hu.to(dev, non_blocking=True)
             if ctx.args.kp_reduce == "peer":
-                out, g_pts, g_rot, g_plane, _ = sharded.kplanes_fwd_bwd_sharded(pp, r, g, uu, reducer=reducer)
+                out, g_pts, g_rot, g_plane, _ = sharded.kplanes_fwd_bwd_sharded(
+                    pp, r, g, uu, reducer=reducer, buckets=ctx.args.kp_buckets,
+                    reduce_ctas=ctx.args.kp_reduce_ctas)
             else:
                 out, g_pts, g_rot, g_plane, _ = sharded.kplanes_fwd_bwd_sharded(pp, r, g, uu,
                                                                               buckets=ctx.args.kp_buckets)
@@ -1378,11 +1383,13 @@ def run_kplanes(ctx: Ctx, steps: int, warmup: int) -> dict:
         "unit": "points/s",
         "ms_per_step": ms_step,
         "gpu_launches": (5 if ctx.world == 1 else
-                         (5 if ctx.args.kp_reduce == "peer" else 2 + 2 * min(max(ctx.args.kp_buckets, 1), T))) * steps,
+                         (3 if ctx.args.kp_reduce == "peer" else 2) + 2 * min(max(ctx.args.kp_buckets, 1), T)) * steps,
         "config": {"workload": DESCRIPTIONS["kplanes"],
                    "points_per_gpu": N,
                    "parallelism": (f"points{ctx.world} (gradient sum: {ctx.args.kp_reduce}"
-                                   + (f", buckets {ctx.args.kp_buckets})" if ctx.args.kp_reduce == "nccl" else ")"))
+                                   + f", buckets {ctx.args.kp_buckets}"
+                                   + (f", reduce CTAs {ctx.args.kp_reduce_ctas})"
+                                      if ctx.args.kp_reduce == "peer" and ctx.args.kp_buckets > 1 else ")"))
                    if ctx.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (512 MiB output + 512 MiB upstream gradient per step)",
                    "fwd_op_ms": f_ms, "bwd_op_ms": b_ms},
@@ -1729,11 +1736,16 @@ def main() -> None:
                     help="default workload only: leave out the K-Planes half of the line")
     ap.add_argument("--kp-reduce", choices=("peer", "nccl"), default="peer",
                     help="multi-GPU K-Planes: gradient sum over peer memory or with NCCL all_reduce")
-    ap.add_argument("--kp-buckets", type=int, default=1,
-                    help="multi-GPU K-Planes: backward launches whose gradient all_reduce overlaps the next")
+    ap.add_argument("--kp-buckets", type=int, default=None,
+                    help="multi-GPU K-Planes: backward launches whose gradient sum overlaps the next "
+                         "(default 4 with the peer sum, 1 with NCCL)")
+    ap.add_argument("--kp-reduce-ctas", type=int, default=32,
+                    help="multi-GPU K-Planes, peer sum with --kp-buckets > 1: CTAs of an overlapped sum")
     ap.add_argument("--tv-transport", choices=("peer", "nccl"), default="peer",
                     help="multi-GPU TV: halos and loss sums over peer memory, or NCCL send/recv + all_gather")
     args = ap.parse_args()
+    if args.kp_buckets is None:
+        args.kp_buckets = 4 if args.kp_reduce == "peer" else 1
     ctx = Ctx(args)
     warmup = max(args.warmup, 3)
 

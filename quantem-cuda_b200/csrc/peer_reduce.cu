@@ -64,12 +64,15 @@ __device__ __forceinline__ float ld_cg1(const float *p) {
     return v;
 }
 
-// Sums float4 i of chunk [b4, e4) over the ranks in rank order and stores it
-// into every rank's buffer. WORLD > 0: the rank count is a compile-time
-// constant, so all WORLD x U loads of a thread are issued before the first
-// add (U float4s per thread per iteration keep 8-16 NVLink reads in flight).
+// Sums float4 i of chunk [b4, e4) of the range that starts at float `base`
+// (16-byte aligned) over the ranks in rank order and stores it into every
+// rank's buffer; `n` is the float count the range's float4s cover. WORLD > 0:
+// the rank count is a compile-time constant, so all WORLD x U loads of a
+// thread are issued before the first add (U float4s per thread per iteration
+// keep 8-16 NVLink reads in flight).
 template <int WORLD>
-__device__ __forceinline__ void sum_chunk(const qc_peer_group &g, long long b4, long long e4, long long n) {
+__device__ __forceinline__ void sum_chunk(const qc_peer_group &g, long long base, long long b4, long long e4,
+                                          long long n) {
     constexpr int U = WORLD <= 4 ? 4 : 2;
     const long long stride = (long long)gridDim.x * blockDim.x;
     long long i = b4 + (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -80,7 +83,7 @@ __device__ __forceinline__ void sum_chunk(const qc_peer_group &g, long long b4, 
 #pragma unroll
         for (int u = 0; u < U; ++u)
 #pragma unroll
-            for (int q = 0; q < WORLD; ++q) v[u][q] = ld_cg4(g.buf[q] + 4 * (i + u * stride));
+            for (int q = 0; q < WORLD; ++q) v[u][q] = ld_cg4(g.buf[q] + base + 4 * (i + u * stride));
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             float4 s = v[u][0];
@@ -93,14 +96,14 @@ __device__ __forceinline__ void sum_chunk(const qc_peer_group &g, long long b4, 
             }
             const long long j = i + u * stride;
 #pragma unroll
-            for (int q = 0; q < WORLD; ++q) *reinterpret_cast<float4 *>(g.buf[q] + 4 * j) = s;
+            for (int q = 0; q < WORLD; ++q) *reinterpret_cast<float4 *>(g.buf[q] + base + 4 * j) = s;
         }
     }
     for (; i < e4; i += stride) {
         if (!QC_IN_BOUNDS(4 * i + 3, n, g_pr_fault_word)) continue;
         float4 v[WORLD];
 #pragma unroll
-        for (int q = 0; q < WORLD; ++q) v[q] = ld_cg4(g.buf[q] + 4 * i);
+        for (int q = 0; q < WORLD; ++q) v[q] = ld_cg4(g.buf[q] + base + 4 * i);
         float4 s = v[0];
 #pragma unroll
         for (int q = 1; q < WORLD; ++q) {
@@ -110,29 +113,38 @@ __device__ __forceinline__ void sum_chunk(const qc_peer_group &g, long long b4, 
             s.w += v[q].w;
         }
 #pragma unroll
-        for (int q = 0; q < WORLD; ++q) *reinterpret_cast<float4 *>(g.buf[q] + 4 * i) = s;
+        for (int q = 0; q < WORLD; ++q) *reinterpret_cast<float4 *>(g.buf[q] + base + 4 * i) = s;
     }
 }
 
 // Any rank count (a runtime loop over the ranks).
-__device__ __forceinline__ void sum_chunk_any(const qc_peer_group &g, long long b4, long long e4, long long n) {
+__device__ __forceinline__ void sum_chunk_any(const qc_peer_group &g, long long base, long long b4, long long e4,
+                                              long long n) {
     const long long stride = (long long)gridDim.x * blockDim.x;
     for (long long i = b4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < e4; i += stride) {
         if (!QC_IN_BOUNDS(4 * i + 3, n, g_pr_fault_word)) continue;
-        float4 s = ld_cg4(g.buf[0] + 4 * i);
+        float4 s = ld_cg4(g.buf[0] + base + 4 * i);
         for (int q = 1; q < g.world; ++q) {
-            const float4 v = ld_cg4(g.buf[q] + 4 * i);
+            const float4 v = ld_cg4(g.buf[q] + base + 4 * i);
             s.x += v.x;
             s.y += v.y;
             s.z += v.z;
             s.w += v.w;
         }
-        for (int q = 0; q < g.world; ++q) *reinterpret_cast<float4 *>(g.buf[q] + 4 * i) = s;
+        for (int q = 0; q < g.world; ++q) *reinterpret_cast<float4 *>(g.buf[q] + base + 4 * i) = s;
     }
 }
 
-__global__ void __launch_bounds__(kThreads) allreduce_kernel(qc_peer_group g,
-                                                             unsigned long long seq, long long n) {
+// One float at index i of every buffer, summed in rank order and stored back.
+__device__ __forceinline__ void sum_one(const qc_peer_group &g, long long i) {
+    float s = ld_cg1(g.buf[0] + i);
+    for (int q = 1; q < g.world; ++q) s += ld_cg1(g.buf[q] + i);
+    for (int q = 0; q < g.world; ++q) g.buf[q][i] = s;
+}
+
+// Sums floats [off, off + n) of every buffer.
+__global__ void __launch_bounds__(kThreads, 2) allreduce_kernel(qc_peer_group g, unsigned long long seq,
+                                                             long long off, long long n) {
     Comm *self = static_cast<Comm *>(g.comm[g.rank]);
     const uint64_t limit = g.timeout_ns ? g.timeout_ns : kDefaultLimitNs;
     __shared__ int go;
@@ -147,23 +159,24 @@ __global__ void __launch_bounds__(kThreads) allreduce_kernel(qc_peer_group g,
     }
     __syncthreads();
     if (go) {
-        // this rank's chunk, in float4 units; the last rank takes the tail
-        const long long n4 = n / 4;
+        // floats before the range's first 16-byte boundary, then float4s,
+        // then the floats after the last whole float4
+        const long long head = (off % 4 == 0) ? 0 : (4 - off % 4 < n ? 4 - off % 4 : n);
+        const long long base = off + head;
+        const long long n4 = (n - head) / 4;
+        // this rank's chunk of the float4s; the last rank takes the remainder
         const long long per = n4 / g.world;
         const long long b4 = per * g.rank;
         const long long e4 = g.rank == g.world - 1 ? n4 : b4 + per;
         switch (g.world) {
-            case 2: sum_chunk<2>(g, b4, e4, n); break;
-            case 4: sum_chunk<4>(g, b4, e4, n); break;
-            case 8: sum_chunk<8>(g, b4, e4, n); break;
-            default: sum_chunk_any(g, b4, e4, n); break;
+            case 2: sum_chunk<2>(g, base, b4, e4, 4 * n4); break;
+            case 4: sum_chunk<4>(g, base, b4, e4, 4 * n4); break;
+            case 8: sum_chunk<8>(g, base, b4, e4, 4 * n4); break;
+            default: sum_chunk_any(g, base, b4, e4, 4 * n4); break;
         }
         if (g.rank == g.world - 1 && blockIdx.x == 0) {
-            for (long long i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) {
-                float s = ld_cg1(g.buf[0] + i);
-                for (int q = 1; q < g.world; ++q) s += ld_cg1(g.buf[q] + i);
-                for (int q = 0; q < g.world; ++q) g.buf[q][i] = s;
-            }
+            if (threadIdx.x < head) sum_one(g, off + threadIdx.x);
+            for (long long i = base + 4 * n4 + threadIdx.x; i < off + n; i += blockDim.x) sum_one(g, i);
         }
     }
     __syncthreads();
@@ -203,13 +216,19 @@ size_t peer_allreduce_comm_bytes(void) { return sizeof(qc::pr::Comm); }
 
 int peer_allreduce_sum_f32_cuda(const qc_peer_group *g, unsigned long long seq, long long n,
                                 cudaStream_t stream) {
+    return peer_allreduce_sum_f32_range_cuda(g, seq, 0, n, 0, stream);
+}
+
+int peer_allreduce_sum_f32_range_cuda(const qc_peer_group *g, unsigned long long seq, long long offset,
+                                      long long n, int max_ctas, cudaStream_t stream) {
     QC_NVTX("quantem::peer_allreduce");
     QC_RETURN_IF(g == nullptr, QC_ERR_INVALID_ARGUMENT, "peer_allreduce: null group");
     QC_RETURN_IF(g->world < 1 || g->world > QC_MAX_PEER_RANKS || g->rank < 0 ||
                      g->rank >= g->world,
                  QC_ERR_INVALID_ARGUMENT, "peer_allreduce: rank %d of %d", g->rank, g->world);
     QC_RETURN_IF(seq == 0, QC_ERR_INVALID_ARGUMENT, "peer_allreduce: seq starts at 1");
-    QC_RETURN_IF(n < 0, QC_ERR_INVALID_ARGUMENT, "peer_allreduce: negative size");
+    QC_RETURN_IF(n < 0 || offset < 0 || max_ctas < 0, QC_ERR_INVALID_ARGUMENT,
+                 "peer_allreduce: negative offset, size or CTA count");
     for (int q = 0; q < g->world; ++q) {
         QC_RETURN_IF(g->comm[q] == nullptr || g->buf[q] == nullptr, QC_ERR_INVALID_ARGUMENT,
                      "peer_allreduce: rank %d's buffer or communication block missing", q);
@@ -221,9 +240,10 @@ int peer_allreduce_sum_f32_cuda(const qc_peer_group *g, unsigned long long seq, 
     if (int st = qc::device_sm_count(&sms)) return st;
     const long long per4 = n / 4 / g->world + 1;
     long long grid = (per4 + qc::pr::kThreads - 1) / qc::pr::kThreads;
-    if (grid > 2LL * sms) grid = 2LL * sms;
+    const long long cap = max_ctas > 0 ? (long long)max_ctas : 2LL * sms;
+    if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    qc::pr::allreduce_kernel<<<(unsigned)grid, qc::pr::kThreads, 0, stream>>>(*g, seq, n);
+    qc::pr::allreduce_kernel<<<(unsigned)grid, qc::pr::kThreads, 0, stream>>>(*g, seq, offset, n);
     QC_CHECK_LAUNCH("peer allreduce_kernel launch");
     return 0;
 }

@@ -444,6 +444,14 @@ PYBIND11_MODULE(_core, m) {
         },
         py::arg("group"), py::arg("seq"), py::arg("n"), py::arg("stream_ptr"));
     m.def(
+        "peer_allreduce_sum_f32_range_cuda",
+        [](const qc_peer_group &g, unsigned long long seq, long long offset, long long n, int max_ctas,
+           uintptr_t stream) {
+            check(peer_allreduce_sum_f32_range_cuda(&g, seq, offset, n, max_ctas, stream_of(stream)));
+        },
+        py::arg("group"), py::arg("seq"), py::arg("offset"), py::arg("n"), py::arg("max_ctas"),
+        py::arg("stream_ptr"));
+    m.def(
         "peer_allreduce_fault_word",
         [](int device, bool clear) {
             unsigned int w = 0;

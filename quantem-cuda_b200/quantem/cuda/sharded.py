@@ -210,6 +210,7 @@ def kplanes_fwd_bwd_sharded(
     fwd_bwd: Callable | None = None,
     buckets: int = 1,
     reducer: "PeerAllReduce | None" = None,
+    reduce_ctas: int = 32,
 ):
     """Forward and backward of one K-Planes level over point-sharded ranks.
 
@@ -234,6 +235,10 @@ def kplanes_fwd_bwd_sharded(
     replaces the NCCL all_reduce: the backward accumulates straight into the
     reducer's peer-memory buffer and one kernel sums it over the ranks in rank
     order (deterministic, identical on every rank); ``work`` is then None.
+    With ``buckets`` > 1 the backward runs bucket by bucket over consecutive
+    rotations and each bucket's plane gradients are summed on a second stream
+    by a kernel of at most ``reduce_ctas`` CTAs while the next bucket's
+    backward computes (the rotation gradients go with the last bucket).
     """
     _, world = _rank_world(group)
     if fwd_bwd is None:
@@ -249,7 +254,8 @@ def kplanes_fwd_bwd_sharded(
                 dist.all_reduce(g_rot, group=group, async_op=True),
             ]
     elif reducer is not None:
-        out, g_pts, g_rot, g_plane = _kplanes_fwd_bwd_peer(pts_local, rotations, plane, grad_out_local, reducer)
+        out, g_pts, g_rot, g_plane = _kplanes_fwd_bwd_peer(pts_local, rotations, plane, grad_out_local, reducer,
+                                                           buckets, reduce_ctas)
         works = []
     else:
         out, g_pts, g_rot, g_plane, works = _kplanes_fwd_bwd_bucketed(
@@ -269,7 +275,14 @@ def kplanes_fwd_bwd_sharded(
     return out, g_pts, g_rot, g_plane, work
 
 
-def _kplanes_fwd_bwd_peer(pts, rotations, plane, grad_out, reducer):
+def _rotation_buckets(t_count: int, buckets: int) -> list[tuple[int, int]]:
+    """Consecutive rotation ranges, as equal as possible, at most ``buckets``."""
+    k = max(1, min(int(buckets), t_count))
+    edges = [t_count * i // k for i in range(k + 1)]
+    return [(a, b) for a, b in zip(edges[:-1], edges[1:]) if b > a]
+
+
+def _kplanes_fwd_bwd_peer(pts, rotations, plane, grad_out, reducer, buckets=1, reduce_ctas=32):
     from quantem.cuda import _core
     from quantem.cuda.core.ml._ops import _channels_last, _from_channels_last
 
@@ -294,10 +307,30 @@ def _kplanes_fwd_bwd_peer(pts, rotations, plane, grad_out, reducer):
         buf[: P + r.numel()].zero_()
         g_cl = buf[:P].view(3 * t_count, h, w, c)
         g_rot = buf[P : P + r.numel()].view(t_count, 3, 3)
-        _core.kplanes_tilted_fuse_grad_cuda(p.data_ptr(), r.data_ptr(), g.data_ptr(), gout.data_ptr(),
-                                            g_cl.data_ptr(), g_rot.data_ptr(), g_pts.data_ptr(),
-                                            n, t_count, c, h, w, stream)
-        reducer.all_reduce()
+        ranges = _rotation_buckets(t_count, buckets)
+        if len(ranges) == 1:
+            _core.kplanes_tilted_fuse_grad_cuda(p.data_ptr(), r.data_ptr(), g.data_ptr(), gout.data_ptr(),
+                                                g_cl.data_ptr(), g_rot.data_ptr(), g_pts.data_ptr(),
+                                                n, t_count, c, h, w, stream)
+            reducer.all_reduce(0, P + r.numel())
+        else:
+            # bucket k's planes 3*t0 .. 3*t1-1 are floats [3*t0*hwc, 3*t1*hwc)
+            # of the channels-last gradient; the last bucket's range runs on
+            # through the rotation gradient, complete only after every bucket
+            main = torch.cuda.current_stream(dev)
+            side = reducer.side_stream()
+            per_rot = 3 * h * w * c
+            for k, (t0, t1) in enumerate(ranges):
+                _core.kplanes_tilted_fuse_grad_rotations_cuda(
+                    p.data_ptr(), r.data_ptr(), g.data_ptr(), gout.data_ptr(), g_cl.data_ptr(),
+                    g_rot.data_ptr(), g_pts.data_ptr(), n, t_count, c, h, w, t0, t1, stream)
+                done = torch.cuda.Event()
+                done.record(main)
+                side.wait_event(done)
+                last = k == len(ranges) - 1
+                end = P + r.numel() if last else t1 * per_rot
+                reducer.all_reduce(t0 * per_rot, end - t0 * per_rot, 0 if last else reduce_ctas, stream=side)
+            main.wait_stream(side)
         # the reducer's buffer is reused by the next call: hand out copies
         g_plane = _from_channels_last(g_cl, plane, stream)
         if g_plane.data_ptr() == g_cl.data_ptr():
@@ -630,18 +663,35 @@ class PeerAllReduce:
                 comms.append(c)
         self._group = _core.PeerGroup(rank, world, int(timeout_s * 1e9), comms, bufs)
         self._seq = 0
+        self._side: torch.cuda.Stream | None = None
         dist.barrier(group=group)
 
-    def all_reduce(self) -> Tensor:
-        """Sums ``buffer`` over the ranks in place (kernel on the current
-        stream) and returns it."""
+    def side_stream(self) -> torch.cuda.Stream:
+        """A stream of this reducer's own, for sums that overlap other work."""
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=self.device)
+        return self._side
+
+    def all_reduce(self, offset: int = 0, count: int | None = None, max_ctas: int = 0,
+                   stream: torch.cuda.Stream | None = None) -> Tensor:
+        """Sums ``buffer[offset : offset + count]`` (all of it by default) over
+        the ranks in place, by one kernel of at most ``max_ctas`` CTAs (0: two
+        per SM) on ``stream`` (default: the current stream), and returns that
+        range. Every rank makes the same calls in the same order."""
         from quantem.cuda import _core
 
+        count = self.numel - offset if count is None else int(count)
+        if offset < 0 or count < 0 or offset + count > self.numel:
+            raise ValueError(f"PeerAllReduce.all_reduce: range [{offset}, {offset + count}) outside the "
+                             f"buffer of {self.numel} floats")
+        if max_ctas < 0:
+            raise ValueError(f"PeerAllReduce.all_reduce: max_ctas must be >= 0, got {max_ctas}")
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
         self._seq += 1
         with torch.cuda.device(self.device):
-            _core.peer_allreduce_sum_f32_cuda(self._group, self._seq, self.numel,
-                                              torch.cuda.current_stream(self.device).cuda_stream)
-        return self.buffer
+            _core.peer_allreduce_sum_f32_range_cuda(self._group, self._seq, int(offset), count, int(max_ctas),
+                                                    st.cuda_stream)
+        return self.buffer[offset : offset + count]
 
     def close(self) -> None:
         """Unmaps the peers' buffers (collective)."""

@@ -184,3 +184,10 @@ def test_peer_entries_reject_bad_arguments_without_a_device():
         _core.tv_loss_3d_slab_peer_cuda(good, 1, 1, _core.TV_SQ, _core.TV_LOSS, 128, 0, 0, 256, 1, 5, 4, 4, 0, 4,
                                         0, 1, 0.0, 1.0, 0, 0, 0)
     assert _core.tv_peer_comm_bytes() >= 8 * 2 * 4 * 8
+    grp = _core.PeerGroup(0, 2, 0, [16, 32], [64, 128])
+    with pytest.raises(RuntimeError, match="seq starts at 1"):
+        _core.peer_allreduce_sum_f32_range_cuda(grp, 0, 0, 4, 0, 0)
+    with pytest.raises(RuntimeError, match="negative offset, size or CTA count"):
+        _core.peer_allreduce_sum_f32_range_cuda(grp, 1, -1, 4, 0, 0)
+    with pytest.raises(RuntimeError, match="negative offset, size or CTA count"):
+        _core.peer_allreduce_sum_f32_range_cuda(grp, 1, 0, 4, -2, 0)

@@ -117,6 +117,19 @@ def test_tv_dslab_matches_whole_volume(world, shape):
         np.testing.assert_allclose(ls[0], want[v][0], rtol=1e-5)
 
 
+def test_rotation_buckets_partition():
+    from quantem.cuda.sharded import _rotation_buckets
+
+    for T in (1, 2, 3, 4, 8, 13):
+        for k in (0, 1, 2, 3, 4, 16):
+            ranges = _rotation_buckets(T, k)
+            assert ranges[0][0] == 0 and ranges[-1][1] == T
+            assert all(a[1] == b[0] and a[1] > a[0] for a, b in zip(ranges, ranges[1:]))
+            assert len(ranges) == max(1, min(k, T))
+            sizes = [b - a for a, b in ranges]
+            assert max(sizes) - min(sizes) <= 1
+
+
 def test_slab_bounds_partition():
     from quantem.cuda import sharded
 

@@ -221,13 +221,19 @@ def _kp_worker(rank, world, port, queue):
         for _ in range(2):
             _, pg_pts, pg_rot, pg_plane, pwork = sharded.kplanes_fwd_bwd_sharded(p, r, g, u, reducer=reducer)
         assert pwork is None
+        # and with the backward in three rotation buckets, each bucket's sum
+        # on the reducer's second stream beside the next bucket's backward
+        for _ in range(2):
+            _, bg_pts, bg_rot, bg_plane, _ = sharded.kplanes_fwd_bwd_sharded(p, r, g, u, reducer=reducer,
+                                                                             buckets=3, reduce_ctas=8)
         torch.cuda.synchronize()
         from quantem.cuda import _core
 
         fault = _core.peer_allreduce_fault_word(rank)
         reducer.close()
         queue.put((rank, lo, hi, out.cpu(), g_pts.cpu(), g_rot.cpu(), g_plane.cpu(),
-                   pg_pts.cpu(), pg_rot.cpu(), pg_plane.cpu(), fault))
+                   pg_pts.cpu(), pg_rot.cpu(), pg_plane.cpu(), fault,
+                   bg_pts.cpu(), bg_rot.cpu(), bg_plane.cpu()))
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
@@ -251,16 +257,17 @@ def test_kplanes_point_sharding_matches_single_gpu():
     pts, rot, plane, up = (t.cuda() for t in _kp_inputs())
     out = torch.ops.quantem_cuda.kplanes_tilted_fuse(pts, rot, plane).cpu()
     ref_pts, ref_rot, ref_plane = (t.cpu() for t in torch.ops.quantem_cuda.kplanes_tilted_fuse_bwd(pts, rot, plane, up))
-    for rank, lo, hi, r_out, r_pts, r_rot, r_plane, p_pts, p_rot, p_plane, fault in res:
+    for rank, lo, hi, r_out, r_pts, r_rot, r_plane, p_pts, p_rot, p_plane, fault, b_pts, b_rot, b_plane in res:
         assert fault == 0
         assert torch.equal(r_out, out[lo:hi])
-        for gp, gr, gg in ((r_pts, r_rot, r_plane), (p_pts, p_rot, p_plane)):
+        for gp, gr, gg in ((r_pts, r_rot, r_plane), (p_pts, p_rot, p_plane), (b_pts, b_rot, b_plane)):
             torch.testing.assert_close(gp, ref_pts[lo:hi], rtol=1e-4, atol=1e-5 * ref_pts.abs().max().item())
             torch.testing.assert_close(gr, ref_rot, rtol=1e-4, atol=1e-4 * ref_rot.abs().max().item())
             torch.testing.assert_close(gg, ref_plane, rtol=1e-4, atol=1e-5 * ref_plane.abs().max().item())
     # both reductions give every rank the same gradients
     assert torch.equal(res[0][5], res[1][5]) and torch.equal(res[0][6], res[1][6])
     assert torch.equal(res[0][8], res[1][8]) and torch.equal(res[0][9], res[1][9])
+    assert torch.equal(res[0][12], res[1][12]) and torch.equal(res[0][13], res[1][13])
 
 
 
@@ -270,6 +277,9 @@ def test_kplanes_point_sharding_matches_single_gpu():
 # Sizes: fewer elements than 4 x ranks (tail only), one float4 per rank plus
 # a tail, and a large size that is not a multiple of 4 x ranks.
 ALLREDUCE_SIZES = (3, 37, 1_000_003)
+# (offset, count, max_ctas) of ranged sums: inside one float4, across a
+# boundary, an unaligned start with a long body and tail, an empty range
+RANGES = ((1, 2, 1), (2, 9, 0), (5, 999_990, 3), (36, 0, 1))
 
 
 def _allreduce_worker(rank, world, port, queue):
@@ -291,6 +301,14 @@ def _allreduce_worker(rank, world, port, queue):
                 gen = torch.Generator().manual_seed(1000 * call + rank)
                 red.buffer.copy_(torch.randn(n, generator=gen).cuda())
                 outs.append(red.all_reduce().cpu().clone())
+            # ranges with unaligned ends, few CTAs: only the range is summed
+            for lo, cnt, ctas in RANGES:
+                if lo + cnt > n:
+                    continue
+                gen = torch.Generator().manual_seed(7000 + rank)
+                red.buffer.copy_(torch.randn(n, generator=gen).cuda())
+                red.all_reduce(lo, cnt, ctas)
+                outs.append(red.buffer.cpu().clone())
             torch.cuda.synchronize()
             red.close()
         queue.put((rank, outs, _core.peer_allreduce_fault_word(rank)))
@@ -323,4 +341,16 @@ def test_peer_allreduce_is_the_rank_ordered_sum(world):
             for rank, outs, fault in res:
                 assert fault == 0
                 assert torch.equal(outs[k], expect), (rank, n, call)
+            k += 1
+        for lo, cnt, _ in RANGES:
+            if lo + cnt > n:
+                continue
+            parts = [torch.randn(n, generator=torch.Generator().manual_seed(7000 + r)) for r in range(world)]
+            total = parts[0].clone()
+            for x in parts[1:]:
+                total += x
+            for rank, outs, fault in res:
+                expect = parts[rank].clone()
+                expect[lo : lo + cnt] = total[lo : lo + cnt]
+                assert torch.equal(outs[k], expect), (rank, n, lo, cnt)
             k += 1
