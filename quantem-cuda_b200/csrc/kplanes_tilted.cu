@@ -311,11 +311,6 @@ __device__ __forceinline__ void kpt_bwd_v4_body(
     float gr[9] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // this group's dL/dR_t
     float hc[9];
     if (NT > 1) tap_offsets(Rt, h, hc);
-    // Merging the corner reductions of points that share a cell pays where a
-    // group is a small share of the warp (C <= 8: 16 or 32 groups) and the
-    // points come in runs along rays; at C >= 16 the shuffles cost more than
-    // the reductions they save.
-    constexpr bool kMerge = L <= 2;
 
     // this block's contiguous range of point tiles, its warps interleaved
     const long long n_tiles = (B + G - 1) / G;
@@ -351,21 +346,6 @@ __device__ __forceinline__ void kpt_bwd_v4_body(
             sample_with_slopes<C>(g0 + p * planeHWC, tap[p], s[p], dx[p], dy[p]);
         }
 
-        // One cheap test per tile before any merging: does a group share a
-        // plane cell with its neighbour (the next point of a ray)? Scattered
-        // points fail it and skip the per-plane votes. Warp-uniform.
-        bool vote = false;
-        if constexpr (kMerge) {
-            bool near = false;
-#pragma unroll
-            for (int p = 0; p < 3; ++p) {
-                const int key = active ? tap[p].cell[0] : -1;
-                const int peer_key = __shfl_xor_sync(0xffffffffu, key, L);
-                near |= active && peer_key == key;
-            }
-            vote = __any_sync(0xffffffffu, near);
-        }
-
         float dgx[3], dgy[3];
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
@@ -376,68 +356,17 @@ __device__ __forceinline__ void kpt_bwd_v4_body(
             other.z = sa.z * sb.z * go.z;
             other.w = sa.w * sb.w * go.w;
             float *gpc = gg0 + p * planeHWC;
-            if constexpr (kMerge) {
-                dgx[p] = other.x * dx[p].x + other.y * dx[p].y + other.z * dx[p].z + other.w * dx[p].w;
-                dgy[p] = other.x * dy[p].x + other.y * dy[p].y + other.z * dy[p].z + other.w * dy[p].w;
-                // Groups of the warp whose points share this plane's cell (the
-                // neighbouring samples of a ray) pair up level by level: the
-                // lower group of a matching pair adds the upper one's corner
-                // terms in registers and alone issues the reductions. The first
-                // corner's index decides, since the other three follow from it.
-                bool live = active;
-                unsigned merged = 0u, take = 0u;
-                if (vote) {
-#pragma unroll
-                    for (int j = 0, off = L; off < 32; ++j, off <<= 1) {
-                        // every lane shuffles (full mask), merged-away lanes with key -1
-                        const int key = live ? tap[p].cell[0] : -1;
-                        const int peer_key = __shfl_xor_sync(0xffffffffu, key, off);
-                        const bool same = live && peer_key == key;
-                        if (__any_sync(0xffffffffu, same)) {  // warp-uniform
-                            merged |= 1u << j;
-                            if (same) {
-                                if ((lane & off) == 0) take |= 1u << j;
-                                else live = false;
-                            }
-                        }
-                    }
-                }
+            if (active) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const float wk = tap[p].w[k];
-                    float4 c = make_float4(other.x * wk, other.y * wk, other.z * wk, other.w * wk);
-#pragma unroll
-                    for (int j = 0, off = L; off < 32; ++j, off <<= 1) {
-                        if (merged & (1u << j)) {
-                            const float ox = __shfl_xor_sync(0xffffffffu, c.x, off);
-                            const float oy = __shfl_xor_sync(0xffffffffu, c.y, off);
-                            const float oz = __shfl_xor_sync(0xffffffffu, c.z, off);
-                            const float ow = __shfl_xor_sync(0xffffffffu, c.w, off);
-                            if (take & (1u << j)) {
-                                c.x += ox;
-                                c.y += oy;
-                                c.z += oz;
-                                c.w += ow;
-                            }
-                        }
-                    }
-                    // a corner whose summed terms are all zero (zero weights) adds nothing
-                    if (live && (c.x != 0.f || c.y != 0.f || c.z != 0.f || c.w != 0.f))
-                        red_add_v4(gpc + tap[p].cell[k] * C, c);
+                    if (wk != 0.f)
+                        red_add_v4(gpc + tap[p].cell[k] * C,
+                                   make_float4(other.x * wk, other.y * wk, other.z * wk, other.w * wk));
                 }
-            } else {
-                if (active) {
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float wk = tap[p].w[k];
-                        if (wk != 0.f)
-                            red_add_v4(gpc + tap[p].cell[k] * C,
-                                       make_float4(other.x * wk, other.y * wk, other.z * wk, other.w * wk));
-                    }
-                }
-                dgx[p] = other.x * dx[p].x + other.y * dx[p].y + other.z * dx[p].z + other.w * dx[p].w;
-                dgy[p] = other.x * dy[p].x + other.y * dy[p].y + other.z * dy[p].z + other.w * dy[p].w;
             }
+            dgx[p] = other.x * dx[p].x + other.y * dx[p].y + other.z * dx[p].z + other.w * dx[p].w;
+            dgy[p] = other.x * dy[p].x + other.y * dy[p].y + other.z * dy[p].z + other.w * dy[p].w;
         }
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
