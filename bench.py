@@ -52,7 +52,6 @@ import math
 import os
 import statistics
 import sys
-import threading
 import time
 from pathlib import Path
 
@@ -92,9 +91,44 @@ def ncu_traffic(workload: str) -> dict | None:
     return None
 
 
+# The NVML poller runs in a process of its own: in a thread of this process it
+# would wait for the GIL, which the loop issuing the timed steps holds for
+# most of a region a few milliseconds long. It keeps (monotonic time, SM MHz,
+# reasons, power W) samples until told the region's bounds on stdin, answers
+# with the samples inside them as one JSON line and exits; it also exits when
+# its stdin closes (this process gone).
+_POLLER = r"""
+import json, select, sys, time
+import pynvml as nv
+nv.nvmlInit()
+key, period = sys.argv[1], float(sys.argv[2])
+h = nv.nvmlDeviceGetHandleByUUID(key[5:]) if key.startswith("uuid:") else nv.nvmlDeviceGetHandleByIndex(int(key[6:]))
+out, k, power = [], 0, float("nan")
+print("ready", flush=True)
+while True:
+    if select.select([sys.stdin], [], [], 0)[0]:
+        line = sys.stdin.readline()
+        if line:
+            t0, t1 = map(float, line.split())
+            print(json.dumps([s for s in out if t0 <= s[0] <= t1]), flush=True)
+        break
+    try:
+        mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        if k % 8 == 0:
+            power = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+        k += 1
+        out.append((time.monotonic(), mhz, reasons, power))
+    except Exception:
+        pass
+    time.sleep(period)
+"""
+
+
 class ClockSampler:
-    """Polls SM clock, power and throttle reasons through NVML while the timed
-    region runs (reads only; changes no setting)."""
+    """Samples SM clock, power and throttle reasons through NVML while the
+    timed region runs (reads only; changes no setting), from a poller process
+    started with the sampler (before the warm-up)."""
 
     REASONS = {
         0x1: "gpu_idle",
@@ -108,67 +142,86 @@ class ClockSampler:
         0x200: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.0005):
-        self.period = period_s
+    def __init__(self, device_index: int, period_s: float = 0.0005, ready_timeout_s: float = 30.0):
+        import subprocess
+
         self.samples: list[tuple[int, int, float]] = []
         self.max_mhz = None
-        self._stop = threading.Event()
-        self._thread = None
         self.handle = None
+        self._proc = None
+        self._t0 = self._t1 = None
         try:
             import pynvml
 
             pynvml.nvmlInit()
-            self.nv = pynvml
-            uuid = None
+            key = None
             try:
-                uuid = torch.cuda.get_device_properties(device_index).uuid
+                key = "uuid:GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(key[5:])
             except Exception:
-                pass
-            self.handle = None
-            if uuid is not None:
-                try:
-                    self.handle = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(uuid))
-                except Exception:
-                    self.handle = None
+                self.handle = None
             if self.handle is None:
                 vis = os.environ.get("CUDA_VISIBLE_DEVICES")
                 idx = int(vis.split(",")[device_index]) if vis and vis.split(",")[0].isdigit() else device_index
+                key = f"index:{idx}"
                 self.handle = pynvml.nvmlDeviceGetHandleByIndex(idx)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
         except Exception:
             self.handle = None
+            return
+        try:
+            self._proc = subprocess.Popen([sys.executable, "-c", _POLLER, key, str(period_s)],
+                                          stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                                          stderr=subprocess.DEVNULL, text=True)
+            if self._readline(ready_timeout_s) != "ready":
+                self._close()
+        except Exception:
+            self._close()
 
-    def _run(self):
-        # clock and reasons every period (timed regions can be a few ms long);
-        # power, the slowest query, on every 8th sample
-        nv = self.nv
-        power = float("nan")
-        k = 0
-        while not self._stop.is_set():
+    def _readline(self, timeout_s: float) -> str | None:
+        import select
+
+        if select.select([self._proc.stdout], [], [], timeout_s)[0]:
+            return self._proc.stdout.readline().strip()
+        return None
+
+    def _close(self):
+        if self._proc is not None:
             try:
-                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                if k % 8 == 0:
-                    power = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
-                k += 1
-                self.samples.append((mhz, reasons, power))
+                self._proc.kill()
+                self._proc.wait(timeout=10)
             except Exception:
                 pass
-            time.sleep(self.period)
+        self._proc = None
+
+    def _collect(self):
+        if self._proc is None:
+            return
+        try:
+            if self._t0 is not None and self._t1 is not None:
+                self._proc.stdin.write(f"{self._t0!r} {self._t1!r}\n")
+                self._proc.stdin.flush()
+                line = self._readline(30.0)
+                if line:
+                    self.samples = [(int(m), int(r), float(p)) for _, m, r, p in json.loads(line)]
+            self._proc.stdin.close()
+            self._proc.wait(timeout=10)
+        except Exception:
+            pass
+        self._close()
 
     def __enter__(self):
-        if self.handle is not None:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
+        self._t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._thread is not None:
-            self._thread.join()
+        self._t1 = time.monotonic()
+
+    def __del__(self):
+        self._close()
 
     def summary(self) -> dict:
+        self._collect()
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
         mhz = [s[0] for s in self.samples]

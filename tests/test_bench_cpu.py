@@ -52,3 +52,48 @@ def test_cpu_baselines_report_their_sample():
         assert cb["value"] > 0 and cb["cores"] >= 1 and per_step > 0 and cb["sample"]
     cb, _ = bench.cpu_tv_sq_128(reps=1, warmup=0)
     assert cb["unit"] == "voxels/s" and "[128, 128, 128]" in cb["sample"]
+
+
+_FAKE_NVML = '''
+import time
+NVML_CLOCK_SM = 1
+_t0 = time.monotonic()
+def nvmlInit(): pass
+def nvmlDeviceGetHandleByIndex(i): return ("h", i)
+def nvmlDeviceGetHandleByUUID(u): raise RuntimeError("no uuid on this host")
+def nvmlDeviceGetMaxClockInfo(h, kind): return 1965
+def nvmlDeviceGetClockInfo(h, kind): return 1905
+def nvmlDeviceGetCurrentClocksEventReasons(h): return 0x4
+def nvmlDeviceGetPowerUsage(h): return 700000
+'''
+
+
+def test_clock_sampler_polls_from_its_own_process(tmp_path, monkeypatch):
+    """The NVML poller runs as a separate process (a thread would wait for
+    the GIL held by the loop issuing the timed steps); only the samples taken
+    between __enter__ and __exit__ are reported. A fake NVML module stands in
+    for the driver, in this process and in the poller."""
+    import importlib.util
+
+    (tmp_path / "pynvml.py").write_text(_FAKE_NVML)
+    spec = importlib.util.spec_from_file_location("pynvml", tmp_path / "pynvml.py")
+    fake = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(fake)
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    monkeypatch.setenv("PYTHONPATH", str(tmp_path))
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES", raising=False)
+    import time
+
+    sampler = bench.ClockSampler(0)
+    assert sampler._proc is not None and sampler.max_mhz == 1965
+    time.sleep(0.05)  # samples before the region are not reported
+    with sampler:
+        t_end = time.monotonic() + 0.03
+        while time.monotonic() < t_end:  # a busy loop holding the GIL
+            pass
+    summary = sampler.summary()
+    assert summary["samples"] >= 5, summary
+    assert summary["sm_mhz"] == 1905 and summary["sm_max_mhz"] == 1965
+    assert summary["reasons"] == ["sw_power_cap"] and summary["power_w_max"] == 700.0
+    assert sampler._proc is None  # the poller has exited
+    assert bench.ClockSampler(0).summary()["samples"] == 0  # never entered: nothing reported
