@@ -329,7 +329,9 @@ size_t peer_allreduce_comm_bytes(void);
 int peer_allreduce_sum_f32_cuda(const qc_peer_group *group, unsigned long long seq, long long n,
                                 cudaStream_t stream);
 /* The same sum over floats [offset, offset + n) of every buffer only (any
- * offset), in one launch of at most max_ctas CTAs (0: two per SM). A small
+ * offset; the caller keeps offset + n within every rank's buffer, whose size
+ * the group does not record), in one launch of at most max_ctas CTAs (0: two
+ * per SM). A small
  * max_ctas lets the sum of one range run beside other work on the GPU, e.g.
  * the backward of the rotations whose gradients fill the next range. Calls
  * share `seq` numbering with peer_allreduce_sum_f32_cuda. */
