@@ -208,7 +208,7 @@ def kplanes_fwd_bwd_sharded(
     group=None,
     async_op: bool = False,
     fwd_bwd: Callable | None = None,
-    buckets: int = 1,
+    buckets: int | None = None,
     reducer: "PeerAllReduce | None" = None,
     reduce_ctas: int = 32,
 ):
@@ -229,7 +229,7 @@ def kplanes_fwd_bwd_sharded(
     B200s at N = 2^20, T = 4, C = 32, 256^2 the overlap costs more than it
     hides (the collective's SMs and L2 traffic slow the L2-bound backward:
     2.61 ms per step with 4 buckets against 2.16 ms with one), so the default
-    is a single backward launch followed by the all_reduce.
+    there is a single backward launch followed by the all_reduce.
 
     ``reducer`` (a :func:`kplanes_gradient_reducer` built once per level)
     replaces the NCCL all_reduce: the backward accumulates straight into the
@@ -238,9 +238,13 @@ def kplanes_fwd_bwd_sharded(
     With ``buckets`` > 1 the backward runs bucket by bucket over consecutive
     rotations and each bucket's plane gradients are summed on a second stream
     by a kernel of at most ``reduce_ctas`` CTAs while the next bucket's
-    backward computes (the rotation gradients go with the last bucket).
+    backward computes (the rotation gradients go with the last bucket); the
+    default there is 4 buckets (at most T), which on eight B200s left 0.21 ms
+    of the sum exposed per step against 0.30 ms with one launch.
     """
     _, world = _rank_world(group)
+    if buckets is None:
+        buckets = 4 if reducer is not None else 1
     if fwd_bwd is None:
         from quantem.cuda.core.ml._ops import _check_kernel_inputs
 

@@ -219,7 +219,8 @@ def _kp_worker(rank, world, port, queue):
         # the same step with the gradients summed over peer memory, twice
         reducer = sharded.kplanes_gradient_reducer(g, r)
         for _ in range(2):
-            _, pg_pts, pg_rot, pg_plane, pwork = sharded.kplanes_fwd_bwd_sharded(p, r, g, u, reducer=reducer)
+            _, pg_pts, pg_rot, pg_plane, pwork = sharded.kplanes_fwd_bwd_sharded(p, r, g, u, reducer=reducer,
+                                                                                buckets=1)
         assert pwork is None
         # and with the backward in three rotation buckets, each bucket's sum
         # on the reducer's second stream beside the next bucket's backward
