@@ -136,3 +136,22 @@ def test_raw_kplanes_ops_check_what_the_kernels_index():
     # host tensors never reach a kernel
     with pytest.raises(ValueError, match="CUDA"):
         torch.ops.quantem_cuda.kplanes_tilted_tv_fuse(p, r, torch.rand(6, 4, 6, 6), 0.1)
+
+
+def test_product_code_never_reaches_the_oracle():
+    """The package and its C sources name no oracle, torch restatement, CPU
+    fallback or subprocess: the only compute path is the CUDA extension, and
+    an op given CPU tensors raises instead of computing."""
+    import re
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    pattern = re.compile(r"^\s*(from|import)\s+(oracle|torch_ref|subprocess|ctypes|numpy)\b", re.M)
+    files = [*(root / "quantem-cuda_b200" / "quantem").rglob("*.py")]
+    assert files
+    for f in files:
+        text = f.read_text()
+        assert not pattern.search(text), f"{f} imports a CPU path"
+    inc = re.compile(r'^\s*#\s*include\s*[<"][^>"]*oracle', re.M)
+    for f in (root / "quantem-cuda_b200" / "csrc").glob("*.c*"):
+        assert not inc.search(f.read_text()), f"{f} includes oracle code"
